@@ -1,0 +1,96 @@
+"""ctypes binding of ``libcv3cuda.so`` (the C ABI declared in ``include/cv3cuda.h``).
+
+The library is loaded from the package directory.  There is no fallback: if it
+is missing, or no CUDA device is present, every operation raises.  Each call
+checks the returned status and raises the exception type the reference raises
+for the same condition (ValueError / IndexError), RuntimeError otherwise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libcv3cuda.so")
+
+CV3_OK, CV3_ERR_VALUE, CV3_ERR_INDEX, CV3_ERR_CUDA, CV3_ERR_UNSUPPORTED = 0, 1, 2, 3, 4
+
+P = ctypes.c_void_p
+I64 = ctypes.c_int64
+I32 = ctypes.c_int
+F = ctypes.c_float
+D = ctypes.c_double
+U64 = ctypes.c_uint64
+
+# name -> argument types (restype is always int status unless listed in _RESTYPE)
+SIGNATURES = {
+    "cv3_abi_version": [],
+    "cv3_device_info": [P, P, P],
+    "cv3_q8_linear": [P, I64, I64, I64, P, P, I64, I64, P, P, P, I64, P],
+    "cv3_f32_linear": [P, I64, I64, I64, P, I64, I64, P, P, P, I64, P],
+    "cv3_q8_dequant": [P, P, I64, I64, I64, P, P],
+    "cv3_unary": [I32, F, P, I64, P, P],
+    "cv3_rms_norm": [P, P, I64, I64, F, P, P],
+    "cv3_layer_norm": [P, P, P, I64, I64, F, P, P],
+    "cv3_softmax": [P, I64, I64, I32, P, P],
+    "cv3_snake": [P, P, I64, I64, P, P],
+    "cv3_embedding": [P, I32, P, I64, I64, I64, P, I64, P, I64, P, P],
+    "cv3_conv1d": [P, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, I64, P, P, I64, P],
+    "cv3_attention": [P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64,
+                      I64, I64, I64, I64, I64, I64, F, I32, I64, I64, P],
+    "cv3_stft": [P, I64, I64, I64, I64, P, P, I64, P],
+    "cv3_istft": [P, I32, I64, I64, I64, I64, P, F, I64, P, P, I64, P],
+    "cv3_interpolate_nearest": [P, I64, I64, I64, P, P],
+    "cv3_interpolate_linear": [P, I64, I64, P, P, P, I64, P, P],
+    "cv3_torch_rand": [U64, I64, I64, P, P],
+    "cv3_torch_randn": [U64, I64, I64, P, P, P],
+}
+_RESTYPE = {"cv3_last_error": ctypes.c_char_p}
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def exported_names():
+    return ["cv3_last_error"] + list(SIGNATURES)
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the library (once) and attach signatures; raises if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(
+            f"libcv3cuda.so not found at {path}; build it with "
+            f"`python cosyvoice3-cpu_b200/build.py` (there is no CPU fallback)")
+    lib = ctypes.CDLL(path)
+    lib.cv3_last_error.restype = ctypes.c_char_p
+    lib.cv3_last_error.argtypes = []
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPE.get(name, ctypes.c_int)
+    _lib = lib
+    return lib
+
+
+class CudaOpError(RuntimeError):
+    pass
+
+
+def check(status: int, name: str) -> None:
+    if status == CV3_OK:
+        return
+    msg = (_lib.cv3_last_error() or b"").decode("utf-8", "replace")
+    if status == CV3_ERR_VALUE:
+        raise ValueError(msg)
+    if status == CV3_ERR_INDEX:
+        raise IndexError(msg)
+    raise CudaOpError(f"{name}: {msg}")
+
+
+def call(name: str, *args) -> None:
+    lib = load()
+    check(getattr(lib, name)(*args), name)

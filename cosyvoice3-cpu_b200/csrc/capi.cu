@@ -1,0 +1,72 @@
+// Library-level entry points and the error convention shared by every kernel file.
+#include <string>
+#include <mutex>
+#include <map>
+#include <utility>
+
+#include "common.cuh"
+
+namespace cv3 {
+
+static thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error.assign(buf);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CV3_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return CV3_OK;
+}
+
+int sm_count() {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  cache[dev] = n;
+  return n;
+}
+
+int allow_smem(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> done;
+  int dev = 0;
+  CV3_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_pair(dev, fn);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return CV3_OK;
+  CV3_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done[key] = bytes;
+  return CV3_OK;
+}
+
+}  // namespace cv3
+
+extern "C" const char* cv3_last_error(void) { return cv3::g_last_error.c_str(); }
+
+extern "C" int cv3_abi_version(void) { return CV3_ABI_VERSION; }
+
+extern "C" int cv3_device_info(int* sm, int* major, int* minor) {
+  int dev = 0;
+  CV3_CUDA(cudaGetDevice(&dev));
+  cudaDeviceProp p;
+  CV3_CUDA(cudaGetDeviceProperties(&p, dev));
+  if (sm) *sm = p.multiProcessorCount;
+  if (major) *major = p.major;
+  if (minor) *minor = p.minor;
+  return CV3_OK;
+}

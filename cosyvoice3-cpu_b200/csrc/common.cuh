@@ -1,0 +1,107 @@
+// Shared helpers for the cv3cuda kernels: status codes, the thread-local error
+// message, launch checking and small device utilities.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "../../include/cv3cuda.h"
+
+namespace cv3 {
+
+// Records a message for cv3_last_error() and returns `code`.
+int fail(int code, const char* fmt, ...);
+
+// Checks the launch that just happened on this thread.
+int check_launch(const char* what);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Number of SMs on the current device (cached per device).
+int sm_count();
+
+// Sets the dynamic shared memory limit of a kernel once per (kernel, size).
+int allow_smem(const void* fn, int bytes);
+
+}  // namespace cv3
+
+#define CV3_REQUIRE(cond, code, ...)                  \
+  do {                                                \
+    if (!(cond)) return ::cv3::fail((code), __VA_ARGS__); \
+  } while (0)
+
+#define CV3_CUDA(call)                                                          \
+  do {                                                                          \
+    cudaError_t e_ = (call);                                                    \
+    if (e_ != cudaSuccess)                                                      \
+      return ::cv3::fail(CV3_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// device utilities
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum for blockDim.x a multiple of 32 (<= 1024).  `red` needs 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  v = (threadIdx.x < nw) ? red[threadIdx.x] : 0.f;
+  if (wid == 0) v = warp_sum(v);
+  if (threadIdx.x == 0) red[0] = v;
+  __syncthreads();
+  v = red[0];
+  return v;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  v = (threadIdx.x < nw) ? red[threadIdx.x] : -INFINITY;
+  if (wid == 0) v = warp_max(v);
+  if (threadIdx.x == 0) red[0] = v;
+  __syncthreads();
+  v = red[0];
+  return v;
+}
+
+// 16-byte streaming load that bypasses L1 (weights are read exactly once).
+__device__ __forceinline__ int4 ld_stream16(const void* p) {
+  int4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float h2f(uint16_t bits) {
+  return __half2float(__ushort_as_half(bits));
+}

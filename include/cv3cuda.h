@@ -1,0 +1,206 @@
+/*
+ * cv3cuda -- the C ABI of the B200 (sm_100a) kernel layer for CosyVoice 3.
+ *
+ * Each entry point replaces one operation of the reference's NumPy kernel
+ * layer (cv3cpu/ops.py, cv3cpu/quant.py, cv3cpu/torch_rng.py) or one fused
+ * group of them used by a model stage (cv3cpu/models/*.py).  The comment on
+ * every declaration names the reference function (path:line) it replaces.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  Unless a parameter says "host", every
+ *     pointer is a CUDA device pointer on the current device.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *     Calls are asynchronous and stream-ordered; none allocates device memory
+ *     unless its comment says so, and none synchronises the stream.
+ *   - Every call returns a status: CV3_OK (0) or one of the CV3_ERR_* codes.
+ *     cv3_last_error() returns a message for the last failure on the calling
+ *     host thread.  The Python host maps CV3_ERR_VALUE to ValueError,
+ *     CV3_ERR_INDEX to IndexError and the rest to RuntimeError, the
+ *     exception types the reference raises for the same conditions.
+ *   - float tensors are row-major, contiguous unless a leading dimension
+ *     (ld*) is given.  q8 weights use the "balanced" layout: int8 q[N][Kp],
+ *     Kp = K rounded up to 64, and float16 scales s[N][Kp/64] (passed as
+ *     uint16_t bit patterns); W[n][k] = float(q[n][k]) * float(s[n][k/64]).
+ */
+#ifndef CV3CUDA_H
+#define CV3CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CV3_OK 0
+#define CV3_ERR_VALUE 1       /* bad shape / argument  -> ValueError   */
+#define CV3_ERR_INDEX 2       /* id outside a table    -> IndexError   */
+#define CV3_ERR_CUDA 3        /* CUDA runtime failure  -> RuntimeError */
+#define CV3_ERR_UNSUPPORTED 4 /* configuration not built -> RuntimeError */
+
+#define CV3_ABI_VERSION 1
+
+/* ------------------------------------------------------------------ */
+/* library                                                             */
+/* ------------------------------------------------------------------ */
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* cv3_last_error(void);
+
+/* CV3_ABI_VERSION of the loaded library. */
+int cv3_abi_version(void);
+
+/* SM count and compute capability of the current device. */
+int cv3_device_info(int* sm_count, int* cc_major, int* cc_minor);
+
+/* ------------------------------------------------------------------ */
+/* linear layers                                                        */
+/* ------------------------------------------------------------------ */
+
+/* y[m][n] = sum_k x[m][k] * W[n][k] + bias[n] (+ residual[m][n]) for a q8 W.
+ * Replaces cv3cpu/quant.py:156-204 (qmatmul with a QTensor, reached through
+ * cv3cpu/ops.py:121 linear).  x: [m][k] fp32 with row stride ldx; bias and
+ * residual may be NULL; y: [m][n] with row stride ldy (y may alias residual).
+ * Any m >= 1; the weight stream is read once for up to 8 rows per pass. */
+int cv3_q8_linear(const float* x, int64_t m, int64_t k, int64_t ldx,
+                  const int8_t* q, const uint16_t* scales, int64_t n, int64_t kp,
+                  const float* bias, const float* residual,
+                  float* y, int64_t ldy, void* stream);
+
+/* Same contract for an fp32 weight W[n][k] (row stride ldw); replaces the
+ * plain-array branch of cv3cpu/quant.py:165-170. fp32-exact SIMT math. */
+int cv3_f32_linear(const float* x, int64_t m, int64_t k, int64_t ldx,
+                   const float* w, int64_t n, int64_t ldw,
+                   const float* bias, const float* residual,
+                   float* y, int64_t ldy, void* stream);
+
+/* Dequantise q8 rows [0, n) into fp32 out[n][k] (k <= kp, padding dropped).
+ * Replaces cv3cpu/quant.py:110-133 (QTensor.dequant_rows). */
+int cv3_q8_dequant(const int8_t* q, const uint16_t* scales, int64_t n, int64_t kp,
+                   int64_t k, float* out, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* elementwise and normalisation                                        */
+/* ------------------------------------------------------------------ */
+
+#define CV3_ACT_SILU 0       /* cv3cpu/ops.py:30  */
+#define CV3_ACT_SIGMOID 1    /* cv3cpu/ops.py:34  */
+#define CV3_ACT_GELU_TANH 2  /* cv3cpu/ops.py:41  */
+#define CV3_ACT_GELU_ERF 3   /* cv3cpu/ops.py:46  (A&S 7.1.26 erf) */
+#define CV3_ACT_MISH 4       /* cv3cpu/ops.py:63  */
+#define CV3_ACT_ELU 5        /* cv3cpu/ops.py:69  (param = alpha) */
+#define CV3_ACT_LEAKY_RELU 6 /* cv3cpu/ops.py:73  (param = slope) */
+#define CV3_ACT_TANH 7       /* np.tanh, cv3cpu/models/hift.py:111 */
+#define CV3_ACT_EXP 8        /* np.exp */
+
+/* y[i] = act(x[i]) for i < n (y may alias x). */
+int cv3_unary(int act, float param, const float* x, int64_t n, float* y, void* stream);
+
+/* y = rms_norm(x, w, eps) over rows of length dim; cv3cpu/ops.py:101-104. */
+int cv3_rms_norm(const float* x, const float* w, int64_t rows, int64_t dim, float eps,
+                 float* y, void* stream);
+
+/* y = layer_norm(x, w, b, eps) over rows; w, b may be NULL; cv3cpu/ops.py:107-118. */
+int cv3_layer_norm(const float* x, const float* w, const float* b, int64_t rows,
+                   int64_t dim, float eps, float* y, void* stream);
+
+/* Row-wise softmax (log=0) or log_softmax (log=1); cv3cpu/ops.py:84-93. */
+int cv3_softmax(const float* x, int64_t rows, int64_t dim, int log, float* y, void* stream);
+
+/* Snake over (C, T): y = x + sin(a x)^2 / (a + 1e-9), a per channel;
+ * cv3cpu/ops.py:77-81. */
+int cv3_snake(const float* x, const float* alpha, int64_t channels, int64_t t,
+              float* y, void* stream);
+
+
+/* ------------------------------------------------------------------ */
+/* gathers, convolution, attention                                      */
+/* ------------------------------------------------------------------ */
+
+#define CV3_TABLE_F32 0
+#define CV3_TABLE_F16 1
+#define CV3_TABLE_Q8 2
+
+/* out[i][:] = table[ids[i]][:] widened to fp32 (q8: dequantised row).
+ * Replaces cv3cpu/ops.py:126-144 (embedding).  ids: device int64[n];
+ * table: f32/f16 [rows][dim] or q8 [rows][kp] with scales.  Rows outside
+ * the table produce zeros and increment *bad (device int, may be NULL);
+ * the host raises IndexError before launching for host-side ids. */
+int cv3_embedding(const void* table, int kind, const uint16_t* scales, int64_t rows, int64_t dim,
+                  int64_t kp, const int64_t* ids, int64_t n, float* out, int64_t ldo, int* bad,
+                  void* stream);
+
+/* Batched 1-D cross-correlation: x [batch][cin][t_in] -> y [batch][cout][t_out]
+ * with weight [cout][cin/groups][k], optional bias, zero padding
+ * (pad_left, pad_right), stride, dilation, groups.  t_out must equal
+ * (t_in + pad_left + pad_right - dilation*(k-1) - 1)/stride + 1.
+ * Replaces cv3cpu/ops.py:165-219 (conv1d) and :222-236 (depthwise_conv1d). */
+int cv3_conv1d(const float* x, int64_t batch, int64_t cin, int64_t t_in, const float* w, int64_t cout,
+               int64_t k, int64_t stride, int64_t dilation, int64_t groups, int64_t pad_left,
+               int64_t pad_right, const float* bias, float* y, int64_t t_out, void* stream);
+
+#define CV3_MASK_NONE 0
+#define CV3_MASK_CAUSAL 1 /* key j visible to query i iff j <= i + a          */
+#define CV3_MASK_CHUNK 2  /* chunk size a, b chunks of left context (-1: all) */
+
+/* Exact-softmax attention.  Element (b, h, i, d) of q/k/v/o lives at
+ * base + b*s_b + h*s_h + i*s_n + d (strides in floats), so (H, N, D) and
+ * token-major (B, N, H*D) layouts are both read in place.  GQA: query head h
+ * uses kv head h / (heads / kv_heads).  Replaces cv3cpu/ops.py:267-310 (sdpa
+ * with _block_mask :244-264); head_dim <= 64. */
+int cv3_attention(const float* q, int64_t qsb, int64_t qsh, int64_t qsn,
+                  const float* k, int64_t ksb, int64_t ksh, int64_t ksn,
+                  const float* v, int64_t vsb, int64_t vsh, int64_t vsn,
+                  float* o, int64_t osb, int64_t osh, int64_t osn,
+                  int64_t batch, int64_t heads, int64_t kv_heads, int64_t n, int64_t m, int64_t d,
+                  float scale, int mask_kind, int64_t mask_a, int64_t mask_b, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* spectral and resampling                                               */
+/* ------------------------------------------------------------------ */
+
+/* One-sided STFT of batch signals x [batch][len], reflect-padded by n_fft/2,
+ * window win[n_fft]; out [batch][2F][frames], F = n_fft/2+1, rows [0,F) real
+ * and [F,2F) imaginary parts.  frames = 1 + len/hop (centre padding).
+ * Replaces cv3cpu/ops.py:346-355 (stft) as the vocoder consumes it
+ * (cv3cpu/models/hift.py:198-199). */
+int cv3_stft(const float* x, int64_t batch, int64_t len, int64_t n_fft, int64_t hop, const float* win,
+             float* out, int64_t frames, void* stream);
+
+#define CV3_ISTFT_REIM 0 /* spec rows: [0,F) real, [F,2F) imaginary                 */
+#define CV3_ISTFT_HIFT 1 /* spec rows: log-magnitude, phase angle (hift.py:204-208) */
+
+/* Inverse STFT with window-square normalisation and clip to +-limit.
+ * y[b][t] = overlap-add sample (t + offset), t < out_len; offset = n_fft/2
+ * gives the centred signal.  frame_scratch: device float [batch][frames][n_fft].
+ * Replaces cv3cpu/ops.py:358-377 (istft) and cv3cpu/models/hift.py:204-210. */
+int cv3_istft(const float* spec, int mode, int64_t batch, int64_t frames, int64_t n_fft, int64_t hop,
+              const float* win, float limit, int64_t offset, float* frame_scratch, float* y,
+              int64_t out_len, void* stream);
+
+/* y [rows][t*scale] = x repeated along time; cv3cpu/ops.py:335-336. */
+int cv3_interpolate_nearest(const float* x, int64_t rows, int64_t t, int64_t scale, float* y, void* stream);
+
+/* y [rows][size] = x[:, i0] * (1 - w) + x[:, i1] * w with host-built index/weight
+ * tables (device int64 i0, i1, float w); cv3cpu/ops.py:318-332. */
+int cv3_interpolate_linear(const float* x, int64_t rows, int64_t t, const int64_t* i0, const int64_t* i1,
+                           const float* w, int64_t size, float* y, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* torch CPU generator replica                                          */
+/* ------------------------------------------------------------------ */
+
+/* out[i] = float32 uniform number (skip + i) of torch.manual_seed(seed)'s
+ * stream (MT19937, low 24 bits); torch_rng.py:88-91 and :145-150. */
+int cv3_torch_rand(uint64_t seed, int64_t skip, int64_t n, float* out, void* stream);
+
+/* out[0..n) = torch.randn(n) drawn from torch.manual_seed(seed)'s generator
+ * after `skip` 32-bit words were consumed (skip = 0: a fresh seed), bit-exact
+ * with cv3cpu/torch_rng.py:117-142.  Consumes n (+16 when n % 16 != 0) words,
+ * or 4*ceil(n/2) words when n < 16.  scratch: 128 device bytes. */
+int cv3_torch_randn(uint64_t seed, int64_t skip, int64_t n, float* out, void* scratch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CV3CUDA_H */

@@ -1,0 +1,168 @@
+"""Pin the CPU oracle: against the reference's frozen goldens and the reference itself.
+
+* torch RNG goldens (copied from the reference's ``tests/reference_values.json``)
+  for every seed/shape the reference's own suite checks;
+* stage goldens produced by running the reference on the small synthetic model
+  (``tests/golden/make_golden.py``);
+* when the reference checkout is present: op-by-op agreement with
+  ``cv3cpu.ops``/``cv3cpu.quant``, and the frozen upstream outputs of
+  ``tests/fixtures/reference_io.npz`` through the converted tiny checkpoint.
+"""
+
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import REFERENCE, have_reference, rel_err
+
+import oracle.numerics as nx
+import oracle.stages as st
+
+
+def _check_golden(g, arr):
+    flat = np.asarray(arr, dtype=np.float64).reshape(-1)
+    assert list(np.shape(arr)) == g["shape"]
+    got = np.array([flat[i] for i in g["idx"]])
+    assert np.abs(got - np.array(g["vals"])).max() < 1e-5
+    assert abs(flat.sum() - g["sum"]) < 1e-2 * max(1.0, abs(g["sum"]))
+
+
+@pytest.mark.parametrize("seed", [0, 1, 42, 1986])
+@pytest.mark.parametrize("shape", [(5,), (17,), (1000,), (1, 80, 15000)])
+def test_oracle_randn_matches_torch_goldens(rng_golden, seed, shape):
+    _check_golden(rng_golden[f"randn_{seed}_{'x'.join(map(str, shape))}"], nx.randn(shape, seed))
+
+
+@pytest.mark.parametrize("seed", [0, 1, 42, 1986])
+def test_oracle_rand_matches_torch_goldens(rng_golden, seed):
+    _check_golden(rng_golden[f"rand_{seed}_1000"], nx.rand((1000,), seed))
+
+
+def test_oracle_shared_generator_advances(rng_golden):
+    g = nx.MT19937(0)
+    first = nx.randn((1000,), gen=g)
+    _check_golden(rng_golden["randn_0_1000"], first)
+    assert not np.array_equal(first, nx.randn((1000,), gen=g))
+
+
+# ---------------------------------------------------------------------------
+# stage goldens from the reference run on the small synthetic model
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("profile", ["balanced", "f32"])
+def test_oracle_lm_matches_reference_goldens(golden, small_weights, profile):
+    W = small_weights[profile]
+    lm = st.SpeechLM(W, W.meta)
+    x0 = lm.prompt_embedding(golden[f"{profile}/lm_text"], (), golden[f"{profile}/lm_prompt_speech"])
+    toks, logps = lm.generate_greedy(x0, 8)
+    assert toks == golden[f"{profile}/lm_tokens"].tolist()
+    assert rel_err(logps, golden[f"{profile}/lm_logp"]) < 1e-5
+
+
+@pytest.mark.parametrize("profile", ["balanced", "f32"])
+def test_oracle_flow_matches_reference_goldens(golden, small_weights, profile):
+    W = small_weights[profile]
+    g = lambda k: golden[f"{profile}/flow_{k}"]  # noqa: E731
+    mel = st.Flow(W, W.meta).inference(g("token"), g("prompt_token"), g("prompt_feat"), g("embedding"))
+    assert mel.shape == g("mel").shape
+    assert rel_err(mel, g("mel")) < 1e-5
+
+
+@pytest.mark.parametrize("profile", ["balanced", "f32"])
+def test_oracle_hift_matches_reference_goldens(golden, small_weights, profile):
+    W = small_weights[profile]
+    h = st.HiFT(W, W.meta)
+    mel = golden[f"{profile}/hift_mel"]
+    assert rel_err(h.inference(mel, chunk=None), golden[f"{profile}/hift_wav"]) < 1e-5
+    assert rel_err(h.inference(mel, chunk=4, context=64), golden[f"{profile}/hift_wav_chunked"]) < 1e-5
+
+
+# ---------------------------------------------------------------------------
+# live reference (this container only)
+# ---------------------------------------------------------------------------
+
+needs_ref = pytest.mark.skipif(not have_reference(), reason="reference checkout not present")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    sys.path.insert(0, REFERENCE)
+    import cv3cpu.ops as rops
+    import cv3cpu.quant as rquant
+    import cv3cpu.torch_rng as rrng
+    return rops, rquant, rrng
+
+
+@needs_ref
+def test_oracle_ops_equal_reference_ops(ref):
+    rops, rquant, _ = ref
+    rng = np.random.default_rng(0)
+    x = (rng.normal(size=(7, 33)) * 3).astype(np.float32)
+    for name in ("silu", "sigmoid", "gelu_tanh", "gelu", "mish", "elu", "softmax", "log_softmax"):
+        assert np.array_equal(getattr(nx, name)(x), getattr(rops, name)(x)), name
+    assert np.array_equal(nx.leaky_relu(x, 0.1), rops.leaky_relu(x, 0.1))
+    a = np.abs(rng.normal(size=7)).astype(np.float32) + 0.5
+    assert np.array_equal(nx.snake(x, a), rops.snake(x, a))
+    w = rng.normal(size=33).astype(np.float32)
+    assert np.array_equal(nx.rms_norm(x, w), rops.rms_norm(x, w))
+    assert np.array_equal(nx.layer_norm(x, None, None, 1e-6), rops.layer_norm(x, None, None, 1e-6))
+    wq = rng.normal(size=(40, 100)).astype(np.float32)
+    qa, sa, _ = nx.quantize_q8(wq)
+    qb, sb, _ = rquant.quantize_q8(wq)
+    assert np.array_equal(qa, qb) and np.array_equal(sa, sb)
+    qt = rquant.QTensor("q8", qb, sb, (40, 100), 64)
+    xx = rng.normal(size=(3, 100)).astype(np.float32)
+    assert rel_err(nx.qmatmul(xx, qt), rquant.qmatmul(xx, qt)) < 1e-6
+    xc = rng.normal(size=(18, 61)).astype(np.float32)
+    wc = (rng.normal(size=(8, 18, 30)) * 0.1).astype(np.float32)
+    assert rel_err(nx.conv1d(xc, wc, None, stride=15, pad=(14, 0)),
+                   rops.conv1d(xc, wc, None, stride=15, pad=(14, 0))) < 1e-6
+    qh, kh, vh = (rng.normal(size=(4, 23, 16)).astype(np.float32) for _ in range(3))
+    for spec in (None, ("causal",), ("causal", 3), ("chunk", 5, 1)):
+        assert rel_err(nx.sdpa(qh, kh, vh, spec), rops.sdpa(qh, kh, vh, spec)) < 1e-6
+    win = nx.hann_window(16)
+    sig = rng.normal(size=400).astype(np.float32)
+    assert np.array_equal(nx.stft(sig, 16, 4, win), rops.stft(sig, 16, 4, win))
+    spec = nx.stft(sig, 16, 4, win)
+    assert np.array_equal(nx.istft(spec, 16, 4, win), rops.istft(spec, 16, 4, win))
+
+
+@needs_ref
+def test_oracle_rng_equals_reference_rng_on_the_flow_buffer(ref):
+    _, _, rrng = ref
+    assert np.array_equal(nx.randn((1, 80, 15000), 0), rrng.randn((1, 80, 15000), 0))
+    assert np.array_equal(nx.MT19937(0).random_float32(4800 * 9), rrng.TorchMT19937(0).random_float32(4800 * 9))
+    for n in (1, 5, 17, 33):
+        assert np.array_equal(nx.randn((n,), 7), rrng.randn((n,), 7))
+
+
+@needs_ref
+def test_oracle_matches_frozen_upstream_outputs(tmp_path):
+    """The reference's own pin (tests/test_reference.py:99-155): the converted tiny
+    checkpoint through the oracle's stages against upstream PyTorch outputs."""
+    sys.path.insert(0, REFERENCE)
+    from cv3cpu.convert import convert
+    from conftest import pkg
+    path = str(tmp_path / "tiny.safetensors")
+    convert(os.path.join(REFERENCE, "tests", "fixtures", "checkpoint"), path, profile="f32", verbose=False)
+    W = pkg("weights").WeightFile(path)
+    io = dict(np.load(os.path.join(REFERENCE, "tests", "fixtures", "reference_io.npz")))
+    mel = st.Flow(W, W.meta).inference(io["token"], io["prompt_token"], io["prompt_feat"], io["embedding"])
+    assert rel_err(mel, io["flow_mel"]) < 5e-4
+    h = st.HiFT(W, W.meta)
+    n = 480 * io["mel"].shape[1]
+    h.set_source_noise(nx.MT19937(0).random_float32(n * 9).reshape(n, 9))
+    assert rel_err(h.inference(io["mel"], chunk=None), io["hift_wav"]) < 2e-3
+    lm = st.SpeechLM(W, W.meta)
+    x = np.concatenate([lm.speech_emb([lm.sos]), lm.text_emb(io["text"]), lm.speech_emb([lm.task_id]),
+                        lm.speech_emb(io["prompt_speech"])], axis=0)
+    cache = lm.body.new_cache()
+    forced = list(io["forced"])
+    for i, refl in enumerate(io["llm_logits"]):
+        got = lm.head(lm.body.forward(x, cache)[-1:])[0]
+        assert rel_err(got, refl) < 1e-3, i
+        if i < len(forced):
+            x = lm.speech_emb([int(forced[i])])
+    W.close()
