@@ -1,0 +1,356 @@
+"""Benchmark: end-to-end balanced CosyVoice 3 synthesis on B200 (config 4 of the baseline).
+
+One step = 8 independent 10 s utterances per GPU through the int8 LM (64..80-id
+random text + 75-token prompt, 250 greedy speech tokens), the 10-step CFG flow
+(N = 2 * (75 + 250) = 650 frames, CFG batch 16) and the vocoder (500 frames ->
+240,000 samples).  Synthetic random weights of the released geometry and seeded
+random inputs (no dataset or checkpoint is involved).  Weak scaling: each rank
+synthesises its own 8 utterances; ``value`` is all ranks' utterances divided by
+the slowest rank's device time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
+
+The reference arm (``--impl reference``) times the CPU oracle -- the NumPy
+restatement of the reference's kernel layer and stages -- on the host cores,
+one bounded per-utterance sample per step (see ``cpu_sample``).
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "10s-utterances/sec at 1/2/4/8 B200 (LM tok/s, flow+HiFT RTF); % HBM/TC roofline"
+UNIT = "utterances/s"
+UTTS = 8
+TOKENS = 250
+PROMPT_TOKENS = 75
+PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
+
+
+def pkg(name=""):
+    return importlib.import_module("cosyvoice3-cpu_b200" + ("." + name if name else ""))
+
+
+def make_requests(seeds, meta):
+    """Config-4 inputs per seed s: text ids U[40, 80] with <|endofprompt|> in the
+    prompt text, a 192-d N(0,1) speaker vector, a 150-frame N(0,1) prompt mel and
+    75 prompt speech tokens."""
+    voice_cls = pkg("voice").VoicePack
+    req_cls = pkg("pipeline").Request
+    eop = int(meta.get("endofprompt_id", 151646))
+    vocab = int(meta["qwen2"]["vocab_size"])
+    sts = int(meta.get("speech_token_size", 6561))
+    out = []
+    for s in seeds:
+        rng = np.random.default_rng(s)
+        n = int(rng.integers(40, 81))
+        text = rng.integers(0, vocab, size=n).tolist()
+        prompt_text = rng.integers(0, vocab, size=8).tolist() + [eop]
+        voice = voice_cls(speech_token=rng.integers(0, sts, size=PROMPT_TOKENS),
+                          mel=rng.normal(size=(2 * PROMPT_TOKENS, 80)).astype(np.float32),
+                          embedding=rng.normal(size=192).astype(np.float32), name=f"seed{s}")
+        out.append(req_cls(text, prompt_text, voice))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle sample (cpu_baseline and the reference arm)
+# ---------------------------------------------------------------------------
+
+def cpu_sample(W, req, decode_steps: int = 4):
+    """Seconds per utterance of the CPU oracle, from a bounded sample of one
+    config-4 utterance: LM prefill of its prompt plus ``decode_steps`` greedy
+    steps (per-step time extrapolated to 250), one DiT forward at the CFG batch
+    (2, 80, 650) (x10 Euler steps), and the full 500-frame vocoder."""
+    import oracle.stages as st
+    meta = W.meta
+    lm = st.SpeechLM(W, meta)
+    v = req.voice
+    x0 = lm.prompt_embedding(req.text_ids, req.prompt_ids, v.speech_token.tolist())
+    cache = lm.body.new_cache()
+    t0 = time.perf_counter()
+    h = lm.body.forward(x0, cache)
+    tok = lm.greedy(lm.head(h[-1:])[0])
+    t_prefill = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    for _ in range(decode_steps):
+        h = lm.body.forward(lm.speech_emb([tok]), cache)
+        tok = lm.greedy(lm.head(h[-1:])[0])
+    t_step = (time.perf_counter() - t0) / decode_steps
+    flow = st.Flow(W, meta)
+    n = 2 * (PROMPT_TOKENS + TOKENS)
+    rng = np.random.default_rng(0)
+    x = rng.normal(size=(2, 80, n)).astype(np.float32)
+    t0 = time.perf_counter()
+    flow.dit.forward(x, x * 0, np.array([0.5, 0.5], np.float32), np.zeros((2, 80), np.float32), x * 0)
+    t_dit = time.perf_counter() - t0
+    hift = st.HiFT(W, meta)
+    mel = np.clip(rng.normal(-5, 2, size=(80, 2 * TOKENS)), -11.5, 2).astype(np.float32)
+    t0 = time.perf_counter()
+    hift.inference(mel, chunk=250)
+    t_hift = time.perf_counter() - t0
+    per_utt = t_prefill + (TOKENS - 1) * t_step + flow.steps * t_dit + t_hift
+    sampled = t_prefill + decode_steps * t_step + t_dit + t_hift
+    return per_utt, sampled, {"lm_prefill_s": t_prefill, "lm_step_s": t_step, "dit_forward_s": t_dit,
+                              "hift_s": t_hift}
+
+
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else (os.cpu_count() or 1)
+    except Exception:
+        return os.cpu_count() or 1
+
+
+CPU_SAMPLE_DESC = ("one config-4 utterance: LM prefill + 4 greedy steps (x250/4 extrapolated), one DiT "
+                   "forward at CFG batch 2 x 650 frames (x10 steps), full 500-frame vocoder (chunk 250)")
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    synth = pkg("synth")
+    W = synth.synthetic_weights("balanced")
+    reqs = make_requests(range(UTTS), W.meta)
+    times = []
+    for i in range(args.warmup + args.steps):
+        per_utt, sampled, parts = cpu_sample(W, reqs[i % len(reqs)])
+        if i >= args.warmup:
+            times.append(per_utt)
+    per_utt = float(np.mean(times))
+    value = 1.0 / per_utt
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_utt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+                         "sample": CPU_SAMPLE_DESC},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def config_dict(args):
+    return {"workload": "config4 e2e balanced synthesis: 8 utterances per GPU, 250 greedy LM tokens each, "
+                        "10-step CFG flow at 650 frames, vocoder 500 frames -> 240000 samples",
+            "utterances_per_gpu": UTTS, "lm_tokens": TOKENS, "prompt_speech_tokens": PROMPT_TOKENS,
+            "flow_frames": 2 * (PROMPT_TOKENS + TOKENS), "cfg_batch": 2 * UTTS, "vocoder_frames": 2 * TOKENS,
+            "profile": "balanced (int8 LM/DiT, f16 vocoder)", "parallelism": f"dp{args.gpus} (independent utterances)",
+            "l2": "working set > L2: 1.2 GB of weights streamed every step"}
+
+
+# ---------------------------------------------------------------------------
+# the device arm
+# ---------------------------------------------------------------------------
+
+def dominant_kernel_roofline(tts, peaks):
+    """Time the DiT FF GEMM at the bench shape in isolation (the largest kernel of
+    the step) with CUDA events on its launching stream; achieved = 2*M*N*K / time."""
+    import torch
+    L = pkg("_lib")
+    dit = tts.flow.estimator
+    dit.prepare()
+    M = 2 * UTTS * 2 * (PROMPT_TOKENS + TOKENS)
+    blk = dit.blocks[0].ff1
+    x = torch.randn(M, blk.k, device="cuda")
+    y = torch.empty(M, blk.n, device="cuda")
+    st = torch.cuda.current_stream()
+    for _ in range(3):
+        blk(x.data_ptr(), M, y.data_ptr(), stream=st.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(reps):
+        blk(x.data_ptr(), M, y.data_ptr(), stream=st.cuda_stream)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = 2.0 * M * blk.n * blk.k
+    achieved = flops / (ms * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops")
+    return {"kernel": "DiT ff1 GEMM (M=%d, N=%d, K=%d, fp32)" % (M, blk.n, blk.k), "bound": "tensor",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
+            "peak_source": "measured bf16 dense (MEASURED_PEAKS.json, burst)", "traffic": None,
+            "avg_launch_ms": ms}
+
+
+def run_cuda(args, rank: int, world: int) -> None:
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    synth, pipeline, L = pkg("synth"), pkg("pipeline"), pkg("_lib")
+    W = synth.synthetic_weights("balanced")
+    tts = pipeline.CosyVoice3CUDA(W)
+    seeds = range(rank * UTTS, rank * UTTS + UTTS)
+    reqs = make_requests(seeds, W.meta)
+    prepared = tts.prepare(reqs)
+    for _ in range(max(args.warmup, 1)):
+        wav, _ = tts.run_prepared(prepared, TOKENS)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # -- value: inputs resident in HBM --------------------------------------------------
+    barrier()
+    torch.cuda.synchronize()
+    l0 = L.executed_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            wav, _ = tts.run_prepared(prepared, TOKENS)
+        e1.record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = L.executed_launches() - l0
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+
+    # -- e2e: host inputs in, host waveforms out, through the public API --------------------
+    barrier()
+    torch.cuda.synchronize()
+    h2d = sum(int(np.asarray(r.text_ids).size + np.asarray(r.prompt_ids).size) * 8 +
+              r.voice.speech_token.nbytes + r.voice.mel.nbytes + r.voice.embedding.nbytes for r in reqs)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        wav_h, _ = tts.synthesize_greedy_batch(reqs, TOKENS, to_host=True)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    t = torch.tensor([e2e_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    d2h = int(wav_h.nbytes)
+
+    peaks = json.load(open(PEAKS)) if os.path.exists(PEAKS) else {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+    roof = dominant_kernel_roofline(tts, peaks) if rank == 0 else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        per_utt, sampled, parts = cpu_sample(W, reqs[0])
+        cpu = {"value": 1.0 / per_utt, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+               "sample": CPU_SAMPLE_DESC, "sampled_cpu_s": sampled, "parts_s": parts}
+    if rank == 0:
+        total_utts = UTTS * world
+        print(json.dumps({
+            "metric": METRIC, "value": total_utts / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_dict(args),
+            "e2e": {"value": total_utts / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "stage_note": "LM tok/s = %.0f per GPU (all stages in one step)" % (UTTS * TOKENS / (ms * 1e-3)),
+        }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if world > 1 and args.impl == "cuda":
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_cuda(args, rank, world)
+    finally:
+        if world > 1 and args.impl == "cuda":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

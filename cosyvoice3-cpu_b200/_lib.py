@@ -27,6 +27,7 @@ U64 = ctypes.c_uint64
 # name -> argument types (restype is always int status unless listed in _RESTYPE)
 SIGNATURES = {
     "cv3_abi_version": [],
+    "cv3_launch_count": [],
     "cv3_device_info": [P, P, P],
     "cv3_q8_linear": [P, I64, I64, I64, P, P, I64, I64, P, P, P, I64, P],
     "cv3_f32_linear": [P, I64, I64, I64, P, I64, I64, P, P, P, I64, P],
@@ -35,7 +36,7 @@ SIGNATURES = {
     "cv3_rms_norm": [P, P, I64, I64, F, P, P],
     "cv3_layer_norm": [P, P, P, I64, I64, F, P, P],
     "cv3_softmax": [P, I64, I64, I32, P, P],
-    "cv3_snake": [P, P, I64, I64, P, P],
+    "cv3_snake": [P, P, I64, I64, I64, P, P],
     "cv3_embedding": [P, I32, P, I64, I64, I64, P, I64, P, I64, P, P],
     "cv3_conv1d": [P, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, I64, P, P, I64, P],
     "cv3_attention": [P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64,
@@ -46,14 +47,51 @@ SIGNATURES = {
     "cv3_interpolate_linear": [P, I64, I64, P, P, P, I64, P, P],
     "cv3_torch_rand": [U64, I64, I64, P, P],
     "cv3_torch_randn": [U64, I64, I64, P, P, P],
+    "cv3_rope_qkv_append": [P, I64, I64, P, P, P, P, I64, I64, I64, P, P, P, I64, P],
+    "cv3_decode_attention": [P, P, P, P, I64, I64, I64, I64, I64, F, P, P],
+    "cv3_swiglu": [P, I64, I64, P, P],
+    "cv3_head_select": [P, I64, I64, I64, P, P, P, P, P, I64, P, P],
+    "cv3_dit_input_cat": [P, P, P, P, I64, I64, I64, I64, P, P],
+    "cv3_ln_modulate": [P, I64, I64, F, P, P, I64, I64, P, P],
+    "cv3_gate_residual": [P, P, P, I64, I64, I64, I64, P],
+    "cv3_partial_rope": [P, I64, I64, I64, I64, I64, P, P, P],
+    "cv3_transpose": [P, I64, I64, I64, P, I32, P],
+    "cv3_cfg_euler": [P, P, I64, I64, I64, D, F, P],
+    "cv3_l2_normalize": [P, I64, I64, P, P],
+    "cv3_f0_classifier": [P, I64, I64, I64, P, P, P, P],
+    "cv3_nsf_source": [P, I64, I64, I64, I64, I64, D, D, D, P, P, P, P, P, P],
+    "cv3_binary": [I32, P, P, F, I64, P, P],
+    "cv3_reflect_left1": [P, I64, I64, P, P],
 }
-_RESTYPE = {"cv3_last_error": ctypes.c_char_p}
+_RESTYPE = {"cv3_last_error": ctypes.c_char_p, "cv3_launch_count": ctypes.c_ulonglong}
 
 _lib: Optional[ctypes.CDLL] = None
 
 
 def exported_names():
     return ["cv3_last_error"] + list(SIGNATURES)
+
+
+def launch_count() -> int:
+    """Kernels launched or graph-recorded by the library so far (``cv3_launch_count``)."""
+    return int(load().cv3_launch_count())
+
+
+_graph_books = {"captured": 0, "replayed": 0}
+
+
+def note_capture(nodes: int) -> None:
+    _graph_books["captured"] += nodes
+
+
+def note_replay(nodes: int) -> None:
+    _graph_books["replayed"] += nodes
+
+
+def executed_launches() -> int:
+    """Kernels of this library executed so far: direct launches plus the kernel
+    nodes of every CUDA-graph replay (recording during capture is not execution)."""
+    return launch_count() - _graph_books["captured"] + _graph_books["replayed"]
 
 
 def load(path: str = LIB_PATH) -> ctypes.CDLL:

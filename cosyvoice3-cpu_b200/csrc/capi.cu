@@ -1,4 +1,5 @@
 // Library-level entry points and the error convention shared by every kernel file.
+#include <atomic>
 #include <string>
 #include <mutex>
 #include <map>
@@ -9,6 +10,7 @@
 namespace cv3 {
 
 static thread_local std::string g_last_error;
+static std::atomic<unsigned long long> g_launches{0};
 
 int fail(int code, const char* fmt, ...) {
   char buf[1024];
@@ -21,6 +23,7 @@ int fail(int code, const char* fmt, ...) {
 }
 
 int check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CV3_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
   return CV3_OK;
@@ -59,6 +62,8 @@ int allow_smem(const void* fn, int bytes) {
 extern "C" const char* cv3_last_error(void) { return cv3::g_last_error.c_str(); }
 
 extern "C" int cv3_abi_version(void) { return CV3_ABI_VERSION; }
+
+extern "C" unsigned long long cv3_launch_count(void) { return cv3::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int cv3_device_info(int* sm, int* major, int* minor) {
   int dev = 0;

@@ -94,11 +94,11 @@ __global__ void softmax_kernel(const float* __restrict__ x, int dim, int lg, flo
   }
 }
 
-__global__ void snake_kernel(const float* __restrict__ x, const float* __restrict__ alpha, int64_t t,
+__global__ void snake_kernel(const float* __restrict__ x, const float* __restrict__ alpha, int64_t channels, int64_t t,
                              int64_t total, float* __restrict__ y) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const float a = alpha[i / t];
+    const float a = alpha[(i / t) % channels];
     const float v = x[i];
     const float s = sinf(a * v);
     y[i] = v + (1.0f / (a + 1e-9f)) * (s * s);
@@ -151,11 +151,11 @@ extern "C" int cv3_softmax(const float* x, int64_t rows, int64_t dim, int lg, fl
   return cv3::check_launch("softmax");
 }
 
-extern "C" int cv3_snake(const float* x, const float* alpha, int64_t channels, int64_t t, float* y,
+extern "C" int cv3_snake(const float* x, const float* alpha, int64_t batch, int64_t channels, int64_t t, float* y,
                          void* stream) {
-  CV3_REQUIRE(channels >= 0 && t >= 0, CV3_ERR_VALUE, "snake: bad shape");
-  const int64_t total = channels * t;
+  CV3_REQUIRE(batch >= 0 && channels > 0 && t >= 0, CV3_ERR_VALUE, "snake: bad shape");
+  const int64_t total = batch * channels * t;
   if (total == 0) return CV3_OK;
-  snake_kernel<<<grid_for(total, 256), 256, 0, cv3::as_stream(stream)>>>(x, alpha, t, total, y);
+  snake_kernel<<<grid_for(total, 256), 256, 0, cv3::as_stream(stream)>>>(x, alpha, channels, t, total, y);
   return cv3::check_launch("snake");
 }

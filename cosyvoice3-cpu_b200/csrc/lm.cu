@@ -1,0 +1,221 @@
+// Qwen2 decode-step kernels (cv3cpu/models/qwen2.py:139-179, cv3cpu/models/llm.py:112-121).
+//
+// Positions, cache lengths and token ids live in device memory so a whole
+// decode step -- every layer, the head and the next input's embedding -- is a
+// fixed sequence of launches that a CUDA graph replays without the host.
+//
+// KV cache layout: k/v [seq][kv_head][cap][head_dim] fp32 (cv3cpu/models/qwen2.py:74-121
+// keeps (kv_head, cap, head_dim) per layer; here all sequences of a batch are
+// stacked and the capacity is reserved up front).
+#include "common.cuh"
+
+namespace {
+
+// rows r of qkv [R][(H + 2Hk) * D]: sequence seq[r] at position pos[r].
+// q -> qout[r][H][D] rotated; k rotated and v copied into the caches.
+__global__ void rope_qkv_append_kernel(const float* __restrict__ qkv, int64_t ldq, const float* __restrict__ cosT,
+                                       const float* __restrict__ sinT, const int* __restrict__ seq,
+                                       const int* __restrict__ pos, int heads, int kv_heads, int d,
+                                       float* __restrict__ qout, float* __restrict__ kc, float* __restrict__ vc,
+                                       int64_t cap) {
+  const int r = blockIdx.x;
+  const int slot = blockIdx.y;  // [0, H) q heads, [H, H+Hk) k heads, [H+Hk, H+2Hk) v heads
+  const int e = threadIdx.x;
+  if (e >= d) return;
+  const int p = pos[r], s = seq[r];
+  const float* row = qkv + (int64_t)r * ldq;
+  if (slot < heads + kv_heads) {
+    const float* x = row + (int64_t)slot * d;
+    const int half = d / 2;
+    const float rot = e < half ? -x[e + half] : x[e - half];
+    const float c = cosT[(int64_t)p * d + e], sn = sinT[(int64_t)p * d + e];
+    const float v = __fadd_rn(__fmul_rn(x[e], c), __fmul_rn(rot, sn));  // x*cos + rotate_half(x)*sin
+    if (slot < heads) {
+      qout[((int64_t)r * heads + slot) * d + e] = v;
+    } else {
+      const int hk = slot - heads;
+      kc[(((int64_t)s * kv_heads + hk) * cap + p) * d + e] = v;
+    }
+  } else {
+    const int hk = slot - heads - kv_heads;
+    vc[(((int64_t)s * kv_heads + hk) * cap + p) * d + e] = row[(int64_t)slot * d + e];
+  }
+}
+
+constexpr int AT = 256;
+constexpr int DM = 64;
+
+// One CTA per (query head, sequence): scores of all visible keys in shared
+// memory, block max / exp / sum, then a coalesced V pass.
+__global__ void __launch_bounds__(AT)
+decode_attention_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                        const int* __restrict__ lens, int heads, int kv_heads, int d, int64_t cap, float scale,
+                        float* __restrict__ out) {
+  extern __shared__ float sm[];  // [cap] scores, then 4*DM partials
+  __shared__ float qs[DM];
+  __shared__ float red[32];
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int hk = h / (heads / kv_heads);
+  const int m = min((int64_t)lens[b], cap);
+  if (threadIdx.x < DM) qs[threadIdx.x] = threadIdx.x < d ? q[((int64_t)b * heads + h) * d + threadIdx.x] * scale : 0.f;
+  __syncthreads();
+  const float* kb = kc + ((int64_t)b * kv_heads + hk) * cap * d;
+  const float* vb = vc + ((int64_t)b * kv_heads + hk) * cap * d;
+  float lmax = -INFINITY;
+  for (int j = threadIdx.x; j < m; j += AT) {
+    const float4* kr = reinterpret_cast<const float4*>(kb + (int64_t)j * d);
+    float s = 0.f;
+    for (int t = 0; t < d / 4; ++t) {
+      const float4 kv = kr[t];
+      s = fmaf(qs[4 * t], kv.x, s);
+      s = fmaf(qs[4 * t + 1], kv.y, s);
+      s = fmaf(qs[4 * t + 2], kv.z, s);
+      s = fmaf(qs[4 * t + 3], kv.w, s);
+    }
+    sm[j] = s;
+    lmax = fmaxf(lmax, s);
+  }
+  const float mx = block_max(lmax, red);
+  float lsum = 0.f;
+  for (int j = threadIdx.x; j < m; j += AT) {
+    const float p = expf(sm[j] - mx);
+    sm[j] = p;
+    lsum += p;
+  }
+  const float sum = block_sum(lsum, red);
+  float* part = sm + cap;
+  const int e = threadIdx.x % DM, grp = threadIdx.x / DM;
+  float acc = 0.f;
+  if (e < d)
+    for (int j = grp; j < m; j += AT / DM) acc = fmaf(sm[j], vb[(int64_t)j * d + e], acc);
+  part[grp * DM + e] = acc;
+  __syncthreads();
+  if (threadIdx.x < d) {
+    float o = 0.f;
+#pragma unroll
+    for (int g = 0; g < AT / DM; ++g) o += part[g * DM + threadIdx.x];
+    out[(int64_t)b * heads * d + (int64_t)h * d + threadIdx.x] = o / sum;
+  }
+}
+
+// y[r][i] = silu(gu[r][i]) * gu[r][inter + i]   (qwen2.py:175-177, ops.py:30-31)
+__global__ void swiglu_kernel(const float* __restrict__ gu, int64_t rows, int64_t inter, float* __restrict__ y) {
+  const int64_t total = rows * inter;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / inter, c = i - r * inter;
+    const float g = gu[r * 2 * inter + c], u = gu[r * 2 * inter + inter + c];
+    y[i] = (g / (1.0f + expf(-g))) * u;
+  }
+}
+
+// Greedy head: logp = log_softmax(logits) over the whole vocabulary
+// (llm.py:114); token = first argmax of logp[:select] (stop ids masked);
+// records the token, feeds it as the next input id and advances the position.
+__global__ void __launch_bounds__(1024)
+head_select_kernel(const float* __restrict__ logits, int64_t vocab, int64_t select, float* logp_out,
+                   int64_t* __restrict__ next_ids, int* __restrict__ pos, int* __restrict__ lens,
+                   int64_t* __restrict__ history, int64_t hist_stride, const int* __restrict__ step) {
+  __shared__ float red[32];
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const int b = blockIdx.x;
+  const float* x = logits + (int64_t)b * vocab;
+  float m = -INFINITY;
+  for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) m = fmaxf(m, x[i]);
+  m = block_max(m, red);
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) s += expf(x[i] - m);
+  s = block_sum(s, red);
+  const float lse = logf(s);
+  float best = -INFINITY;
+  int besti = 0x7FFFFFFF;
+  for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float lp = (x[i] - m) - lse;
+    if (logp_out) logp_out[(int64_t)b * vocab + i] = lp;
+    if (i < select && (lp > best || (lp == best && i < besti))) { best = lp; besti = (int)i; }
+  }
+  // warp argmax, lowest index on ties
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) { bv[wid] = best; bi[wid] = besti; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int nw = (blockDim.x + 31) / 32;
+    float B = bv[0];
+    int I = bi[0];
+    for (int w = 1; w < nw; ++w)
+      if (bv[w] > B || (bv[w] == B && bi[w] < I)) { B = bv[w]; I = bi[w]; }
+    next_ids[b] = I;
+    if (history) history[(int64_t)b * hist_stride + (step ? *step : 0)] = I;
+    pos[b] += 1;
+    lens[b] += 1;
+  }
+}
+
+__global__ void step_increment_kernel(int* step) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *step += 1;
+}
+
+}  // namespace
+
+extern "C" int cv3_rope_qkv_append(const float* qkv, int64_t rows, int64_t ldq, const float* cos_table,
+                                   const float* sin_table, const int* seq, const int* pos, int64_t heads,
+                                   int64_t kv_heads, int64_t head_dim, float* q_out, float* k_cache, float* v_cache,
+                                   int64_t cap, void* stream) {
+  CV3_REQUIRE(rows >= 0 && heads > 0 && kv_heads > 0 && head_dim > 0 && head_dim <= 1024 && head_dim % 2 == 0,
+              CV3_ERR_VALUE, "rope_qkv_append: bad shape");
+  CV3_REQUIRE(ldq >= (heads + 2 * kv_heads) * head_dim, CV3_ERR_VALUE, "rope_qkv_append: ldq too small");
+  if (rows == 0) return CV3_OK;
+  dim3 grid((unsigned)rows, (unsigned)(heads + 2 * kv_heads));
+  const int threads = ((int)head_dim + 31) / 32 * 32;
+  rope_qkv_append_kernel<<<grid, threads, 0, cv3::as_stream(stream)>>>(
+      qkv, ldq, cos_table, sin_table, seq, pos, (int)heads, (int)kv_heads, (int)head_dim, q_out, k_cache, v_cache, cap);
+  return cv3::check_launch("rope_qkv_append");
+}
+
+extern "C" int cv3_decode_attention(const float* q, const float* k_cache, const float* v_cache, const int* lens,
+                                    int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap,
+                                    float scale, float* out, void* stream) {
+  CV3_REQUIRE(batch >= 0 && heads > 0 && kv_heads > 0 && heads % kv_heads == 0, CV3_ERR_VALUE,
+              "%lld query heads is not a multiple of %lld kv heads", (long long)heads, (long long)kv_heads);
+  CV3_REQUIRE(head_dim % 4 == 0 && head_dim <= DM, CV3_ERR_UNSUPPORTED, "decode_attention: head_dim %lld",
+              (long long)head_dim);
+  CV3_REQUIRE(cap > 0 && (cap + 4 * DM) * 4 <= 200 * 1024, CV3_ERR_UNSUPPORTED, "decode_attention: cap too large");
+  if (batch == 0) return CV3_OK;
+  const int smem = (int)((cap + 4 * DM) * 4);
+  if (smem > 48 * 1024) {
+    int rc = cv3::allow_smem((const void*)decode_attention_kernel, smem);
+    if (rc) return rc;
+  }
+  dim3 grid((unsigned)heads, (unsigned)batch);
+  decode_attention_kernel<<<grid, AT, smem, cv3::as_stream(stream)>>>(q, k_cache, v_cache, lens, (int)heads,
+                                                                       (int)kv_heads, (int)head_dim, cap, scale, out);
+  return cv3::check_launch("decode_attention");
+}
+
+extern "C" int cv3_swiglu(const float* gate_up, int64_t rows, int64_t inter, float* y, void* stream) {
+  CV3_REQUIRE(rows >= 0 && inter > 0, CV3_ERR_VALUE, "swiglu: bad shape");
+  if (rows == 0) return CV3_OK;
+  int64_t grid = (rows * inter + 255) / 256;
+  if (grid > cv3::sm_count() * 16) grid = cv3::sm_count() * 16;
+  swiglu_kernel<<<(unsigned)grid, 256, 0, cv3::as_stream(stream)>>>(gate_up, rows, inter, y);
+  return cv3::check_launch("swiglu");
+}
+
+extern "C" int cv3_head_select(const float* logits, int64_t batch, int64_t vocab, int64_t select, float* logp_out,
+                               int64_t* next_ids, int* pos, int* lens, int64_t* history, int64_t hist_stride,
+                               int* step, void* stream) {
+  CV3_REQUIRE(batch >= 0 && vocab > 0 && select > 0 && select <= vocab, CV3_ERR_VALUE, "head_select: bad shape");
+  if (batch == 0) return CV3_OK;
+  cudaStream_t st = cv3::as_stream(stream);
+  head_select_kernel<<<(unsigned)batch, 1024, 0, st>>>(logits, vocab, select, logp_out, next_ids, pos, lens, history,
+                                                       hist_stride, step);
+  int rc = cv3::check_launch("head_select");
+  if (rc || !step) return rc;
+  step_increment_kernel<<<1, 32, 0, st>>>(step);
+  return cv3::check_launch("step_increment");
+}

@@ -1,0 +1,99 @@
+"""Helpers shared by the device stages: fused weight preparation and raw launches.
+
+The stages call the C ABI with raw device pointers (Python ints) so that a
+step's launch sequence is cheap to issue and can be captured once into a CUDA
+graph.  Weights are prepared once per process and cached in
+:class:`~..weights.DeviceWeights` (fused QKV / gate-up matrices, pre-split
+operands), so the per-step work is launches only.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .. import _dev as D
+from .._lib import call
+from ..quant import QTensor
+
+torch = D.torch
+
+
+class Lin:
+    """A linear layer's device operands: q8 (payload, scales) or fp32 matrix, and bias."""
+
+    __slots__ = ("q8", "w", "scales", "n", "k", "kp", "bias", "_keep")
+
+    def __init__(self, w, bias=None):
+        self._keep = [w, bias]
+        if isinstance(w, QTensor):
+            self.q8 = True
+            self.w, self.scales = w.q.data_ptr(), w.scales.data_ptr()
+            self.n, self.k, self.kp = int(w.shape[0]), int(w.shape[1]), w.padded_k
+        else:
+            self.q8 = False
+            self.w, self.scales = w.data_ptr(), None
+            self.n, self.k = int(w.shape[0]), int(w.shape[1])
+            self.kp = self.k
+        self.bias = bias.data_ptr() if bias is not None else None
+
+    def __call__(self, x: int, m: int, y: int, residual: int = None, ldx: int = None, ldy: int = None,
+                 stream=None):
+        s = stream if stream is not None else D.stream()
+        ldx = self.k if ldx is None else ldx
+        ldy = self.n if ldy is None else ldy
+        if self.q8:
+            call("cv3_q8_linear", x, m, self.k, ldx, self.w, self.scales, self.n, self.kp, self.bias,
+                 residual, y, ldy, s)
+        else:
+            call("cv3_f32_linear", x, m, self.k, ldx, self.w, self.n, self.k, self.bias, residual, y, ldy, s)
+
+
+def cat_rows(parts):
+    """Stack weights along the output dimension (q8 payload + scales, or fp32)."""
+    if all(isinstance(p, QTensor) for p in parts):
+        k = parts[0].shape[1]
+        q = torch.cat([p.q for p in parts], 0).contiguous()
+        s = torch.cat([p.scales for p in parts], 0).contiguous()
+        return QTensor("q8", q, s, (int(q.shape[0]), k), parts[0].block, None)
+    # mixed storage (small q8 and fp32 parts): stack fp32, dequantised exactly on the GPU
+    return torch.cat([f32_of(p) for p in parts], 0).contiguous()
+
+
+def f32_of(w):
+    """fp32 device matrix of a device weight (q8 dequantised on the GPU, exactly)."""
+    if isinstance(w, QTensor):
+        n, k = int(w.shape[0]), int(w.shape[1])
+        out = D.empty((n, k))
+        call("cv3_q8_dequant", w.q.data_ptr(), w.scales.data_ptr(), n, w.padded_k, k, out.data_ptr(), D.stream())
+        return out
+    return w
+
+
+class Graph:
+    """A captured launch sequence; counts its kernel nodes for the launch books."""
+
+    def __init__(self):
+        self.g = None
+        self.nodes = 0
+
+    def capture(self, fn) -> None:
+        from .. import _lib
+        start = _lib.launch_count()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            fn(D.stream())
+        torch.cuda.current_stream().wait_stream(side)
+        self.nodes = _lib.launch_count() - start
+        _lib.note_capture(self.nodes)
+        self.g = g
+
+    def replay(self) -> None:
+        from .. import _lib
+        self.g.replay()
+        _lib.note_replay(self.nodes)
+
+
+def host_table(fn, *args):
+    return torch.from_numpy(np.ascontiguousarray(fn(*args))).cuda()

@@ -1,0 +1,318 @@
+"""Qwen2 decoder body on the GPU (mirror of ``cv3cpu/models/qwen2.py``).
+
+``Qwen2Model.forward(x, cache)`` keeps the reference's contract (embeddings in,
+final hidden states out, causal prefill, one-token steps see the whole cache)
+for any number of rows of one sequence.  :class:`DecodeEngine` runs the
+batched greedy decode: all sequences of a batch advance one token per step,
+and a step -- 24 layers, the head, the greedy pick and the next input's
+embedding -- is one CUDA graph replay with positions, cache lengths and token
+ids kept in device memory.
+
+Per-layer weights are fused once at load: q/k/v rows stacked into one
+``(H + 2 Hk) * D``-row matrix with one bias, gate and up rows stacked into one
+``2 * I``-row matrix; both keep the q8 layout, so a decode step streams each
+int8 payload exactly once.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+from .. import _dev as D
+from .._lib import call
+from ..quant import QTensor
+from ._common import Graph, Lin, cat_rows, f32_of
+
+torch = D.torch
+
+
+@dataclass
+class Qwen2Config:
+    hidden_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    intermediate_size: int
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1000000.0
+    vocab_size: int = 151936
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_attention_heads
+
+    @classmethod
+    def from_meta(cls, meta: dict) -> "Qwen2Config":
+        m = meta["qwen2"]
+        return cls(**{k: m[k] for k in cls.__dataclass_fields__ if k in m})
+
+
+def rope_tables(n: int, dim: int, theta: float):
+    """Half-split RoPE tables, angles in float64 then cast (cv3cpu/models/qwen2.py:46-56)."""
+    inv = 1.0 / (theta ** (np.arange(0, dim, 2, dtype=np.float64) / dim))
+    ang = np.arange(n, dtype=np.float64)[:, None] * inv[None, :]
+    ang = np.concatenate([ang, ang], axis=-1)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+class KVCache:
+    """Device KV cache for ``batch`` sequences: k/v ``[layer][seq][kv_head][cap][head_dim]`` fp32.
+
+    ``len(cache)`` is the cached length of sequence 0 (the reference's one-sequence
+    contract, cv3cpu/models/qwen2.py:74-121); capacity is reserved up front.
+    """
+
+    def __init__(self, layers: int, heads: int, head_dim: int, batch: int = 1, cap: int = 1024):
+        self.layers, self.heads, self.head_dim, self.batch, self.cap = layers, heads, head_dim, batch, cap
+        self.k = D.zeros((layers, batch, heads, cap, head_dim))
+        self.v = D.zeros((layers, batch, heads, cap, head_dim))
+        self.lengths = [0] * batch
+
+    def __len__(self) -> int:
+        return self.lengths[0]
+
+    def layer_ptrs(self, i: int):
+        return self.k[i].data_ptr(), self.v[i].data_ptr()
+
+    def nbytes(self) -> int:
+        return self.k.numel() * 4 * 2
+
+
+class _Layer:
+    __slots__ = ("qkv", "o", "gu", "down", "ln1", "ln2", "qkv32", "o32", "gu32", "down32")
+
+
+class Qwen2Model:
+    """Decoder-only Qwen2 over embeddings; forward follows cv3cpu/models/qwen2.py:139-179."""
+
+    def __init__(self, weights, cfg: Qwen2Config, prefix: str = "llm.model."):
+        self.w = weights
+        self.cfg = cfg
+        self.prefix = prefix
+        self._layers = None
+        self._rope = (0, None, None)
+
+    # -- weights -----------------------------------------------------------------
+    def _t(self, name):
+        return self.w.weight(self.prefix + name)
+
+    def layers(self):
+        if self._layers is None:
+            out = []
+            for i in range(self.cfg.num_hidden_layers):
+                p = f"layers.{i}."
+                L = _Layer()
+                qkv = self.w.cache((self.prefix + p + "qkv",), lambda p=p: cat_rows(
+                    [self._t(p + f"self_attn.{n}_proj.weight") for n in "qkv"]))
+                bqkv = self.w.cache((self.prefix + p + "qkv_bias",), lambda p=p: torch.cat(
+                    [self.w.f32(self.prefix + p + f"self_attn.{n}_proj.bias") for n in "qkv"]).contiguous())
+                gu = self.w.cache((self.prefix + p + "gate_up",), lambda p=p: cat_rows(
+                    [self._t(p + "mlp.gate_proj.weight"), self._t(p + "mlp.up_proj.weight")]))
+                L.qkv = Lin(qkv, bqkv)
+                L.o = Lin(self._t(p + "self_attn.o_proj.weight"))
+                L.gu = Lin(gu)
+                L.down = Lin(self._t(p + "mlp.down_proj.weight"))
+                L.ln1 = self.w.f32(self.prefix + p + "input_layernorm")
+                L.ln2 = self.w.f32(self.prefix + p + "post_attention_layernorm")
+                L.qkv32 = L.o32 = L.gu32 = L.down32 = None
+                out.append(L)
+            self._layers = out
+        return self._layers
+
+    def _wide(self, L: _Layer):
+        """fp32 copies (dequantised on the GPU) for multi-row prefill GEMMs."""
+        if L.qkv32 is None:
+            L.qkv32 = Lin(f32_of(L.qkv._keep[0]), L.qkv._keep[1])
+            L.o32 = Lin(f32_of(L.o._keep[0]))
+            L.gu32 = Lin(f32_of(L.gu._keep[0]))
+            L.down32 = Lin(f32_of(L.down._keep[0]))
+        return L.qkv32, L.o32, L.gu32, L.down32
+
+    def norm_w(self):
+        return self.w.f32(self.prefix + "norm")
+
+    def rope(self, n: int):
+        if self._rope[0] < n:
+            cap = max(n, 2 * self._rope[0], 1024)
+            c, s = rope_tables(cap, self.cfg.head_dim, self.cfg.rope_theta)
+            self._rope = (cap, torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda())
+        return self._rope[1], self._rope[2]
+
+    def embed(self, ids):
+        from .. import ops
+        return ops.embedding(self.w.weight(self.prefix + "embed_tokens"), ids)
+
+    def new_cache(self, batch: int = 1, cap: int = 1024) -> KVCache:
+        c = self.cfg
+        return KVCache(c.num_hidden_layers, c.num_key_value_heads, c.head_dim, batch, cap)
+
+    # -- forward over T rows of one sequence ---------------------------------------
+    def forward(self, x, cache: KVCache = None, seq: int = 0, tile_bytes: int = 0):
+        """``x`` ``(T, hidden)`` -> final hidden states ``(T, hidden)`` (host in -> host out)."""
+        host = D.is_host(x)
+        h = D.dev(x).clone()
+        T = int(h.shape[0])
+        c = self.cfg
+        H, Hk, hd, hid = c.num_attention_heads, c.num_key_value_heads, c.head_dim, c.hidden_size
+        if cache is None:
+            cache = self.new_cache(1, max(T, 1))
+            seq = 0
+        past = cache.lengths[seq]
+        if past + T > cache.cap:
+            raise ValueError(f"KV cache capacity {cache.cap} exceeded ({past} + {T})")
+        cos, sin = self.rope(past + T)
+        st = D.stream()
+        n = D.empty((T, hid))
+        qkv = D.empty((T, (H + 2 * Hk) * hd))
+        q = D.empty((T, H * hd))
+        a = D.empty((T, H * hd))
+        gu = D.empty((T, 2 * c.intermediate_size))
+        act = D.empty((T, c.intermediate_size))
+        seqs = torch.full((T,), seq, dtype=torch.int32, device="cuda")
+        pos = torch.arange(past, past + T, dtype=torch.int32, device="cuda")
+        scale = float(np.float32(1.0 / np.sqrt(hd)))
+        mask_kind = 1 if T > 1 else 0
+        for i, L in enumerate(self.layers()):
+            lq, lo, lg, ld = (L.qkv, L.o, L.gu, L.down) if T <= 8 else self._wide(L)
+            kc, vc = cache.layer_ptrs(i)
+            call("cv3_rms_norm", h.data_ptr(), L.ln1.data_ptr(), T, hid, c.rms_norm_eps, n.data_ptr(), st)
+            lq(n.data_ptr(), T, qkv.data_ptr(), stream=st)
+            call("cv3_rope_qkv_append", qkv.data_ptr(), T, qkv.shape[1], cos.data_ptr(), sin.data_ptr(),
+                 seqs.data_ptr(), pos.data_ptr(), H, Hk, hd, q.data_ptr(), kc, vc, cache.cap, st)
+            kseq = seq * Hk * cache.cap * hd * 4
+            call("cv3_attention", q.data_ptr(), 0, hd, H * hd,
+                 kc + kseq, 0, cache.cap * hd, hd, vc + kseq, 0, cache.cap * hd, hd,
+                 a.data_ptr(), 0, hd, H * hd, 1, H, Hk, T, past + T, hd, scale, mask_kind, past, 0, st)
+            lo(a.data_ptr(), T, h.data_ptr(), residual=h.data_ptr(), stream=st)
+            call("cv3_rms_norm", h.data_ptr(), L.ln2.data_ptr(), T, hid, c.rms_norm_eps, n.data_ptr(), st)
+            lg(n.data_ptr(), T, gu.data_ptr(), stream=st)
+            call("cv3_swiglu", gu.data_ptr(), T, c.intermediate_size, act.data_ptr(), st)
+            ld(act.data_ptr(), T, h.data_ptr(), residual=h.data_ptr(), stream=st)
+        out = D.empty((T, hid))
+        call("cv3_rms_norm", h.data_ptr(), self.norm_w().data_ptr(), T, hid, c.rms_norm_eps, out.data_ptr(), st)
+        cache.lengths[seq] = past + T
+        return D.out(out, host)
+
+
+class DecodeEngine:
+    """Batched greedy decode, one CUDA graph per step.
+
+    Device state per sequence: ``pos`` (position of the token being fed),
+    ``lens`` (cache length after it is appended), ``next_ids`` (token fed next)
+    and ``history`` (tokens chosen so far).  A step runs every layer on the
+    ``batch`` rows, the head GEMV, :c:func:`cv3_head_select` (log_softmax,
+    first argmax over the speech tokens, bookkeeping) and the embedding gather
+    of the chosen tokens into the next step's input.
+    """
+
+    def __init__(self, model: Qwen2Model, head_w, speech_emb, speech_tokens: int, batch: int, cap: int,
+                 max_steps: int):
+        c = model.cfg
+        self.m, self.c, self.B, self.cap = model, c, batch, cap
+        H, Hk, hd, hid = c.num_attention_heads, c.num_key_value_heads, c.head_dim, c.hidden_size
+        self.cache = model.new_cache(batch, cap)
+        self.head = Lin(head_w)
+        self.vocab = self.head.n
+        self.select = speech_tokens
+        self.emb = speech_emb
+        self.h = D.zeros((batch, hid))
+        self.n = D.empty((batch, hid))
+        self.qkv = D.empty((batch, (H + 2 * Hk) * hd))
+        self.q = D.empty((batch, H * hd))
+        self.a = D.empty((batch, H * hd))
+        self.gu = D.empty((batch, 2 * c.intermediate_size))
+        self.act = D.empty((batch, c.intermediate_size))
+        self.logits = D.empty((batch, self.vocab))
+        self.logp = D.empty((batch, self.vocab))
+        self.next_ids = torch.zeros(batch, dtype=torch.int64, device="cuda")
+        self.seqs = torch.arange(batch, dtype=torch.int32, device="cuda")
+        self.pos = torch.zeros(batch, dtype=torch.int32, device="cuda")
+        self.lens = torch.zeros(batch, dtype=torch.int32, device="cuda")
+        self.step_no = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.history = torch.zeros((batch, max_steps), dtype=torch.int64, device="cuda")
+        self.max_steps = max_steps
+        self.cos, self.sin = model.rope(cap)
+        self.scale = float(np.float32(1.0 / np.sqrt(hd)))
+        self.graph = None
+        self.keep_logp = False
+
+    def launches(self, st):
+        """One decode step for every sequence (all pointers fixed -> graph-capturable)."""
+        c, B = self.c, self.B
+        H, Hk, hd, hid = c.num_attention_heads, c.num_key_value_heads, c.head_dim, c.hidden_size
+        for i, L in enumerate(self.m.layers()):
+            kc, vc = self.cache.layer_ptrs(i)
+            call("cv3_rms_norm", self.h.data_ptr(), L.ln1.data_ptr(), B, hid, c.rms_norm_eps, self.n.data_ptr(), st)
+            L.qkv(self.n.data_ptr(), B, self.qkv.data_ptr(), stream=st)
+            call("cv3_rope_qkv_append", self.qkv.data_ptr(), B, self.qkv.shape[1], self.cos.data_ptr(),
+                 self.sin.data_ptr(), self.seqs.data_ptr(), self.pos.data_ptr(), H, Hk, hd, self.q.data_ptr(),
+                 kc, vc, self.cap, st)
+            call("cv3_decode_attention", self.q.data_ptr(), kc, vc, self.lens.data_ptr(), B, H, Hk, hd, self.cap,
+                 self.scale, self.a.data_ptr(), st)
+            L.o(self.a.data_ptr(), B, self.h.data_ptr(), residual=self.h.data_ptr(), stream=st)
+            call("cv3_rms_norm", self.h.data_ptr(), L.ln2.data_ptr(), B, hid, c.rms_norm_eps, self.n.data_ptr(), st)
+            L.gu(self.n.data_ptr(), B, self.gu.data_ptr(), stream=st)
+            call("cv3_swiglu", self.gu.data_ptr(), B, c.intermediate_size, self.act.data_ptr(), st)
+            L.down(self.act.data_ptr(), B, self.h.data_ptr(), residual=self.h.data_ptr(), stream=st)
+        call("cv3_rms_norm", self.h.data_ptr(), self.m.norm_w().data_ptr(), B, hid, c.rms_norm_eps,
+             self.n.data_ptr(), st)
+        self.select_and_feed(st)
+
+    def select_and_feed(self, st):
+        self.head(self.n.data_ptr(), self.B, self.logits.data_ptr(), stream=st)
+        call("cv3_head_select", self.logits.data_ptr(), self.B, self.vocab, self.select,
+             self.logp.data_ptr() if self.keep_logp else None, self.next_ids.data_ptr(), self.pos.data_ptr(),
+             self.lens.data_ptr(), self.history.data_ptr(), self.max_steps, self.step_no.data_ptr(), st)
+        e = self.emb
+        if isinstance(e, QTensor):
+            call("cv3_embedding", e.q.data_ptr(), 2, e.scales.data_ptr(), int(e.shape[0]), int(e.shape[1]),
+                 e.padded_k, self.next_ids.data_ptr(), self.B, self.h.data_ptr(), int(e.shape[1]), None, st)
+        else:
+            call("cv3_embedding", e.data_ptr(), 0, None, int(e.shape[0]), int(e.shape[1]), int(e.shape[1]),
+                 self.next_ids.data_ptr(), self.B, self.h.data_ptr(), int(e.shape[1]), None, st)
+
+    def prefill(self, prompts):
+        """Run each sequence's prompt rows, pick its first token, set positions."""
+        if len(prompts) != self.B:
+            raise ValueError(f"{len(prompts)} prompts for a batch of {self.B}")
+        last = D.empty((self.B, self.c.hidden_size))
+        self.cache.lengths = [0] * self.B          # a new batch overwrites the cache from position 0
+        for b, x in enumerate(prompts):
+            hb = self.m.forward(D.dev(x), self.cache, seq=b)
+            last[b].copy_(hb[-1])
+        T = torch.tensor([int(np.shape(x)[0]) for x in prompts], dtype=torch.int32, device="cuda")
+        self.pos.copy_(T - 1)       # head_select advances pos/lens by one
+        self.lens.copy_(T)
+        self.step_no.zero_()
+        self.n.copy_(last)
+        self.select_and_feed(D.stream())
+
+    def capture(self):
+        g = Graph()
+        g.capture(self.launches)
+        self.graph = g
+
+    def step(self):
+        if self.graph is None:
+            self.launches(D.stream())
+        else:
+            self.graph.replay()
+
+    def run(self, prompts, n_tokens: int, use_graph: bool = True):
+        """Greedy-decode ``n_tokens`` tokens for every prompt; returns ``[B][n_tokens]`` ids (device)."""
+        if n_tokens > self.max_steps:
+            raise ValueError("n_tokens exceeds max_steps")
+        if max(int(np.shape(x)[0]) for x in prompts) + n_tokens > self.cap:
+            raise ValueError("prompt + tokens exceed the KV cache capacity")
+        self.prefill(prompts)
+        if use_graph and self.graph is None and n_tokens > 1:
+            # capture replays from a snapshot of the state so capture's own launch has no effect
+            saved = [t.clone() for t in (self.h, self.pos, self.lens, self.step_no, self.next_ids, self.history)]
+            self.capture()
+            for t, s in zip((self.h, self.pos, self.lens, self.step_no, self.next_ids, self.history), saved):
+                t.copy_(s)
+        for _ in range(n_tokens - 1):
+            self.step()
+        return self.history[:, :n_tokens].clone()

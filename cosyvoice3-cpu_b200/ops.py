@@ -79,7 +79,7 @@ def snake(x, alpha, eps: float = 1e-9):
     if ad.numel() != c:
         raise ValueError(f"snake: {ad.numel()} alphas for {c} channels")
     y = torch.empty_like(xd)
-    call("cv3_snake", D.ptr(xd), D.ptr(ad), c, xd.numel() // max(c, 1), D.ptr(y), D.stream())
+    call("cv3_snake", D.ptr(xd), D.ptr(ad), 1, c, xd.numel() // max(c, 1), D.ptr(y), D.stream())
     return D.out(y, host)
 
 
@@ -298,8 +298,10 @@ def interpolate_linear(x, size: int, align_corners: bool = False):   # cv3cpu/op
     i1 = np.minimum(i0 + 1, t - 1)
     w = (pos - i0).astype(np.float32)
     y = D.empty((c, size))
-    call("cv3_interpolate_linear", D.ptr(xd), c, t, D.ptr(D.dev(i0, torch.int64)),
-         D.ptr(D.dev(i1, torch.int64)), D.ptr(D.dev(w)), size, D.ptr(y), D.stream())
+    # keep every temporary alive until the launch is queued (a freed block could
+    # otherwise be handed to the next temporary of the same call)
+    i0d, i1d, wd = D.dev(i0, torch.int64), D.dev(i1, torch.int64), D.dev(w)
+    call("cv3_interpolate_linear", D.ptr(xd), c, t, D.ptr(i0d), D.ptr(i1d), D.ptr(wd), size, D.ptr(y), D.stream())
     return D.out(y, host)
 
 
@@ -318,7 +320,8 @@ def stft_stacked(x, n_fft: int, hop: int, win):
     frames = 1 + L // hop
     nb = n_fft // 2 + 1
     out = D.empty(lead + (2 * nb, frames))
-    call("cv3_stft", D.ptr(xd), b, L, n_fft, hop, D.ptr(D.dev(win)), D.ptr(out), frames, D.stream())
+    wd = D.dev(win)
+    call("cv3_stft", D.ptr(xd), b, L, n_fft, hop, D.ptr(wd), D.ptr(out), frames, D.stream())
     return out
 
 
@@ -348,7 +351,8 @@ def istft_stacked(spec, n_fft: int, hop: int, win, mode: int = 0, limit: float =
     n_out = total - 2 * off if center else total
     scratch = D.empty((b, frames, n_fft))
     y = D.empty(lead + (n_out,))
-    call("cv3_istft", D.ptr(sd), mode, b, frames, n_fft, hop, D.ptr(D.dev(win)), float(limit), off,
+    wd = D.dev(win)
+    call("cv3_istft", D.ptr(sd), mode, b, frames, n_fft, hop, D.ptr(wd), float(limit), off,
          D.ptr(scratch), D.ptr(y), n_out, D.stream())
     if length is not None:
         if n_out >= length:

@@ -207,7 +207,8 @@ class DeviceWeights:
         def up():
             t = self.host_tensor(name)
             if isinstance(t, QTensor):
-                return torch.from_numpy(np.ascontiguousarray(t.dequant())).to(self.device)
+                from .models._common import f32_of      # dequantised on the GPU
+                return f32_of(self.weight(name))
             return torch.from_numpy(np.ascontiguousarray(np.asarray(t, dtype=np.float32))).to(self.device)
         return self._put(("f32", name), up)
 

@@ -49,6 +49,11 @@ const char* cv3_last_error(void);
 /* CV3_ABI_VERSION of the loaded library. */
 int cv3_abi_version(void);
 
+
+/* Kernels this library has launched (or recorded into a graph being
+ * captured) since it was loaded, over all host threads. */
+unsigned long long cv3_launch_count(void);
+
 /* SM count and compute capability of the current device. */
 int cv3_device_info(int* sm_count, int* cc_major, int* cc_minor);
 
@@ -106,9 +111,9 @@ int cv3_layer_norm(const float* x, const float* w, const float* b, int64_t rows,
 /* Row-wise softmax (log=0) or log_softmax (log=1); cv3cpu/ops.py:84-93. */
 int cv3_softmax(const float* x, int64_t rows, int64_t dim, int log, float* y, void* stream);
 
-/* Snake over (C, T): y = x + sin(a x)^2 / (a + 1e-9), a per channel;
+/* Snake over [batch][C][T]: y = x + sin(a x)^2 / (a + 1e-9), a per channel;
  * cv3cpu/ops.py:77-81. */
-int cv3_snake(const float* x, const float* alpha, int64_t channels, int64_t t,
+int cv3_snake(const float* x, const float* alpha, int64_t batch, int64_t channels, int64_t t,
               float* y, void* stream);
 
 
@@ -198,6 +203,114 @@ int cv3_torch_rand(uint64_t seed, int64_t skip, int64_t n, float* out, void* str
  * with cv3cpu/torch_rng.py:117-142.  Consumes n (+16 when n % 16 != 0) words,
  * or 4*ceil(n/2) words when n < 16.  scratch: 128 device bytes. */
 int cv3_torch_randn(uint64_t seed, int64_t skip, int64_t n, float* out, void* scratch, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Qwen2 decode step (cv3cpu/models/qwen2.py:139-179, llm.py:112-121)    */
+/* ------------------------------------------------------------------ */
+
+/* RoPE + KV append for `rows` rows of fused qkv [rows][ldq] (q heads, then k,
+ * then v, head_dim each).  Row r belongs to sequence seq[r] at position pos[r]
+ * (device int32).  q is rotated into q_out [rows][heads][head_dim]; k is
+ * rotated and v copied into k_cache/v_cache [seq][kv_heads][cap][head_dim].
+ * Half-split rotation x*cos + rotate_half(x)*sin with host-built float64->
+ * float32 tables [positions][head_dim]; replaces qwen2.py:64-71 apply_rope and
+ * :108-118 KVCache.append. */
+int cv3_rope_qkv_append(const float* qkv, int64_t rows, int64_t ldq, const float* cos_table,
+                        const float* sin_table, const int* seq, const int* pos, int64_t heads,
+                        int64_t kv_heads, int64_t head_dim, float* q_out, float* k_cache, float* v_cache,
+                        int64_t cap, void* stream);
+
+/* One-query-per-sequence attention over the cache: out [batch][heads*head_dim]
+ * from q [batch][heads][head_dim] and the first lens[b] (device int32) cached
+ * keys of sequence b.  Replaces ops.sdpa with mask None for a 1-token step
+ * (qwen2.py:148, :169). */
+int cv3_decode_attention(const float* q, const float* k_cache, const float* v_cache, const int* lens,
+                         int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap,
+                         float scale, float* out, void* stream);
+
+/* y[r][i] = silu(gu[r][i]) * gu[r][inter + i]; qwen2.py:175-177. */
+int cv3_swiglu(const float* gate_up, int64_t rows, int64_t inter, float* y, void* stream);
+
+/* Greedy head for `batch` rows of logits [batch][vocab]: log_softmax over the
+ * vocabulary (llm.py:114; stored to logp_out when non-NULL), token = first
+ * argmax of the log-probabilities over [0, select) (stop ids masked), written
+ * to next_ids[b] and history[b][*step]; then pos[b]++, lens[b]++ and, when
+ * step is non-NULL, ++*step.  All state is device memory. */
+int cv3_head_select(const float* logits, int64_t batch, int64_t vocab, int64_t select, float* logp_out,
+                    int64_t* next_ids, int* pos, int* lens, int64_t* history, int64_t hist_stride,
+                    int* step, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* DiT flow estimator and Euler/CFG solve (cv3cpu/models/dit.py, flow.py) */
+/* ------------------------------------------------------------------ */
+
+/* CFG input rows: out [2*utts][frames][3*mel + spk_dim] = concat(x, cond, mu,
+ * spk) for b = 2u (utterance u) and concat(x, 0, 0, 0) for b = 2u+1; x, cond,
+ * mu are channel-major [utts][mel][frames], spk [utts][spk_dim].
+ * Replaces dit.py:92-97 with flow.py:71-77. */
+int cv3_dit_input_cat(const float* x, const float* cond, const float* mu, const float* spk, int64_t utts,
+                      int64_t frames, int64_t mel, int64_t spk_dim, float* out, void* stream);
+
+/* y = layer_norm(h, eps) * (1 + scale) + shift per row (no affine); row r
+ * uses scale/shift + (r / rows_per_group) * mod_stride (rows_per_group 0:
+ * one shared vector).  Replaces dit.py:168-169, :171-172, :178. */
+int cv3_ln_modulate(const float* h, int64_t rows, int64_t dim, float eps, const float* scale,
+                    const float* shift, int64_t rows_per_group, int64_t mod_stride, float* y, void* stream);
+
+/* h += gate * y per row (gate chosen like cv3_ln_modulate); dit.py:170, :173. */
+int cv3_gate_residual(float* h, const float* y, const float* gate, int64_t rows, int64_t dim,
+                      int64_t rows_per_group, int64_t gate_stride, void* stream);
+
+/* In place, on rows of fused qkv [rows][ld]: rotate channel pairs
+ * (2i, 2i+1), i < width/2, of q (offset 0) and k (offset k_offset) by the
+ * angle tables [frames][width] at position row % frames -- the reference's
+ * rotate-before-head-split quirk that only moves head 0 (dit.py:32-54). */
+int cv3_partial_rope(float* qkv, int64_t rows, int64_t ld, int64_t k_offset, int64_t frames,
+                     int64_t width, const float* cos_table, const float* sin_table, void* stream);
+
+/* out[b] = in[b]^T for batch matrices [rows][cols]; accumulate=1 adds. */
+int cv3_transpose(const float* in, int64_t batch, int64_t rows, int64_t cols, float* out, int accumulate,
+                  void* stream);
+
+/* Euler step with guidance: x[u][c][n] += dt * ((1 + cfg) * d[2u][n][c] - cfg * d[2u+1][n][c]),
+ * d token-major [2*utts][frames][mel]; flow.py:86-87. */
+int cv3_cfg_euler(float* x, const float* d, int64_t utts, int64_t mel, int64_t frames, double cfg_rate,
+                  float dt, void* stream);
+
+/* y = x / max(||x||_2, 1e-12) per row; flow.py:105-106. */
+int cv3_l2_normalize(const float* x, int64_t rows, int64_t dim, float* y, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* HiFT vocoder (cv3cpu/models/hift.py)                                 */
+/* ------------------------------------------------------------------ */
+
+/* f0[b][t] = float32(|sum_c double(x[b][c][t]) * w[c] + b[0]|): the F0 head's
+ * float64 classifier over float32 condnet features; hift.py:69-72, :217. */
+int cv3_f0_classifier(const float* x, int64_t batch, int64_t channels, int64_t t, const double* w,
+                      const double* b, float* f0, void* stream);
+
+/* NSF harmonic source: out[b][s], s < up*t, = tanh(sum_h sw[s][h] * w[h] + bias)
+ * with sw = float32(sin(phase[t][h])) * alpha * uv + amp * noise[s][h],
+ * phase = cumsum_t((f0*(h+1)/sample_rate) mod 1) * 2pi * up in float64,
+ * uv = f0 > voiced_threshold, amp = uv*sigma + (1-uv)*alpha/3.  noise is the
+ * fixed uniform dither [up*t][harmonics]; sines_scratch holds
+ * [batch][t][harmonics] floats.  Replaces hift.py:90-111. */
+int cv3_nsf_source(const float* f0, int64_t batch, int64_t t, int64_t harmonics, int64_t sample_rate,
+                   int64_t up, double alpha, double sigma, double voiced_threshold, const float* noise,
+                   const float* w, const float* bias, float* sines_scratch, float* out, void* stream);
+
+#define CV3_BIN_ADD 0
+#define CV3_BIN_SUB 1
+#define CV3_BIN_MUL 2
+#define CV3_BIN_DIV_SCALAR 3
+#define CV3_BIN_MUL_SCALAR 4
+
+/* y = a (op) b, or a (op) scalar; the residual sums and the resblock mean of
+ * hift.py:128, :164-165. */
+int cv3_binary(int op, const float* a, const float* b, float scalar, int64_t n, float* y, void* stream);
+
+/* y[r] = [x[r][1], x[r][0..t)]: ReflectionPad1d((1, 0)); hift.py:144. */
+int cv3_reflect_left1(const float* x, int64_t rows, int64_t t, float* y, void* stream);
 
 #ifdef __cplusplus
 }

@@ -250,16 +250,19 @@ def conv1d(x, weight, bias=None, stride: int = 1, dilation: int = 1, groups: int
         return np.zeros((cout, 0), F32)
     out = np.empty((cout, t_out), F32)
     cout_g = cout // groups
+    # time tiles sized like the reference's 8 MB im2col budget (ops.py:198-199)
+    tile_frames = max(1, min(t_out, (8 << 20) // max(1, cin_g * k * 4)))
     for g in range(groups):
         xg = xp[g * cin_g:(g + 1) * cin_g]
         wg = weight if is_quant(weight) else \
             weight[g * cout_g:(g + 1) * cout_g].reshape(cout_g, cin_g * k)
+        sc, stt = xg.strides
         for t0 in range(0, t_out, tile_frames):
             t1 = min(t_out, t0 + tile_frames)
-            # column (c, j) of frame t reads xg[c, t*stride + j*dilation]
-            taps = (np.arange(t0, t1)[None, :] * stride
-                    + (np.arange(k) * dilation)[:, None])          # (k, t)
-            cols = xg[:, taps].reshape(cin_g * k, t1 - t0)
+            # column (c, j) of frame t reads xg[c, t*stride + j*dilation]: a strided view
+            view = np.lib.stride_tricks.as_strided(xg[:, t0 * stride:], shape=(cin_g, k, t1 - t0),
+                                                   strides=(sc, stt * dilation, stt * stride), writeable=False)
+            cols = np.ascontiguousarray(view).reshape(cin_g * k, t1 - t0)
             if is_quant(wg):
                 out[:, t0:t1] = qmatmul(cols.T, wg).T
             else:

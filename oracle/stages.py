@@ -170,7 +170,7 @@ class SpeechLM:
             top = self.greedy(logp)
             toks.append(top)
             logps.append(logp)
-            nxt = top if forced is None else int(forced[i])
+            nxt = top if (forced is None or i >= len(forced)) else int(forced[i])
             x = self.speech_emb([nxt])
         return toks, np.stack(logps) if logps else np.zeros((0, 0), F32)
 
