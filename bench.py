@@ -326,8 +326,40 @@ def run_cuda(args, rank: int, world: int) -> None:
         }), flush=True)
 
 
+def run_slice(args) -> None:
+    """Profiling slice: build everything, then, between cudaProfilerStart/Stop, run
+    one eager batched LM decode step, one DiT forward at the bench's CFG shape and
+    one batched vocoder pass (every kernel of a step, each launched once or per
+    layer), for ``ncu --profile-from-start off``."""
+    import torch
+    synth, pipeline = pkg("synth"), pkg("pipeline")
+    W = synth.synthetic_weights("balanced")
+    tts = pipeline.CosyVoice3CUDA(W)
+    reqs = make_requests(range(UTTS), W.meta)
+    prepared = tts.prepare(reqs)
+    tts.run_prepared(prepared, 4)                    # builds engines, graphs, tables
+    eng = tts.llm.last_engine
+    flow, dit = tts.flow, tts.flow.estimator
+    N = 2 * (PROMPT_TOKENS + TOKENS)
+    S = flow._solver(UTTS, N)
+    mel = torch.randn(UTTS, 80, 2 * TOKENS, device="cuda")
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    st = torch.cuda.current_stream().cuda_stream
+    eng.launches(st)
+    pkg("_lib").call("cv3_dit_input_cat", S["x"].data_ptr(), S["cond"].data_ptr(), S["mu"].data_ptr(),
+                     S["spk"].data_ptr(), UTTS, N, 80, 80, S["ws"].cat.data_ptr(), st)
+    dit.modulation(S["tfeat"][0:1], S["mods"], S["temb"], st)
+    dit.body(S["ws"], S["mods"], 0, st)
+    tts.hift.inference_batch(mel)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print("slice done", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--slice", action="store_true", help="profiling slice (see run_slice)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
@@ -342,7 +374,9 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     try:
-        if args.impl == "reference":
+        if args.slice:
+            run_slice(args)
+        elif args.impl == "reference":
             run_reference(args, rank, world)
         else:
             run_cuda(args, rank, world)

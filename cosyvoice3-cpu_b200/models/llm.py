@@ -162,6 +162,7 @@ class CosyVoice3LM:
         need = max(int(np.shape(p)[0]) for p in prompts) + n_tokens
         cap = cap or max(256, -(-need // 256) * 256)
         eng = self.engine(B, cap, max(n_tokens, 1))
+        self.last_engine = eng
         eng.keep_logp = keep_logp
         if keep_logp and eng.graph is not None:
             eng.graph = None
