@@ -62,10 +62,16 @@ SIGNATURES = {
     "cv3_nsf_source": [P, I64, I64, I64, I64, I64, D, D, D, P, P, P, P, P, P],
     "cv3_binary": [I32, P, P, F, I64, P, P],
     "cv3_reflect_left1": [P, I64, I64, P, P],
+    "cv3_tc_gemm": [P, I64, P, I64, P, I64, I64, I64, I64, I32, P, P, I64, I64, P],
+    "cv3_tc_gemm_status": [P],
+    "cv3_tc_gemm_cfg": [P, I64, P, I64, P, I64, I64, I64, I64, I32, P, P, I64, I64, I32, I32, P],
 }
 _RESTYPE = {"cv3_last_error": ctypes.c_char_p, "cv3_launch_count": ctypes.c_ulonglong}
 
 _lib: Optional[ctypes.CDLL] = None
+
+
+EPI_BIAS, EPI_GELU, EPI_GATED_RESIDUAL, EPI_RESIDUAL = 0, 1, 2, 3
 
 
 def exported_names():

@@ -1,0 +1,424 @@
+// fp32-accurate GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+//   C[M][N] = epilogue(A[M][K] . B[N][K]^T)      A, B, C fp32, row-major, K-major operands
+//
+// Precision: 3xTF32.  Each operand element x is split into hi = x with its low
+// 13 mantissa bits cleared (exactly a tf32 value) and lo = x - hi (exact in
+// fp32, <= 13 significant bits), and the product is accumulated in fp32 in
+// TMEM as hi*hi + hi*lo + lo*hi; the dropped lo*lo term and the truncation of
+// lo to tf32 leave ~2^-21 relative error per product, fp32-SGEMM territory.
+// This is how the DiT's fp32 linears (cv3cpu/ops.py:121 -> BLAS sgemm) run on
+// tensor cores without leaving the reference's 1e-5 tolerance.
+//
+// CTA = 6 warps, one 128x128 output tile, K in 32-element (128 B) blocks:
+//   warp 0   TMA producer: A and B tiles (SWIZZLE_128B) into a 3-stage ring;
+//   warp 1   MMA issuer (one thread): 4 K-steps x 3 tcgen05.mma kind::tf32 per
+//            stage, tcgen05.commit frees the stage / signals the accumulator;
+//   warps 2-5 split each landed stage in place (hi) and into the lo buffers,
+//            then run the epilogue: tcgen05.ld 32 lanes x 32 columns at a
+//            time, bias / GELU-tanh / gated residual, fp32 stores.
+// The split buffers share the TMA tile's swizzled layout element for element,
+// so the converters never need to know the swizzle.
+//
+// Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records
+// an error code (read with cv3_tc_gemm_status), skips its remaining work, waits
+// (bounded) for its own MMAs, frees TMEM and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 32;  // BK fp32 = 128 bytes = one swizzle row
+constexpr int STAGES = 3;
+constexpr int TILE_A = BM * BK * 4;  // 16 KB
+constexpr int TILE_B = BN * BK * 4;  // 16 KB
+constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;  // up to 4 accumulators of BN fp32 columns
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
+
+__device__ int g_tc_err = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; returns false (and records `code`) if the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  while (!mbar_test(bar, parity)) {
+    if (now_ns() - t0 > WAIT_NS) {
+      atomicCAS(&g_tc_err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor, K-major, SWIZZLE_128B: 8-row x 128 B atoms,
+// atoms 1024 B apart (SBO), leading offset unused (1), Blackwell version 1.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::tf32 instruction descriptor: D f32, A/B tf32, K-major, M = 128, N = BN.
+constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(IDESC), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Split one stage in place: hi = x & ~0x1FFF (tf32), lo = x - hi.
+__device__ __forceinline__ void split_tile(float* hi, float* lo, int bytes, int tid, int nthreads) {
+  float4* h4 = reinterpret_cast<float4*>(hi);
+  float4* l4 = reinterpret_cast<float4*>(lo);
+  for (int i = tid; i < bytes / 16; i += nthreads) {
+    float4 x = h4[i], h, l;
+    h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+    h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+    h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+    h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+    l.x = x.x - h.x;
+    l.y = x.y - h.y;
+    l.z = x.z - h.z;
+    l.w = x.w - h.w;
+    h4[i] = h;
+    l4[i] = l;
+  }
+}
+
+struct Epi {
+  int k_chunks;          // 1, 2 or 4 accumulators, each summing a contiguous K range
+  int split_cross;       // 1: hi*lo + lo*hi accumulate apart from hi*hi (k_chunks <= 2)
+  int mode;              // 0: +bias; 1: gelu_tanh(+bias); 2: h += gate * (+bias); 3: h += (+bias)
+  const float* bias;     // [N] or null
+  const float* gate;     // mode 2: gate + (row / rows_per_group) * gate_stride
+  int64_t rows_per_group, gate_stride;
+};
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float c = 0.7978845608028654f;
+  const float inner = x + 0.044715f * x * x * x;
+  return 0.5f * x * (1.0f + tanhf(c * inner));
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, int M, int N,
+               int K, float* __restrict__ C, int64_t ldc, Epi ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* conv = full + STAGES;
+  uint64_t* empty = conv + STAGES;
+  uint64_t* accb = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* issued = abort_flag + 1;  // [STAGES]: last round loaded into each stage, -1 if none
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int nk = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);  // one arrival per converter warp
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    *abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) issued[s] = -1;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t round = kb / STAGES;
+        if (*(volatile int*)abort_flag || !mbar_wait(&empty[s], (round & 1) ^ 1, 1)) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        issued[s] = (int)round;
+        mbar_expect_tx(&full[s], TILE_A + TILE_B);
+        tma_load_2d(st, &map_a, &full[s], kb * BK, m0);
+        tma_load_2d(st + 2 * TILE_A, &map_b, &full[s], kb * BK, n0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t round = kb / STAGES;
+        if (*(volatile int*)abort_flag || !mbar_wait(&conv[s], round & 1, 2)) {
+          *(volatile int*)abort_flag = 1;
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_hi = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t a_lo = a_hi + TILE_A;
+        const uint32_t b_hi = a_hi + 2 * TILE_A;
+        const uint32_t b_lo = b_hi + TILE_B;
+        // accumulator of this K block: K range chunk, cross terms optionally apart
+        const int chunk = kb * ep.k_chunks / nk;
+        const int first_kb = (chunk * nk + ep.k_chunks - 1) / ep.k_chunks;  // first kb of this chunk
+        const uint32_t d_main = tmem + (uint32_t)(chunk * BN);
+        const uint32_t d_cross = ep.split_cross ? tmem + (uint32_t)((ep.k_chunks + chunk) * BN) : d_main;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
+          const bool start = (kb == first_kb && kk == 0);
+          mma_tf32(d_cross, umma_desc(a_lo + off), umma_desc(b_hi + off), start ? 0u : 1u);
+          mma_tf32(d_cross, umma_desc(a_hi + off), umma_desc(b_lo + off), 1u);
+          mma_tf32(d_main, umma_desc(a_hi + off), umma_desc(b_hi + off), (start && ep.split_cross) ? 0u : 1u);
+        }
+        mma_commit(&empty[s]);
+      }
+      // the accumulator barrier is committed even on abort so waiters are released
+      // once whatever was issued has completed
+      mma_commit(accb);
+      (void)ok;
+    }
+  } else {
+    // converters, then the epilogue
+    const int ctid = threadIdx.x - 64;  // 0..127
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t round = kb / STAGES;
+      bool go = !*(volatile int*)abort_flag && mbar_wait(&full[s], round & 1, 3);
+      go = __all_sync(0xffffffffu, go);  // warp-uniform, the loop body syncs the warp
+      if (!go) {
+        *(volatile int*)abort_flag = 1;
+        break;
+      }
+      float* st = reinterpret_cast<float*>(smem + s * STAGE_BYTES);
+      split_tile(st, st + TILE_A / 4, TILE_A, ctid, 128);
+      split_tile(st + 2 * TILE_A / 4, st + (2 * TILE_A + TILE_B) / 4, TILE_B, ctid, 128);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+    bool ok = mbar_wait(accb, 0, 4) && !*(volatile int*)abort_flag;
+    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+      const int quarter = warp & 3;  // TMEM lanes this warp may read
+      const int row = m0 + quarter * 32 + lane;
+      const int nacc = ep.k_chunks * (ep.split_cross ? 2 : 1);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        // small (cross-term) accumulators first, then the main ones, in fp32
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((nacc - 1) * BN + c0), v);
+        for (int a = nacc - 2; a >= 0; --a) {
+          float w[32];
+          tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * BN + c0), w);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += w[j];
+        }
+        if (row < M) {
+          float* crow = C + (int64_t)row * ldc + n0 + c0;
+          const float* gate = ep.mode == 2 ? ep.gate + (ep.rows_per_group > 0 ? row / ep.rows_per_group : 0) *
+                                                           ep.gate_stride + n0 + c0
+                                           : nullptr;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = n0 + c0 + j;
+            if (col < N) {
+              float y = v[j];
+              if (ep.bias) y = __fadd_rn(y, ep.bias[col]);
+              if (ep.mode == 1) {
+                y = gelu_tanh(y);
+              } else if (ep.mode == 2) {
+                y = __fadd_rn(crow[j], __fmul_rn(gate[j], y));
+              } else if (ep.mode == 3) {
+                y = __fadd_rn(crow[j], y);
+              }
+              crow[j] = y;
+            }
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    if (*(volatile int*)abort_flag) {
+      // on abort: let every issued TMA copy land and every issued MMA finish
+      // (bounded) before the shared memory and the accumulator are released
+      if (lane == 0)
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s] >= 0) mbar_wait(&full[s], (uint32_t)issued[s] & 1, 6);
+      mbar_wait(accb, 0, 5);
+    }
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the library
+// does not link libcuda and loads on machines without a driver.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int make_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  static_assert(sizeof(CUtensorMap) == 128, "tensor map size");
+  PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  CV3_REQUIRE(encode != nullptr, CV3_ERR_CUDA, "tc_gemm: cuTensorMapEncodeTiled is unavailable");
+  CV3_REQUIRE(((uintptr_t)ptr & 15) == 0, CV3_ERR_VALUE, "tc_gemm: operand base must be 16-byte aligned");
+  CV3_REQUIRE((ld * 4) % 16 == 0, CV3_ERR_VALUE, "tc_gemm: row stride must be a multiple of 16 bytes");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)ptr, dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CV3_REQUIRE(r == CUDA_SUCCESS, CV3_ERR_CUDA, "tc_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return CV3_OK;
+}
+
+}  // namespace
+
+extern "C" int cv3_tc_gemm_cfg(const float* a, int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc,
+                               int64_t m, int64_t n, int64_t k, int mode, const float* bias, const float* gate,
+                               int64_t rows_per_group, int64_t gate_stride, int k_chunks, int split_cross,
+                               void* stream) {
+  CV3_REQUIRE(m >= 0 && n >= 0 && k >= 0 && mode >= 0 && mode <= 3, CV3_ERR_VALUE, "tc_gemm: bad arguments");
+  CV3_REQUIRE((k_chunks == 1 || k_chunks == 2 || k_chunks == 4) && (split_cross == 0 || split_cross == 1) &&
+                  k_chunks * (split_cross + 1) <= 4,
+              CV3_ERR_VALUE, "tc_gemm: accumulator layout needs k_chunks in {1,2,4} and at most 4 accumulators");
+  CV3_REQUIRE(mode != 2 || gate != nullptr, CV3_ERR_VALUE, "tc_gemm: gated residual needs a gate");
+  CV3_REQUIRE(lda >= k && ldb >= k && ldc >= n, CV3_ERR_VALUE, "tc_gemm: leading dimension too small");
+  CV3_REQUIRE(k % 4 == 0, CV3_ERR_VALUE, "tc_gemm: K must be a multiple of 4 (16-byte rows)");
+  if (m == 0 || n == 0) return CV3_OK;
+  CV3_REQUIRE(k > 0, CV3_ERR_VALUE, "tc_gemm: K must be positive");
+  CV3_REQUIRE(m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31), CV3_ERR_VALUE, "tc_gemm: too large");
+  CUtensorMap ma, mb;
+  int rc = make_map(&ma, a, m, k, lda, BM);
+  if (rc) return rc;
+  rc = make_map(&mb, b, n, k, ldb, BN);
+  if (rc) return rc;
+  rc = cv3::allow_smem((const void*)tc_gemm_kernel, SMEM_BYTES);
+  if (rc) return rc;
+  dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM));
+  CV3_REQUIRE(grid.y <= 65535, CV3_ERR_VALUE, "tc_gemm: too many row tiles");
+  const int nk = (int)((k + BK - 1) / BK);
+  if (k_chunks > nk) k_chunks = nk >= 4 ? 4 : (nk >= 2 ? 2 : 1);
+  Epi ep{k_chunks, split_cross, mode, bias, gate, rows_per_group, gate_stride};
+  tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, cv3::as_stream(stream)>>>(ma, mb, (int)m, (int)n, (int)k, c, ldc, ep);
+  return cv3::check_launch("tc_gemm");
+}
+
+extern "C" int cv3_tc_gemm(const float* a, int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc, int64_t m,
+                           int64_t n, int64_t k, int mode, const float* bias, const float* gate,
+                           int64_t rows_per_group, int64_t gate_stride, void* stream) {
+  // Two K-range accumulators for the hi*hi products and two for the hi*lo +
+  // lo*hi terms (all 512 TMEM columns): measured against fp64 this keeps the
+  // error of K = 1024 / 2048 reductions at 1.7e-6 / 3.1e-6, where a single
+  // accumulator gives 1.0e-5 / 1.7e-5 -- small addends lose bits when the
+  // tensor core adds them into a large accumulator.  Same speed.
+  return cv3_tc_gemm_cfg(a, lda, b, ldb, c, ldc, m, n, k, mode, bias, gate, rows_per_group, gate_stride, 2, 1,
+                         stream);
+}
+
+extern "C" int cv3_tc_gemm_status(int* code) {
+  int v = 0;
+  CV3_CUDA(cudaMemcpyFromSymbol(&v, g_tc_err, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    CV3_CUDA(cudaMemcpyToSymbol(g_tc_err, &zero, sizeof(int)));
+  }
+  if (code) *code = v;
+  return CV3_OK;
+}

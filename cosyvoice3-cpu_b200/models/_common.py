@@ -18,6 +18,9 @@ from ..quant import QTensor
 torch = D.torch
 
 
+TC_MIN_ROWS = 16   # below this many rows the fp32 GEMV/SIMT path is used
+
+
 class Lin:
     """A linear layer's device operands: q8 (payload, scales) or fp32 matrix, and bias."""
 
@@ -38,14 +41,31 @@ class Lin:
 
     def __call__(self, x: int, m: int, y: int, residual: int = None, ldx: int = None, ldy: int = None,
                  stream=None):
+        """y = x W^T + bias (+ residual).  fp32 weights with >= TC_MIN_ROWS rows of x run
+        on the tensor cores (3xTF32); q8 weights stream through the GEMV kernel."""
         s = stream if stream is not None else D.stream()
         ldx = self.k if ldx is None else ldx
         ldy = self.n if ldy is None else ldy
         if self.q8:
             call("cv3_q8_linear", x, m, self.k, ldx, self.w, self.scales, self.n, self.kp, self.bias,
                  residual, y, ldy, s)
+        elif m >= TC_MIN_ROWS and self.k % 4 == 0 and ldx % 4 == 0:
+            if residual is not None and residual != y:
+                raise ValueError("tensor-core linear adds the residual in place (residual must alias y)")
+            call("cv3_tc_gemm", x, ldx, self.w, self.k, y, ldy, m, self.n, self.k,
+                 3 if residual is not None else 0, self.bias, None, 0, 0, s)
         else:
             call("cv3_f32_linear", x, m, self.k, ldx, self.w, self.n, self.k, self.bias, residual, y, ldy, s)
+
+    def tc(self, x: int, m: int, y: int, mode: int, gate: int = None, rows_per_group: int = 0,
+           gate_stride: int = 0, stream=None):
+        """Tensor-core linear with a fused epilogue (0 bias, 1 GELU-tanh, 2 gated residual
+        into y, 3 residual into y); fp32 weights only."""
+        if self.q8:
+            raise ValueError("fused tensor-core epilogues need fp32 weights")
+        s = stream if stream is not None else D.stream()
+        call("cv3_tc_gemm", x, self.k, self.w, self.k, y, self.n, m, self.n, self.k, mode, self.bias, gate,
+             rows_per_group, gate_stride, s)
 
 
 def cat_rows(parts):

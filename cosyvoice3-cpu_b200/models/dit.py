@@ -21,7 +21,7 @@ import numpy as np
 from .. import _dev as D
 from .._lib import call
 from ..quant import QTensor
-from ._common import Lin, cat_rows, f32_of
+from ._common import TC_MIN_ROWS, Lin, cat_rows, f32_of
 
 torch = D.torch
 
@@ -179,6 +179,14 @@ class DiT:
             call("cv3_attention", q, N * 3 * d, hd, 3 * d, q + d * F, N * 3 * d, hd, 3 * d,
                  q + 2 * d * F, N * 3 * d, hd, 3 * d, ws.a.data_ptr(), N * d, hd, d,
                  B, H, H, N, N, hd, scale, mk, ma, mb, st)
+            if R >= TC_MIN_ROWS:
+                # tensor-core GEMMs with the gated residual / GELU fused in the epilogue
+                blk.out.tc(ws.a.data_ptr(), R, ws.h.data_ptr(), 2, g_a, rows_per_group, mw, st)
+                call("cv3_ln_modulate", ws.h.data_ptr(), R, d, 1e-6, sc_f, sh_f, rows_per_group, mw,
+                     ws.z.data_ptr(), st)
+                blk.ff1.tc(ws.z.data_ptr(), R, ws.f1.data_ptr(), 1, stream=st)
+                blk.ff2.tc(ws.f1.data_ptr(), R, ws.h.data_ptr(), 2, g_f, rows_per_group, mw, st)
+                continue
             blk.out(ws.a.data_ptr(), R, ws.y.data_ptr(), stream=st)
             call("cv3_gate_residual", ws.h.data_ptr(), ws.y.data_ptr(), g_a, R, d, rows_per_group, mw, st)
             call("cv3_ln_modulate", ws.h.data_ptr(), R, d, 1e-6, sc_f, sh_f, rows_per_group, mw, ws.z.data_ptr(), st)

@@ -158,6 +158,12 @@ def linear(x, weight: Weight, bias=None, residual=None, out=None):
     if isinstance(w, QTensor):
         call("cv3_q8_linear", D.ptr(x2), m, k, k, D.ptr(w.q), D.ptr(w.scales), n, w.padded_k,
              D.ptr(bd), D.ptr(rd), D.ptr(y), n, D.stream())
+    elif m >= 16 and k % 4 == 0:
+        # fp32 weights, enough rows: tensor cores (3xTF32, fp32-level accuracy)
+        if rd is not None:
+            y.copy_(rd.reshape(y.shape))
+        call("cv3_tc_gemm", D.ptr(x2), k, D.ptr(w), k, D.ptr(y), n, m, n, k, 3 if rd is not None else 0,
+             D.ptr(bd), None, 0, 0, D.stream())
     else:
         call("cv3_f32_linear", D.ptr(x2), m, k, k, D.ptr(w), n, k, D.ptr(bd), D.ptr(rd),
              D.ptr(y), n, D.stream())

@@ -312,6 +312,37 @@ int cv3_binary(int op, const float* a, const float* b, float scalar, int64_t n, 
 /* y[r] = [x[r][1], x[r][0..t)]: ReflectionPad1d((1, 0)); hift.py:144. */
 int cv3_reflect_left1(const float* x, int64_t rows, int64_t t, float* y, void* stream);
 
+/* ------------------------------------------------------------------ */
+/* tensor-core fp32 GEMM (tcgen05 + TMEM + TMA, 3xTF32)                 */
+/* ------------------------------------------------------------------ */
+
+#define CV3_EPI_BIAS 0          /* c = acc + bias                              */
+#define CV3_EPI_BIAS_GELU 1     /* c = gelu_tanh(acc + bias)                   */
+#define CV3_EPI_GATED_RESIDUAL 2 /* c += gate[row/rows_per_group] * (acc + bias) */
+#define CV3_EPI_RESIDUAL 3      /* c += acc + bias                             */
+
+/* c[m][n] = epilogue(sum_k a[m][k] * b[n][k]) with fp32 operands computed as
+ * 3xTF32 on the tensor cores (hi*hi + hi*lo + lo*hi, fp32 accumulation in
+ * TMEM): the fp32 linears of the DiT (cv3cpu/ops.py:121 via quant.py:165-170
+ * for plain weights), with the bias / GELU-tanh (dit.py:140) / gated
+ * residual (dit.py:170, :173) epilogues fused.  k % 4 == 0, 16-byte aligned
+ * rows; bias may be NULL. */
+int cv3_tc_gemm(const float* a, int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc, int64_t m,
+                int64_t n, int64_t k, int mode, const float* bias, const float* gate, int64_t rows_per_group,
+                int64_t gate_stride, void* stream);
+
+/* cv3_tc_gemm with an explicit accumulator layout: k_chunks (1, 2, 4)
+ * TMEM accumulators each sum a contiguous K range, split_cross = 1 keeps the
+ * hi*lo + lo*hi terms in their own accumulators; all are summed in fp32 in the
+ * epilogue (at most 4 accumulators).  cv3_tc_gemm uses 2 and 1. */
+int cv3_tc_gemm_cfg(const float* a, int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc,
+                    int64_t m, int64_t n, int64_t k, int mode, const float* bias, const float* gate,
+                    int64_t rows_per_group, int64_t gate_stride, int k_chunks, int split_cross, void* stream);
+
+/* Error word of the tensor-core kernels (0 = none; else the code of the
+ * first bounded wait that expired), read and cleared.  Synchronises. */
+int cv3_tc_gemm_status(int* code);
+
 #ifdef __cplusplus
 }
 #endif
