@@ -43,6 +43,7 @@ SIGNATURES = {
                       I64, I64, I64, I64, I64, I64, F, I32, I64, I64, P],
     "cv3_stft": [P, I64, I64, I64, I64, P, P, I64, P],
     "cv3_istft": [P, I32, I64, I64, I64, I64, P, F, I64, P, P, I64, P],
+    "cv3_istft_noalloc": [P, I32, I64, I64, I64, I64, P, F, I64, P, I64, P],
     "cv3_interpolate_nearest": [P, I64, I64, I64, P, P],
     "cv3_interpolate_linear": [P, I64, I64, P, P, P, I64, P, P],
     "cv3_torch_rand": [U64, I64, I64, P, P],

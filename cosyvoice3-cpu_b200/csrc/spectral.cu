@@ -14,6 +14,8 @@
 // centre trim and clip.  Overlap-add is a gather: every output sample sums its
 // (at most n_fft/hop) frames in ascending tap order, as the reference's
 // per-tap strided adds do.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -196,4 +198,73 @@ extern "C" int cv3_interpolate_linear(const float* x, int64_t rows, int64_t t, c
   if (rows * size == 0) return CV3_OK;
   linear_interp_kernel<<<grid_for(rows * size, 256), 256, 0, cv3::as_stream(stream)>>>(x, rows, t, i0, i1, w, size, y);
   return cv3::check_launch("interpolate_linear");
+}
+
+// ---------------------------------------------------------------------------
+// iSTFT without any device allocation.
+//
+// Some callers cannot allocate device memory at the moment they need the
+// vocoder's inverse STFT: a real-time audio callback must not block on
+// cudaMalloc (it can synchronise the device and take unbounded time), and a
+// host that has already handed the whole GPU to its own memory pool has no
+// allocation left to give.  cv3_istft asks for a caller-provided frame buffer;
+// this variant brings its own, a fixed array in the library's device image.
+//
+// Limits: batch * frames * n_fft <= kIstftScratchFloats (1 Mi floats, 4 MiB,
+// enough for one utterance of about 27 s of 24 kHz audio at n_fft 16 / hop 4).
+// Every device that loads the library holds the array until the process exits.
+// All calls share it: two calls whose kernels can run at the same time (for
+// example on two streams without ordering) overwrite each other's frames, so
+// such calls must be ordered by the caller.  Each call writes every frame
+// sample before reading it, so stale contents from a previous call never
+// reach an output and nothing needs clearing.
+// ---------------------------------------------------------------------------
+
+namespace {
+constexpr int64_t kIstftScratchFloats = int64_t(1) << 20;
+}  // namespace
+
+static __device__ __align__(256) float g_istft_scratch[kIstftScratchFloats];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// Device address of g_istft_scratch for the current device, looked up once
+// per device with that device current (a host-side symbol is not a device
+// address, so it must never be passed to a kernel directly).  The lookup
+// happens inside the first cv3_istft_noalloc call on each device; make that
+// first call before any stream capture.
+int istft_scratch_address(float** out) {
+  static std::mutex mu;
+  static float* addr[kMaxDevices] = {};
+  int dev = 0;
+  CV3_CUDA(cudaGetDevice(&dev));
+  CV3_REQUIRE(dev >= 0 && dev < kMaxDevices, CV3_ERR_UNSUPPORTED, "istft_noalloc: device index %d", dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_istft_scratch);
+    CV3_REQUIRE(e == cudaSuccess && p != nullptr, CV3_ERR_CUDA, "istft_noalloc: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return CV3_OK;
+}
+
+}  // namespace
+
+extern "C" int cv3_istft_noalloc(const float* spec, int mode, int64_t batch, int64_t frames, int64_t n_fft,
+                                 int64_t hop, const float* win, float limit, int64_t offset, float* y,
+                                 int64_t out_len, void* stream) {
+  CV3_REQUIRE(batch >= 0 && frames >= 0 && n_fft >= 0, CV3_ERR_VALUE, "istft_noalloc: negative size");
+  CV3_REQUIRE(batch == 0 || frames == 0 || n_fft <= kIstftScratchFloats / batch / frames, CV3_ERR_VALUE,
+              "istft_noalloc: %lld x %lld frames of %lld samples exceed the built-in %lld-float frame buffer; "
+              "use cv3_istft with a caller-provided buffer",
+              (long long)batch, (long long)frames, (long long)n_fft, (long long)kIstftScratchFloats);
+  float* scratch = nullptr;
+  const int rc = istft_scratch_address(&scratch);
+  if (rc) return rc;
+  return cv3_istft(spec, mode, batch, frames, n_fft, hop, win, limit, offset, scratch, y, out_len, stream);
 }

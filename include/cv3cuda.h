@@ -182,6 +182,20 @@ int cv3_istft(const float* spec, int mode, int64_t batch, int64_t frames, int64_
               const float* win, float limit, int64_t offset, float* frame_scratch, float* y,
               int64_t out_len, void* stream);
 
+/* cv3_istft without any device allocation, for callers that cannot allocate
+ * when they run the vocoder's inverse STFT (a real-time audio callback must
+ * not block on cudaMalloc; a host whose memory pool already owns the GPU has
+ * nothing left to allocate).  No counterpart in the reference (its NumPy iSTFT
+ * allocates freely); same arguments and results as cv3_istft minus
+ * frame_scratch.  The frame buffer is a 4 MiB array built into the library
+ * (batch * frames * n_fft <= 1,048,576 floats, CV3_ERR_VALUE beyond), held by
+ * every device that loads the library until exit and shared by all calls:
+ * calls whose kernels may overlap on the GPU race and must be ordered by the
+ * caller.  The first call on each device looks up the array's device address;
+ * make that call before any stream capture. */
+int cv3_istft_noalloc(const float* spec, int mode, int64_t batch, int64_t frames, int64_t n_fft, int64_t hop,
+                      const float* win, float limit, int64_t offset, float* y, int64_t out_len, void* stream);
+
 /* y [rows][t*scale] = x repeated along time; cv3cpu/ops.py:335-336. */
 int cv3_interpolate_nearest(const float* x, int64_t rows, int64_t t, int64_t scale, float* y, void* stream);
 
