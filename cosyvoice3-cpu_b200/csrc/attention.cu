@@ -63,30 +63,48 @@ attn_full_kernel(AttnArgs a) {
   float mrun = -INFINITY, lrun = 0.f;
   const float* kb = a.k + b * a.ksb + hk * a.ksh;
   const float* vb = a.v + b * a.vsb + hk * a.vsh;
-  for (int j0 = 0; j0 < a.m; j0 += KT) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < KT * DMAX; i += QT) {
-      const int r = i / DMAX, c = i - r * DMAX;
+  // K/V tiles are fetched one tile ahead into registers (float4, all loads of a
+  // tile in flight together) so their latency overlaps the current tile's math.
+  constexpr int F4 = KT * DMAX / 4 / QT;  // float4 of K (and of V) per thread per tile
+  float4 kpre[F4], vpre[F4];
+  auto fetch = [&](int j0) {
+#pragma unroll
+    for (int u = 0; u < F4; ++u) {
+      const int f = threadIdx.x + u * QT;
+      const int r = f / (DMAX / 4), c = (f % (DMAX / 4)) * 4;
       const int j = j0 + r;
       const bool ok = j < a.m && c < a.d;
-      reinterpret_cast<float*>(Ks)[i] = ok ? kb[(int64_t)j * a.ksn + c] : 0.f;
-      reinterpret_cast<float*>(Vs)[i] = ok ? vb[(int64_t)j * a.vsn + c] : 0.f;
+      kpre[u] = ok ? *reinterpret_cast<const float4*>(kb + (int64_t)j * a.ksn + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      vpre[u] = ok ? *reinterpret_cast<const float4*>(vb + (int64_t)j * a.vsn + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  fetch(0);
+  for (int j0 = 0; j0 < a.m; j0 += KT) {
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < F4; ++u) {
+      const int f = threadIdx.x + u * QT;
+      Ks[f / (DMAX / 4)][f % (DMAX / 4)] = kpre[u];
+      Vs[f / (DMAX / 4)][f % (DMAX / 4)] = vpre[u];
     }
     __syncthreads();
+    if (j0 + KT < a.m) fetch(j0 + KT);
     float tmax = -INFINITY;
     for (int r = 0; r < KT; ++r) {
       const int j = j0 + r;
       float s = -INFINITY;
       if (j < a.m && allowed(a, qi, j)) {
-        s = 0.f;
+        // four independent partial sums: the dot product is a 16-deep chain, not 64
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
         for (int d4 = 0; d4 < DMAX / 4; ++d4) {
           const float4 kv = Ks[r][d4];
-          s = fmaf(qv[4 * d4], kv.x, s);
-          s = fmaf(qv[4 * d4 + 1], kv.y, s);
-          s = fmaf(qv[4 * d4 + 2], kv.z, s);
-          s = fmaf(qv[4 * d4 + 3], kv.w, s);
+          s0 = fmaf(qv[4 * d4], kv.x, s0);
+          s1 = fmaf(qv[4 * d4 + 1], kv.y, s1);
+          s2 = fmaf(qv[4 * d4 + 2], kv.z, s2);
+          s3 = fmaf(qv[4 * d4 + 3], kv.w, s3);
         }
+        s = (s0 + s1) + (s2 + s3);
       }
       S[r][threadIdx.x] = s;
       tmax = fmaxf(tmax, s);
@@ -181,6 +199,9 @@ extern "C" int cv3_attention(const float* q, int64_t qsb, int64_t qsh, int64_t q
   CV3_REQUIRE(heads % kv_heads == 0, CV3_ERR_VALUE, "%lld query heads is not a multiple of %lld kv heads",
               (long long)heads, (long long)kv_heads);
   CV3_REQUIRE(d >= 1 && d <= DMAX, CV3_ERR_UNSUPPORTED, "attention: head dim %lld > %d not built", (long long)d, DMAX);
+  CV3_REQUIRE(d % 4 == 0 && ksn % 4 == 0 && vsn % 4 == 0 && ksh % 4 == 0 && vsh % 4 == 0 && ksb % 4 == 0 &&
+                  vsb % 4 == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0,
+              CV3_ERR_UNSUPPORTED, "attention: head dim, key/value strides and bases must be 16-byte multiples");
   CV3_REQUIRE(mask_kind >= 0 && mask_kind <= 2, CV3_ERR_VALUE, "attention: unknown mask kind %d", mask_kind);
   CV3_REQUIRE(mask_kind != 2 || mask_a > 0, CV3_ERR_VALUE, "attention: chunk size must be positive");
   if (batch == 0 || n == 0) return CV3_OK;

@@ -44,57 +44,97 @@ __global__ void rope_qkv_append_kernel(const float* __restrict__ qkv, int64_t ld
 
 constexpr int AT = 256;
 constexpr int DM = 64;
+constexpr int HPG = 8;     // most query heads sharing one kv head (Qwen2-0.5B: 7)
+constexpr int PG = 16;     // key groups of the V pass (16 groups x 16 lanes x float4)
 
-// One CTA per (query head, sequence): scores of all visible keys in shared
-// memory, block max / exp / sum, then a coalesced V pass.
+// One CTA per (sequence, kv head): every query head of the group reads each
+// cached key/value row once.  Scores: one key per thread (its 256-byte row as
+// 16 independent float4 loads) against all heads of the group.  Softmax: one
+// warp per head.  V pass: 16 key groups x 16 lanes of float4 dims, per-group
+// partial sums reduced in a fixed order.  Same arithmetic as ops.sdpa with no
+// mask (cv3cpu/ops.py:284-300): scores of the scaled query, exp(s - max), sum,
+// then P.V / sum.
 __global__ void __launch_bounds__(AT)
 decode_attention_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                        const int* __restrict__ lens, int heads, int kv_heads, int d, int64_t cap, float scale,
+                        const int* __restrict__ lens, int heads, int kv_heads, int64_t cap, float scale,
                         float* __restrict__ out) {
-  extern __shared__ float sm[];  // [cap] scores, then 4*DM partials
-  __shared__ float qs[DM];
-  __shared__ float red[32];
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int hk = h / (heads / kv_heads);
-  const int m = min((int64_t)lens[b], cap);
-  if (threadIdx.x < DM) qs[threadIdx.x] = threadIdx.x < d ? q[((int64_t)b * heads + h) * d + threadIdx.x] * scale : 0.f;
-  __syncthreads();
-  const float* kb = kc + ((int64_t)b * kv_heads + hk) * cap * d;
-  const float* vb = vc + ((int64_t)b * kv_heads + hk) * cap * d;
-  float lmax = -INFINITY;
-  for (int j = threadIdx.x; j < m; j += AT) {
-    const float4* kr = reinterpret_cast<const float4*>(kb + (int64_t)j * d);
-    float s = 0.f;
-    for (int t = 0; t < d / 4; ++t) {
-      const float4 kv = kr[t];
-      s = fmaf(qs[4 * t], kv.x, s);
-      s = fmaf(qs[4 * t + 1], kv.y, s);
-      s = fmaf(qs[4 * t + 2], kv.z, s);
-      s = fmaf(qs[4 * t + 3], kv.w, s);
-    }
-    sm[j] = s;
-    lmax = fmaxf(lmax, s);
+  extern __shared__ float sc[];  // [hpg][cap] scores, then probabilities
+  __shared__ float4 qs[HPG][DM / 4];
+  __shared__ float4 part[PG][HPG][DM / 4];
+  __shared__ float stat[HPG][2];
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int hpg = heads / kv_heads;
+  const int m = (int)min((int64_t)lens[b], cap);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < hpg * (DM / 4); i += AT) {
+    const int h = i / (DM / 4), c = i - h * (DM / 4);
+    float4 v = reinterpret_cast<const float4*>(q + ((int64_t)b * heads + g * hpg + h) * DM)[c];
+    v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
+    qs[h][c] = v;
   }
-  const float mx = block_max(lmax, red);
-  float lsum = 0.f;
-  for (int j = threadIdx.x; j < m; j += AT) {
-    const float p = expf(sm[j] - mx);
-    sm[j] = p;
-    lsum += p;
-  }
-  const float sum = block_sum(lsum, red);
-  float* part = sm + cap;
-  const int e = threadIdx.x % DM, grp = threadIdx.x / DM;
-  float acc = 0.f;
-  if (e < d)
-    for (int j = grp; j < m; j += AT / DM) acc = fmaf(sm[j], vb[(int64_t)j * d + e], acc);
-  part[grp * DM + e] = acc;
   __syncthreads();
-  if (threadIdx.x < d) {
-    float o = 0.f;
+  const float* kb = kc + ((int64_t)b * kv_heads + g) * cap * DM;
+  const float* vb = vc + ((int64_t)b * kv_heads + g) * cap * DM;
+  for (int j = tid; j < m; j += AT) {
+    float4 kr[DM / 4];
+    const float4* src = reinterpret_cast<const float4*>(kb + (int64_t)j * DM);
 #pragma unroll
-    for (int g = 0; g < AT / DM; ++g) o += part[g * DM + threadIdx.x];
-    out[(int64_t)b * heads * d + (int64_t)h * d + threadIdx.x] = o / sum;
+    for (int c = 0; c < DM / 4; ++c) kr[c] = src[c];
+    for (int h = 0; h < hpg; ++h) {
+      float s = 0.f;
+#pragma unroll
+      for (int c = 0; c < DM / 4; ++c) {
+        const float4 qq = qs[h][c];
+        s = fmaf(qq.x, kr[c].x, s);
+        s = fmaf(qq.y, kr[c].y, s);
+        s = fmaf(qq.z, kr[c].z, s);
+        s = fmaf(qq.w, kr[c].w, s);
+      }
+      sc[h * cap + j] = s;
+    }
+  }
+  __syncthreads();
+  if (warp < hpg) {
+    float* row = sc + warp * cap;
+    float mx = -INFINITY;
+    for (int j = lane; j < m; j += 32) mx = fmaxf(mx, row[j]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int j = lane; j < m; j += 32) {
+      const float p = expf(row[j] - mx);
+      row[j] = p;
+      sum += p;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) stat[warp][0] = sum;
+  }
+  __syncthreads();
+  const int grp = tid / (DM / 4), l = tid % (DM / 4);
+  float4 acc[HPG];
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = grp; j < m; j += PG) {
+    const float4 v = reinterpret_cast<const float4*>(vb + (int64_t)j * DM)[l];
+#pragma unroll
+    for (int h = 0; h < HPG; ++h) {
+      if (h < hpg) {
+        const float p = sc[h * cap + j];
+        acc[h].x = fmaf(p, v.x, acc[h].x);
+        acc[h].y = fmaf(p, v.y, acc[h].y);
+        acc[h].z = fmaf(p, v.z, acc[h].z);
+        acc[h].w = fmaf(p, v.w, acc[h].w);
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h)
+    if (h < hpg) part[grp][h][l] = acc[h];
+  __syncthreads();
+  for (int i = tid; i < hpg * DM; i += AT) {
+    const int h = i / DM, e = i - h * DM;
+    float o = 0.f;
+    for (int p = 0; p < PG; ++p) o += reinterpret_cast<const float*>(&part[p][h][0])[e];
+    out[(int64_t)b * heads * DM + (int64_t)(g * hpg + h) * DM + e] = o / stat[h][0];
   }
 }
 
@@ -182,18 +222,19 @@ extern "C" int cv3_decode_attention(const float* q, const float* k_cache, const 
                                     float scale, float* out, void* stream) {
   CV3_REQUIRE(batch >= 0 && heads > 0 && kv_heads > 0 && heads % kv_heads == 0, CV3_ERR_VALUE,
               "%lld query heads is not a multiple of %lld kv heads", (long long)heads, (long long)kv_heads);
-  CV3_REQUIRE(head_dim % 4 == 0 && head_dim <= DM, CV3_ERR_UNSUPPORTED, "decode_attention: head_dim %lld",
-              (long long)head_dim);
-  CV3_REQUIRE(cap > 0 && (cap + 4 * DM) * 4 <= 200 * 1024, CV3_ERR_UNSUPPORTED, "decode_attention: cap too large");
+  CV3_REQUIRE(head_dim == DM, CV3_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (built for %d)",
+              (long long)head_dim, DM);
+  CV3_REQUIRE(heads / kv_heads <= HPG, CV3_ERR_UNSUPPORTED, "decode_attention: more than %d heads per kv head", HPG);
+  const int64_t smem = (heads / kv_heads) * cap * 4;
+  CV3_REQUIRE(cap > 0 && smem <= 150 * 1024, CV3_ERR_UNSUPPORTED, "decode_attention: cap too large");
+  CV3_REQUIRE(((uintptr_t)q & 15) == 0 && ((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0,
+              CV3_ERR_VALUE, "decode_attention: 16-byte aligned tensors required");
   if (batch == 0) return CV3_OK;
-  const int smem = (int)((cap + 4 * DM) * 4);
-  if (smem > 48 * 1024) {
-    int rc = cv3::allow_smem((const void*)decode_attention_kernel, smem);
-    if (rc) return rc;
-  }
-  dim3 grid((unsigned)heads, (unsigned)batch);
-  decode_attention_kernel<<<grid, AT, smem, cv3::as_stream(stream)>>>(q, k_cache, v_cache, lens, (int)heads,
-                                                                       (int)kv_heads, (int)head_dim, cap, scale, out);
+  int rc = cv3::allow_smem((const void*)decode_attention_kernel, (int)smem);
+  if (rc) return rc;
+  dim3 grid((unsigned)kv_heads, (unsigned)batch);
+  decode_attention_kernel<<<grid, AT, (size_t)smem, cv3::as_stream(stream)>>>(q, k_cache, v_cache, lens, (int)heads,
+                                                                               (int)kv_heads, cap, scale, out);
   return cv3::check_launch("decode_attention");
 }
 

@@ -68,6 +68,51 @@ class Lin:
              rows_per_group, gate_stride, s)
 
 
+class DecodeGemv:
+    """A q8 weight streamed by ``cv3_q8_decode_gemv`` for <= 8 activation rows.
+
+    Small matrices split K over several CTAs so every SM streams part of the
+    weight; the split needs a private partial-sum workspace and per-row-tile
+    counters (zero, and left zero by the kernel), allocated here once.
+    ``norm_w`` fuses an RMSNorm of x; ``swiglu`` expects rows interleaved
+    gate/up and writes ``silu(gate) * up``.
+    """
+
+    def __init__(self, w: QTensor, bias=None, norm_w=None, eps: float = 1e-6, swiglu: bool = False,
+                 target_ctas: int = 296):
+        self._keep = [w, bias, norm_w]
+        self.n, self.k, self.kp = int(w.shape[0]), int(w.shape[1]), w.padded_k
+        self.q, self.scales = w.q.data_ptr(), w.scales.data_ptr()
+        self.bias = bias.data_ptr() if bias is not None else None
+        self.norm = norm_w.data_ptr() if norm_w is not None else None
+        self.eps = float(eps)
+        self.swiglu = 1 if swiglu else 0
+        tiles = -(-self.n // 32)
+        self.splits = max(1, min(64, -(-target_ctas // tiles), self.kp // 64))
+        kps = -(-(self.kp // self.splits) // 16) * 16
+        eff = -(-self.kp // kps)
+        self.ws = D.empty((eff * 8 * self.n,)) if eff > 1 else None
+        self.cnt = torch.zeros(tiles, dtype=torch.int32, device="cuda") if eff > 1 else None
+
+    def __call__(self, x: int, m: int, y: int, residual: int = None, ldx: int = None, ldy: int = None,
+                 stream=None):
+        s = stream if stream is not None else D.stream()
+        ldx = self.k if ldx is None else ldx
+        ldy = (self.n // 2 if self.swiglu else self.n) if ldy is None else ldy
+        call("cv3_q8_decode_gemv", x, m, self.k, ldx, self.q, self.scales, self.n, self.kp, self.bias, residual,
+             self.norm, self.eps, self.swiglu, y, ldy, self.splits,
+             self.ws.data_ptr() if self.ws is not None else None, self.ws.numel() if self.ws is not None else 0,
+             self.cnt.data_ptr() if self.cnt is not None else None, s)
+
+
+def interleave_rows(a: QTensor, b: QTensor) -> QTensor:
+    """q8 rows a_0, b_0, a_1, b_1, ... (the SwiGLU pairing of cv3_q8_decode_gemv)."""
+    n, kp = int(a.q.shape[0]), int(a.q.shape[1])
+    q = torch.stack([a.q, b.q], dim=1).reshape(2 * n, kp).contiguous()
+    s = torch.stack([a.scales, b.scales], dim=1).reshape(2 * n, -1).contiguous()
+    return QTensor("q8", q, s, (2 * n, int(a.shape[1])), a.block, None)
+
+
 def cat_rows(parts):
     """Stack weights along the output dimension (q8 payload + scales, or fp32)."""
     if all(isinstance(p, QTensor) for p in parts):

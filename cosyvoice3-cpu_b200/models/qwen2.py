@@ -23,7 +23,7 @@ import numpy as np
 from .. import _dev as D
 from .._lib import call
 from ..quant import QTensor
-from ._common import Graph, Lin, cat_rows, f32_of
+from ._common import DecodeGemv, Graph, Lin, cat_rows, f32_of, interleave_rows
 
 torch = D.torch
 
@@ -237,6 +237,22 @@ class DecodeEngine:
         self.scale = float(np.float32(1.0 / np.sqrt(hd)))
         self.graph = None
         self.keep_logp = False
+        # fused q8 decode GEMVs (RMSNorm in, residual / SwiGLU out) where the layer is q8
+        self.fast = []
+        for i, L in enumerate(model.layers()):
+            p = f"layers.{i}."
+            ws = [L.qkv._keep[0], L.o._keep[0], model._t(p + "mlp.gate_proj.weight"),
+                  model._t(p + "mlp.up_proj.weight"), L.down._keep[0]]
+            if all(isinstance(w, QTensor) for w in ws):
+                gu = model.w.cache((model.prefix + p + "gate_up_interleaved",), lambda ws=ws: interleave_rows(ws[2], ws[3]))
+                self.fast.append((DecodeGemv(ws[0], L.qkv._keep[1], L.ln1, c.rms_norm_eps),
+                                  DecodeGemv(ws[1]),
+                                  DecodeGemv(gu, norm_w=L.ln2, eps=c.rms_norm_eps, swiglu=True),
+                                  DecodeGemv(ws[4])))
+            else:
+                self.fast.append(None)
+        self.fast_head = DecodeGemv(head_w, norm_w=model.norm_w(), eps=c.rms_norm_eps) \
+            if isinstance(head_w, QTensor) else None
 
     def launches(self, st):
         """One decode step for every sequence (all pointers fixed -> graph-capturable)."""
@@ -244,6 +260,18 @@ class DecodeEngine:
         H, Hk, hd, hid = c.num_attention_heads, c.num_key_value_heads, c.head_dim, c.hidden_size
         for i, L in enumerate(self.m.layers()):
             kc, vc = self.cache.layer_ptrs(i)
+            F = self.fast[i]
+            if F is not None:
+                F[0](self.h.data_ptr(), B, self.qkv.data_ptr(), stream=st)
+                call("cv3_rope_qkv_append", self.qkv.data_ptr(), B, self.qkv.shape[1], self.cos.data_ptr(),
+                     self.sin.data_ptr(), self.seqs.data_ptr(), self.pos.data_ptr(), H, Hk, hd, self.q.data_ptr(),
+                     kc, vc, self.cap, st)
+                call("cv3_decode_attention", self.q.data_ptr(), kc, vc, self.lens.data_ptr(), B, H, Hk, hd,
+                     self.cap, self.scale, self.a.data_ptr(), st)
+                F[1](self.a.data_ptr(), B, self.h.data_ptr(), residual=self.h.data_ptr(), stream=st)
+                F[2](self.h.data_ptr(), B, self.act.data_ptr(), stream=st)
+                F[3](self.act.data_ptr(), B, self.h.data_ptr(), residual=self.h.data_ptr(), stream=st)
+                continue
             call("cv3_rms_norm", self.h.data_ptr(), L.ln1.data_ptr(), B, hid, c.rms_norm_eps, self.n.data_ptr(), st)
             L.qkv(self.n.data_ptr(), B, self.qkv.data_ptr(), stream=st)
             call("cv3_rope_qkv_append", self.qkv.data_ptr(), B, self.qkv.shape[1], self.cos.data_ptr(),
@@ -256,12 +284,17 @@ class DecodeEngine:
             L.gu(self.n.data_ptr(), B, self.gu.data_ptr(), stream=st)
             call("cv3_swiglu", self.gu.data_ptr(), B, c.intermediate_size, self.act.data_ptr(), st)
             L.down(self.act.data_ptr(), B, self.h.data_ptr(), residual=self.h.data_ptr(), stream=st)
+        if self.fast_head is not None and B <= 8:
+            self.fast_head(self.h.data_ptr(), B, self.logits.data_ptr(), stream=st)
+            self.select_and_feed(st, logits_ready=True)
+            return
         call("cv3_rms_norm", self.h.data_ptr(), self.m.norm_w().data_ptr(), B, hid, c.rms_norm_eps,
              self.n.data_ptr(), st)
         self.select_and_feed(st)
 
-    def select_and_feed(self, st):
-        self.head(self.n.data_ptr(), self.B, self.logits.data_ptr(), stream=st)
+    def select_and_feed(self, st, logits_ready: bool = False):
+        if not logits_ready:
+            self.head(self.n.data_ptr(), self.B, self.logits.data_ptr(), stream=st)
         call("cv3_head_select", self.logits.data_ptr(), self.B, self.vocab, self.select,
              self.logp.data_ptr() if self.keep_logp else None, self.next_ids.data_ptr(), self.pos.data_ptr(),
              self.lens.data_ptr(), self.history.data_ptr(), self.max_steps, self.step_no.data_ptr(), st)

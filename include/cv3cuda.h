@@ -71,6 +71,21 @@ int cv3_q8_linear(const float* x, int64_t m, int64_t k, int64_t ldx,
                   const float* bias, const float* residual,
                   float* y, int64_t ldy, void* stream);
 
+/* Decode-step q8 GEMV for 1..8 activation rows with the Qwen2 layer's
+ * fusions: y = epi(norm(x) . W^T + bias) where norm is RMSNorm with weight
+ * norm_w (NULL: none; cv3cpu/ops.py:101-104), epi adds residual (y may alias
+ * it) or, with swiglu = 1 and weight rows interleaved gate/up, writes
+ * y[m][i] = silu(row 2i) * row 2i+1 (qwen2.py:175-177).  `splits` > 1 splits K
+ * over CTAs: then workspace must hold splits*8*n floats and counters n/32 ints,
+ * zero on the first call and left zero by every call (per-weight buffers; do
+ * not share them between concurrent calls).  Replaces the per-token
+ * ops.linear calls of qwen2.py:156-177 and llm.py:74-78. */
+int cv3_q8_decode_gemv(const float* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
+                       const uint16_t* scales, int64_t n, int64_t kp, const float* bias,
+                       const float* residual, const float* norm_w, float eps, int swiglu, float* y,
+                       int64_t ldy, int64_t splits, float* workspace, int64_t workspace_floats,
+                       int* counters, void* stream);
+
 /* Same contract for an fp32 weight W[n][k] (row stride ldw); replaces the
  * plain-array branch of cv3cpu/quant.py:165-170. fp32-exact SIMT math. */
 int cv3_f32_linear(const float* x, int64_t m, int64_t k, int64_t ldx,

@@ -1,0 +1,90 @@
+"""The fused decode GEMV (cv3_q8_decode_gemv) and the decode engine's fused path.
+
+Kernel vs the oracle: RMSNorm-fused input, bias, residual, SwiGLU row pairs,
+K split over CTAs (deterministic reduction), 1..8 rows; tolerance 1e-5 (the
+int8 dequantisation is exact).  Engine: a small LM whose every linear is q8,
+so the fused path runs, against the oracle's greedy decode.
+"""
+
+import numpy as np
+import pytest
+
+from conftest import pkg, rel_err
+
+import oracle.numerics as nx
+import oracle.stages as st
+
+pytestmark = pytest.mark.gpu
+
+
+def _dg(qt, **kw):
+    return pkg("models._common").DecodeGemv(qt.to_device(), **kw)
+
+
+@pytest.mark.parametrize("n,k", [(1152, 896), (896, 896), (896, 4864), (9728, 896), (6761, 896), (96, 100)])
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_decode_gemv_plain_and_residual(n, k, m):
+    import torch
+    rng = np.random.default_rng(n + k + m)
+    w = (rng.normal(size=(n, k)) * 0.02).astype(np.float32)
+    qt = pkg("quant").make_qtensor(w)
+    oq = nx.QTensor("q8", qt.q, qt.scales, qt.shape, 64)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    b = rng.normal(size=n).astype(np.float32)
+    r = rng.normal(size=(m, n)).astype(np.float32)
+    g = _dg(qt, bias=torch.from_numpy(b).cuda())
+    xd, y = torch.from_numpy(x).cuda(), torch.from_numpy(r).cuda()
+    for _ in range(2):                       # twice: the split counters must be left at zero
+        y.copy_(torch.from_numpy(r))
+        g(xd.data_ptr(), m, y.data_ptr(), residual=y.data_ptr())
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), nx.qmatmul(x, oq, b) + r) < 1e-5
+
+
+@pytest.mark.parametrize("m", [1, 5, 8])
+def test_decode_gemv_fused_norm_and_swiglu(m):
+    import torch
+    C = pkg("models._common")
+    rng = np.random.default_rng(m)
+    k, inter = 896, 4864
+    gate = (rng.normal(size=(inter, k)) * 0.02).astype(np.float32)
+    up = (rng.normal(size=(inter, k)) * 0.02).astype(np.float32)
+    qg, qu = pkg("quant").make_qtensor(gate), pkg("quant").make_qtensor(up)
+    nw = (1 + 0.1 * rng.normal(size=k)).astype(np.float32)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    n = nx.rms_norm(x, nw, 1e-6)
+    og = nx.qmatmul(n, nx.QTensor("q8", qg.q, qg.scales, qg.shape, 64))
+    ou = nx.qmatmul(n, nx.QTensor("q8", qu.q, qu.scales, qu.shape, 64))
+    ref = nx.silu(og) * ou
+    inter_q = C.interleave_rows(qg.to_device(), qu.to_device())
+    g = C.DecodeGemv(inter_q, norm_w=torch.from_numpy(nw).cuda(), eps=1e-6, swiglu=True)
+    y = torch.empty(m, inter, device="cuda")
+    g(torch.from_numpy(x).cuda().data_ptr(), m, y.data_ptr())
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), ref) < 1e-5
+
+
+def test_engine_fused_path_matches_oracle(small_weights):
+    """Small LM with every linear quantised: the engine takes the fused path."""
+    W0 = small_weights["f32"]
+    Q = pkg("quant")
+    tensors = dict(W0)
+    for name, t in W0.items():
+        if name.startswith("llm.") and ("proj.weight" in name or "llm_decoder.weight" in name):
+            tensors[name] = Q.make_qtensor(t)
+    W = pkg("weights").TensorDict(tensors, W0.meta)
+    lm = pkg("models.llm").CosyVoice3LM(pkg("weights").DeviceWeights(W))
+    olm = st.SpeechLM(W, W.meta)
+    rng = np.random.default_rng(9)
+    eop = W.meta["endofprompt_id"]
+    prompts, oprompts = [], []
+    for nn in (6, 11):
+        text = [eop] + rng.integers(0, 2000, size=nn).tolist()
+        prompts.append(lm.prompt_embedding(text, (), [1, 2, 3]))
+        oprompts.append(olm.prompt_embedding(text, (), [1, 2, 3]))
+    toks = lm.generate_greedy(prompts, 16).cpu().numpy()
+    eng = lm.last_engine
+    assert all(f is not None for f in eng.fast) and eng.fast_head is not None
+    for b in range(2):
+        ref, _ = olm.generate_greedy(oprompts[b], 16)
+        assert toks[b].tolist() == ref
