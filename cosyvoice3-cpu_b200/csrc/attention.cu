@@ -11,7 +11,7 @@
 //  * decode (<= 4 queries): one CTA per (batch, head, query); scores of all
 //    keys in shared memory, then block max, exp, sum and a V pass with
 //    coalesced rows.
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace {
 
@@ -43,6 +43,7 @@ constexpr int QT = 128;  // queries per CTA (one per thread)
 constexpr int KT = 32;   // keys per tile
 constexpr int DMAX = 64;
 
+template <bool VEC>
 __global__ void __launch_bounds__(QT)
 attn_full_kernel(AttnArgs a) {
   __shared__ float4 Ks[KT][DMAX / 4];
@@ -74,8 +75,19 @@ attn_full_kernel(AttnArgs a) {
       const int r = f / (DMAX / 4), c = (f % (DMAX / 4)) * 4;
       const int j = j0 + r;
       const bool ok = j < a.m && c < a.d;
-      kpre[u] = ok ? *reinterpret_cast<const float4*>(kb + (int64_t)j * a.ksn + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      vpre[u] = ok ? *reinterpret_cast<const float4*>(vb + (int64_t)j * a.vsn + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      kpre[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      vpre[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ok && VEC) {
+        kpre[u] = *reinterpret_cast<const float4*>(kb + (int64_t)j * a.ksn + c);
+        vpre[u] = *reinterpret_cast<const float4*>(vb + (int64_t)j * a.vsn + c);
+      } else if (ok) {
+        float* kp = reinterpret_cast<float*>(&kpre[u]);
+        float* vp = reinterpret_cast<float*>(&vpre[u]);
+        for (int e = 0; e < 4 && c + e < a.d; ++e) {
+          kp[e] = kb[(int64_t)j * a.ksn + c + e];
+          vp[e] = vb[(int64_t)j * a.vsn + c + e];
+        }
+      }
     }
   };
   fetch(0);
@@ -187,6 +199,424 @@ attn_decode_kernel(AttnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core path for head dim 64: flash-attention tiling on tcgen05, 3xTF32.
+//
+// CTA = one (batch, head) and 128 queries; keys in 64-key tiles through a
+// 3-stage TMA ring (K and V read in place through 4-D tensor maps over the
+// strided layout).  10 warps:
+//   warp 0     TMA producer (K and V tiles, SWIZZLE_128B);
+//   warp 1     MMA issuer: S_t = Q.K_t^T into TMEM, O_t = P_t.V_t into TMEM,
+//              both as hi*lo + lo*hi + hi*hi tf32 products (fp32-accurate);
+//   warps 2-5  softmax: one query row per thread (TMEM lane), online max / sum
+//              in fp32, P_t split into tf32 hi/lo written back to TMEM, and
+//              the per-tile O_t folded into a register accumulator;
+//   warps 6-9  split the scaled Q rows into TMEM once, then every landed K
+//              tile in place into hi/lo shared-memory buffers and every V
+//              tile, transposed, the same way.
+// TMEM columns: Q hi | Q lo | S/P-hi x2 | P-lo x2 | O x2 (512).  Q and P are
+// the A operands straight from TMEM; K and the transposed V are K-major B
+// operands in shared memory.  S for tile t+2 is issued behind O for tile t, so the
+// tensor pipe works while the softmax warps do.  Every wait is bounded; on a
+// timeout the CTA records an error (cv3_tc_attention_status), drains what it
+// issued and exits.
+// ---------------------------------------------------------------------------
+namespace tc {
+
+using namespace cv3tc;
+
+constexpr int BQ = 128, BKV = 64, HD = 64, STAGES = 3;
+constexpr int HALF = BKV * 32 * 4;  // 8 KB: 64 keys x 32 floats (one TMA box, 128-byte rows)
+constexpr int TILE = 2 * HALF;      // 16 KB: 64 keys x 64 floats
+constexpr int STAGE = 4 * TILE;     // K hi | K lo | V hi | V lo
+constexpr int THREADS = 320;
+constexpr uint32_t C_QHI = 0, C_QLO = 64, C_S = 128, C_PLO = 256, C_O = 384;
+constexpr uint32_t ID_S = idesc_tf32(BQ, BKV);
+constexpr uint32_t ID_PV = idesc_tf32(BQ, HD);
+
+// byte offset of element (row, col) of a [rows][64] fp32 tile held as two
+// 32-column TMA boxes of [rows][128 B] with the 128-byte swizzle (16-byte
+// chunks XOR row % 8); boxes HALF bytes apart
+__device__ __forceinline__ uint32_t swz(int row, int col) {
+  return (uint32_t)((col >> 5) * HALF + row * 128 + ((((col & 31) >> 2) ^ (row & 7)) << 4) + (col & 3) * 4);
+}
+
+struct Bars {
+  uint64_t kfull[STAGES], vfull[STAGES], kconv[STAGES], vconv[STAGES], kempty[STAGES], vempty[STAGES];
+  uint64_t sfull[2], pready[2], ofull[2], ofree[2];
+  uint64_t qready, done;
+  uint32_t tmem;
+  int abort_flag;
+  int issued_k[STAGES], issued_v[STAGES];
+};
+constexpr int SMEM = STAGES * STAGE + 1024 + (int)sizeof(Bars);
+
+__device__ int g_attn_err = 0;
+
+__device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity, int code) {
+  return cv3tc::mbar_wait(bar, parity, &g_attn_err, code);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars& B = *reinterpret_cast<Bars*>(smem + STAGES * STAGE);
+  volatile int* abort_flag = &B.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int b = bh / a.heads, h = bh - b * a.heads;
+  const int hk = h / (a.heads / a.kv_heads);
+  const int q0 = blockIdx.x * BQ;
+  const int qlast = min(a.n, q0 + BQ) - 1;
+  // keys any query of this CTA may see
+  int kbeg = 0, kend = a.m;
+  if (a.mask_kind == 1) {
+    kend = (int)min((long long)a.m, (long long)qlast + a.mask_a + 1);
+  } else if (a.mask_kind == 2) {
+    kend = (int)min((long long)a.m, ((long long)qlast / a.mask_a + 1) * a.mask_a);
+    if (a.mask_b >= 0) kbeg = max((q0 / a.mask_a - a.mask_b) * a.mask_a, 0);
+  }
+  const int tbeg = kbeg / BKV;
+  const int nt = kend > kbeg ? (kend + BKV - 1) / BKV - tbeg : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&B.kfull[s], 1);
+      mbar_init(&B.vfull[s], 1);
+      mbar_init(&B.kconv[s], 4);
+      mbar_init(&B.vconv[s], 4);
+      mbar_init(&B.kempty[s], 1);
+      mbar_init(&B.vempty[s], 1);
+      B.issued_k[s] = -1;
+      B.issued_v[s] = -1;
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.sfull[i], 1);
+      mbar_init(&B.pready[i], 4);
+      mbar_init(&B.ofull[i], 1);
+      mbar_init(&B.ofree[i], 4);
+    }
+    mbar_init(&B.qready, 4);
+    mbar_init(&B.done, 1);
+    B.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B.tmem)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = B.tmem;
+
+  if (warp == 0) {
+    // ---- TMA producer ----------------------------------------------------------------
+    if (lane == 0) {
+      for (int t = 0; t < nt; ++t) {
+        const int s = t % STAGES;
+        const uint32_t r = (uint32_t)(t / STAGES);
+        const int key0 = (tbeg + t) * BKV;
+        uint8_t* st = smem + s * STAGE;
+        if (*abort_flag || !bwait(&B.kempty[s], (r & 1) ^ 1, 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        B.issued_k[s] = (int)r;
+        mbar_expect_tx(&B.kfull[s], TILE);
+        tma_load_4d(st, &kmap, &B.kfull[s], 0, key0, hk, b);
+        tma_load_4d(st + HALF, &kmap, &B.kfull[s], 32, key0, hk, b);
+        if (*abort_flag || !bwait(&B.vempty[s], (r & 1) ^ 1, 2)) {
+          *abort_flag = 1;
+          break;
+        }
+        B.issued_v[s] = (int)r;
+        mbar_expect_tx(&B.vfull[s], TILE);
+        tma_load_4d(st + 2 * TILE, &vmap, &B.vfull[s], 0, key0, hk, b);
+        tma_load_4d(st + 2 * TILE + HALF, &vmap, &B.vfull[s], 32, key0, hk, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer --------------------------------------------------------------------
+    if (lane == 0) {
+      auto issue_s = [&](int t) -> bool {
+        const int s = t % STAGES;
+        const uint32_t r = (uint32_t)(t / STAGES);
+        if (*abort_flag || !bwait(&B.kconv[s], r & 1, 3)) return false;
+        fence_after();
+        const uint32_t khi = smem_u32(smem + s * STAGE), klo = khi + TILE;
+        const uint32_t d = tmem + C_S + 64u * (t & 1);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * HALF + (kk & 3) * 32);
+          mma_ts(d, tmem + C_QHI + 8 * kk, desc_k_sw128(klo + off), ID_S, kk > 0 ? 1u : 0u);
+          mma_ts(d, tmem + C_QLO + 8 * kk, desc_k_sw128(khi + off), ID_S, 1u);
+          mma_ts(d, tmem + C_QHI + 8 * kk, desc_k_sw128(khi + off), ID_S, 1u);
+        }
+        mma_commit(&B.sfull[t & 1]);
+        mma_commit(&B.kempty[s]);
+        return true;
+      };
+      auto issue_pv = [&](int t) -> bool {
+        const int s = t % STAGES;
+        const uint32_t r = (uint32_t)(t / STAGES);
+        if (*abort_flag || !bwait(&B.pready[t & 1], (uint32_t)(t >> 1) & 1, 4)) return false;
+        if (!bwait(&B.vconv[s], r & 1, 5)) return false;
+        if (t >= 2 && !bwait(&B.ofree[t & 1], (uint32_t)((t - 2) >> 1) & 1, 6)) return false;
+        fence_after();
+        const uint32_t vhi = smem_u32(smem + s * STAGE + 2 * TILE), vlo = vhi + TILE;
+        const uint32_t d = tmem + C_O + 64u * (t & 1);
+        const uint32_t phi = tmem + C_S + 64u * (t & 1), plo = tmem + C_PLO + 64u * (t & 1);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 8; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * HALF + (kk & 3) * 32);
+          mma_ts(d, phi + 8 * kk, desc_k_sw128(vlo + off), ID_PV, kk > 0 ? 1u : 0u);
+          mma_ts(d, plo + 8 * kk, desc_k_sw128(vhi + off), ID_PV, 1u);
+          mma_ts(d, phi + 8 * kk, desc_k_sw128(vhi + off), ID_PV, 1u);
+        }
+        mma_commit(&B.ofull[t & 1]);
+        mma_commit(&B.vempty[s]);
+        return true;
+      };
+      bool ok = nt == 0 || (!*abort_flag && bwait(&B.qready, 0, 7));
+      if (ok && nt > 0) {
+        fence_after();
+        ok = issue_s(0) && (nt < 2 || issue_s(1));
+        for (int t = 0; ok && t < nt; ++t) ok = issue_pv(t) && (t + 2 >= nt || issue_s(t + 2));
+      }
+      if (!ok) *abort_flag = 1;
+      mma_commit(&B.done);  // arrives once everything issued above has completed
+    }
+  } else if (warp >= 6) {
+    // ---- Q into TMEM, then K/V tiles split in place --------------------------------------
+    const int quarter = warp & 3;
+    const int ctid = threadIdx.x - 192;
+    const int row = quarter * 32 + lane;
+    const int qi = q0 + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    if (nt > 0) {
+      const float* qp = a.q + (int64_t)b * a.qsb + (int64_t)h * a.qsh + (int64_t)min(qi, a.n - 1) * a.qsn;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float hi[32], lo[32];
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (qi < a.n) x = *reinterpret_cast<const float4*>(qp + half * 32 + c4 * 4);
+          const float xs[4] = {x.x * a.scale, x.y * a.scale, x.z * a.scale, x.w * a.scale};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            hi[c4 * 4 + e] = tf32_hi(xs[e]);
+            lo[c4 * 4 + e] = xs[e] - hi[c4 * 4 + e];
+          }
+        }
+        tmem_st32(tmem + lane_base + C_QHI + 32 * half, hi);
+        tmem_st32(tmem + lane_base + C_QLO + 32 * half, lo);
+      }
+      tmem_st_wait();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.qready);
+    }
+    for (int t = 0; t < nt; ++t) {
+      const int s = t % STAGES;
+      const uint32_t r = (uint32_t)(t / STAGES);
+      float* st = reinterpret_cast<float*>(smem + s * STAGE);
+      bool go = !*abort_flag && bwait(&B.kfull[s], r & 1, 8);
+      go = __all_sync(0xffffffffu, go);
+      if (!go) {
+        *abort_flag = 1;
+        break;
+      }
+      split_tile(st, st + TILE / 4, TILE, ctid, 128);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.kconv[s]);
+      go = !*abort_flag && bwait(&B.vfull[s], r & 1, 9);
+      go = __all_sync(0xffffffffu, go);
+      if (!go) {
+        *abort_flag = 1;
+        break;
+      }
+      {
+        // V_t arrives as [key][d]; the MMA wants V_t^T [d][key] as a K-major
+        // operand (tf32 has no MN-major form with this swizzle), so the tile is
+        // transposed while it is split: all raw reads, a barrier of the four
+        // converter warps, then the hi/lo writes over the raw tile.
+        uint8_t* vraw = reinterpret_cast<uint8_t*>(st) + 2 * TILE;
+        float rv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int e = ctid + 128 * i;
+          rv[i] = *reinterpret_cast<const float*>(vraw + swz(e >> 6, e & 63));
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        float* vlo = st + 3 * TILE / 4;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const uint32_t off = swz(ctid & 63, (ctid >> 6) + 2 * i);
+          const float hv = tf32_hi(rv[i]);
+          *reinterpret_cast<float*>(vraw + off) = hv;
+          *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(vlo) + off) = rv[i] - hv;
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.vconv[s]);
+    }
+  } else {
+    // ---- softmax and output (warps 2-5) --------------------------------------------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int qi = q0 + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    float o[HD];
+#pragma unroll
+    for (int c = 0; c < HD; ++c) o[c] = 0.f;
+    float mrun = -INFINITY, l = 0.f, macc = -INFINITY, mprev = -INFINITY;
+    bool ok = true;
+    // fold O_u (relative to max mu) into the accumulator (relative to macc)
+    auto fold = [&](int u, float mu) -> bool {
+      bool go = !*abort_flag && bwait(&B.ofull[u & 1], (uint32_t)(u >> 1) & 1, 10);
+      go = __all_sync(0xffffffffu, go);
+      if (!go) return false;
+      fence_after();
+      const float c = (macc == -INFINITY) ? 0.f : expf(macc - (mu == -INFINITY ? 0.f : mu));
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float ov[32];
+        tmem_ld32(tmem + lane_base + C_O + 64u * (u & 1) + 32 * half, ov);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[half * 32 + j] = fmaf(o[half * 32 + j], c, ov[j]);
+      }
+      macc = mu;
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.ofree[u & 1]);
+      return true;
+    };
+    for (int t = 0; t < nt; ++t) {
+      const int key0 = (tbeg + t) * BKV;
+      bool go = !*abort_flag && bwait(&B.sfull[t & 1], (uint32_t)(t >> 1) & 1, 11);
+      go = __all_sync(0xffffffffu, go);
+      if (!go) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      float sv[BKV];
+      tmem_ld32(tmem + lane_base + C_S + 64u * (t & 1), sv);
+      tmem_ld32(tmem + lane_base + C_S + 64u * (t & 1) + 32, sv + 32);
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < BKV; ++j) {
+        const int kj = key0 + j;
+        if (kj >= a.m || !allowed(a, qi, kj)) sv[j] = -INFINITY;
+        tmax = fmaxf(tmax, sv[j]);
+      }
+      const float mnew = fmaxf(mrun, tmax);
+      const float base = mnew == -INFINITY ? 0.f : mnew;
+      float psum = 0.f;
+#pragma unroll
+      for (int j = 0; j < BKV; ++j) {
+        sv[j] = expf(sv[j] - base);
+        psum += sv[j];
+      }
+      l = (mrun == -INFINITY ? 0.f : l * expf(mrun - base)) + psum;
+      mrun = mnew;
+      // P_lo buffer (t & 1) was last read by O_{t-2}, which fold(t-2) waited for
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float lo[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float p = sv[half * 32 + j];
+          sv[half * 32 + j] = tf32_hi(p);
+          lo[j] = p - sv[half * 32 + j];
+        }
+        tmem_st32(tmem + lane_base + C_S + 64u * (t & 1) + 32 * half, sv + half * 32);
+        tmem_st32(tmem + lane_base + C_PLO + 64u * (t & 1) + 32 * half, lo);
+      }
+      tmem_st_wait();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.pready[t & 1]);
+      if (t >= 1 && !fold(t - 1, mprev)) {
+        ok = false;
+        break;
+      }
+      mprev = mnew;
+    }
+    if (ok && nt > 0) ok = fold(nt - 1, mprev);
+    if (!ok) *abort_flag = 1;
+    if (ok && qi < a.n) {
+      const float inv = 1.0f / l;
+      float* op = a.o + (int64_t)b * a.osb + (int64_t)h * a.osh + (int64_t)qi * a.osn;
+#pragma unroll
+      for (int c4 = 0; c4 < HD / 4; ++c4)
+        reinterpret_cast<float4*>(op)[c4] =
+            make_float4(o[4 * c4] * inv, o[4 * c4 + 1] * inv, o[4 * c4 + 2] * inv, o[4 * c4 + 3] * inv);
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) {
+      if (*abort_flag) {
+        // let every issued TMA copy land before the shared memory is released
+        for (int s = 0; s < STAGES; ++s) {
+          if (B.issued_k[s] >= 0) bwait(&B.kfull[s], (uint32_t)B.issued_k[s] & 1, 12);
+          if (B.issued_v[s] >= 0) bwait(&B.vfull[s], (uint32_t)B.issued_v[s] & 1, 13);
+        }
+      }
+      bwait(&B.done, 0, 14);  // every MMA (and its barrier arrivals) finished
+    }
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+  }
+}
+
+// 4-D map (head dim, keys, kv heads, batch) over a strided K or V; size-1 modes
+// get a nominal stride (they are never stepped).
+int make_kv_map(CUtensorMap* map, const float* base, int64_t m, int64_t kv_heads, int64_t batch, int64_t sn, int64_t sh,
+                int64_t sb) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  CV3_REQUIRE(encode != nullptr, CV3_ERR_CUDA, "attention: cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)m, (cuuint64_t)kv_heads, (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)(sn * 4), (cuuint64_t)((kv_heads > 1 ? sh : sn) * 4),
+                           (cuuint64_t)((batch > 1 ? sb : sn) * 4)};
+  for (int i = 0; i < 3; ++i)
+    CV3_REQUIRE(strides[i] > 0 && strides[i] % 16 == 0 && strides[i] < (1ull << 40), CV3_ERR_VALUE,
+                "attention: key/value stride not usable by TMA");
+  cuuint32_t box[4] = {32, (cuuint32_t)BKV, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CV3_REQUIRE(r == CUDA_SUCCESS, CV3_ERR_CUDA, "attention: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return CV3_OK;
+}
+
+int launch(const AttnArgs& a, int64_t batch, cudaStream_t st) {
+  CUtensorMap km, vm;
+  int rc = make_kv_map(&km, a.k, a.m, a.kv_heads, batch, a.ksn, a.ksh, a.ksb);
+  if (rc) return rc;
+  rc = make_kv_map(&vm, a.v, a.m, a.kv_heads, batch, a.vsn, a.vsh, a.vsb);
+  if (rc) return rc;
+  rc = cv3::allow_smem((const void*)attn_tc_kernel, SMEM);
+  if (rc) return rc;
+  dim3 grid((unsigned)((a.n + BQ - 1) / BQ), (unsigned)(batch * a.heads));
+  attn_tc_kernel<<<grid, THREADS, SMEM, st>>>(km, vm, a);
+  return cv3::check_launch("attention_tc");
+}
+
+}  // namespace tc
+
 }  // namespace
 
 extern "C" int cv3_attention(const float* q, int64_t qsb, int64_t qsh, int64_t qsn,
@@ -199,9 +629,6 @@ extern "C" int cv3_attention(const float* q, int64_t qsb, int64_t qsh, int64_t q
   CV3_REQUIRE(heads % kv_heads == 0, CV3_ERR_VALUE, "%lld query heads is not a multiple of %lld kv heads",
               (long long)heads, (long long)kv_heads);
   CV3_REQUIRE(d >= 1 && d <= DMAX, CV3_ERR_UNSUPPORTED, "attention: head dim %lld > %d not built", (long long)d, DMAX);
-  CV3_REQUIRE(d % 4 == 0 && ksn % 4 == 0 && vsn % 4 == 0 && ksh % 4 == 0 && vsh % 4 == 0 && ksb % 4 == 0 &&
-                  vsb % 4 == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0,
-              CV3_ERR_UNSUPPORTED, "attention: head dim, key/value strides and bases must be 16-byte multiples");
   CV3_REQUIRE(mask_kind >= 0 && mask_kind <= 2, CV3_ERR_VALUE, "attention: unknown mask kind %d", mask_kind);
   CV3_REQUIRE(mask_kind != 2 || mask_a > 0, CV3_ERR_VALUE, "attention: chunk size must be positive");
   if (batch == 0 || n == 0) return CV3_OK;
@@ -221,7 +648,24 @@ extern "C" int cv3_attention(const float* q, int64_t qsb, int64_t qsh, int64_t q
     attn_decode_kernel<<<grid, DT, (size_t)smem, st>>>(a);
     return cv3::check_launch("attention_decode");
   }
+  const bool kv16 = d % 4 == 0 && ksn % 4 == 0 && vsn % 4 == 0 && ksh % 4 == 0 && vsh % 4 == 0 && ksb % 4 == 0 &&
+                   vsb % 4 == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0;
+  const bool qo16 = qsn % 4 == 0 && qsh % 4 == 0 && qsb % 4 == 0 && ((uintptr_t)q & 15) == 0 && osn % 4 == 0 &&
+                    osh % 4 == 0 && osb % 4 == 0 && ((uintptr_t)o & 15) == 0;
+  if (d == tc::HD && kv16 && qo16) return tc::launch(a, batch, st);
   dim3 grid((unsigned)((n + QT - 1) / QT), (unsigned)(batch * heads));
-  attn_full_kernel<<<grid, QT, 0, st>>>(a);
+  if (kv16) attn_full_kernel<true><<<grid, QT, 0, st>>>(a);
+  else attn_full_kernel<false><<<grid, QT, 0, st>>>(a);
   return cv3::check_launch("attention_full");
+}
+
+extern "C" int cv3_tc_attention_status(int* code) {
+  int v = 0;
+  CV3_CUDA(cudaMemcpyFromSymbol(&v, tc::g_attn_err, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    CV3_CUDA(cudaMemcpyToSymbol(tc::g_attn_err, &zero, sizeof(int)));
+  }
+  if (code) *code = v;
+  return CV3_OK;
 }

@@ -23,12 +23,11 @@
 // Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records
 // an error code (read with cv3_tc_gemm_status), skips its remaining work, waits
 // (bounded) for its own MMAs, frees TMEM and exits.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace {
+
+using namespace cv3tc;
 
 constexpr int BM = 128, BN = 128, BK = 32;  // BK fp32 = 128 bytes = one swizzle row
 constexpr int STAGES = 3;
@@ -38,119 +37,20 @@ constexpr int STAGE_BYTES = 2 * TILE_A + 2 * TILE_B;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;  // up to 4 accumulators of BN fp32 columns
-constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
 
 __device__ int g_tc_err = 0;
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ unsigned long long now_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait; returns false (and records `code`) if the phase never completes.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
-  if (mbar_test(bar, parity)) return true;
-  const unsigned long long t0 = now_ns();
-  while (!mbar_test(bar, parity)) {
-    if (now_ns() - t0 > WAIT_NS) {
-      atomicCAS(&g_tc_err, 0, code);
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
-          "r"(smem_u32(dst)),
-      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
-// UMMA shared-memory descriptor, K-major, SWIZZLE_128B: 8-row x 128 B atoms,
-// atoms 1024 B apart (SBO), leading offset unused (1), Blackwell version 1.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+  return cv3tc::mbar_wait(bar, parity, &g_tc_err, code);
 }
 
 // kind::tf32 instruction descriptor: D f32, A/B tf32, K-major, M = 128, N = BN.
-constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t addr) { return desc_k_sw128(addr); }
 
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(IDESC), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Split one stage in place: hi = x & ~0x1FFF (tf32), lo = x - hi.
-__device__ __forceinline__ void split_tile(float* hi, float* lo, int bytes, int tid, int nthreads) {
-  float4* h4 = reinterpret_cast<float4*>(hi);
-  float4* l4 = reinterpret_cast<float4*>(lo);
-  for (int i = tid; i < bytes / 16; i += nthreads) {
-    float4 x = h4[i], h, l;
-    h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
-    h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
-    h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
-    h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
-    l.x = x.x - h.x;
-    l.y = x.y - h.y;
-    l.z = x.z - h.z;
-    l.w = x.w - h.w;
-    h4[i] = h;
-    l4[i] = l;
-  }
+  mma_ss(d_tmem, a, b, IDESC, accumulate);
 }
 
 struct Epi {
@@ -335,20 +235,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
-}
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point, so the library
-// does not link libcuda and loads on machines without a driver.
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
 }
 
 int make_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {

@@ -166,7 +166,9 @@ int cv3_conv1d(const float* x, int64_t batch, int64_t cin, int64_t t_in, const f
  * base + b*s_b + h*s_h + i*s_n + d (strides in floats), so (H, N, D) and
  * token-major (B, N, H*D) layouts are both read in place.  GQA: query head h
  * uses kv head h / (heads / kv_heads).  Replaces cv3cpu/ops.py:267-310 (sdpa
- * with _block_mask :244-264); head_dim <= 64. */
+ * with _block_mask :244-264); head_dim <= 64.  Head dim 64 with 16-byte
+ * aligned rows (the DiT and Qwen2 shapes) and more than 4 queries runs on the
+ * tensor cores (tcgen05, 3xTF32, flash tiling); other shapes on CUDA cores. */
 int cv3_attention(const float* q, int64_t qsb, int64_t qsh, int64_t qsn,
                   const float* k, int64_t ksb, int64_t ksh, int64_t ksn,
                   const float* v, int64_t vsb, int64_t vsh, int64_t vsn,
@@ -371,6 +373,9 @@ int cv3_tc_gemm_cfg(const float* a, int64_t lda, const float* b, int64_t ldb, fl
 /* Error word of the tensor-core kernels (0 = none; else the code of the
  * first bounded wait that expired), read and cleared.  Synchronises. */
 int cv3_tc_gemm_status(int* code);
+
+/* Same for the tensor-core attention kernel (cv3_attention, head dim 64). */
+int cv3_tc_attention_status(int* code);
 
 #ifdef __cplusplus
 }
