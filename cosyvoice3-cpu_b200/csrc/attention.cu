@@ -208,18 +208,20 @@ attn_decode_kernel(AttnArgs a) {
 //   warp 0     TMA producer (K and V tiles, SWIZZLE_128B);
 //   warp 1     MMA issuer: S_t = Q.K_t^T into TMEM, O_t = P_t.V_t into TMEM,
 //              both as hi*lo + lo*hi + hi*hi tf32 products (fp32-accurate);
-//   warps 2-5  softmax: one query row per thread (TMEM lane), online max / sum
-//              in fp32, P_t split into tf32 hi/lo written back to TMEM, and
-//              the per-tile O_t folded into a register accumulator;
-//   warps 6-9  split the scaled Q rows into TMEM once, then every landed K
-//              tile in place into hi/lo shared-memory buffers and every V
-//              tile, transposed, the same way.
+//              S_{t+2} is issued right behind O_t so the tensor pipe has work
+//              while the softmax warps handle tile t+1;
+//   warps 2-5  softmax, one query row per thread (= TMEM lane): running max,
+//              P_t = 2^(s*log2e - m*log2e) split into tf32 hi/lo and written
+//              back to TMEM, the row sum, and the rescale factor alpha_t of the
+//              running output (shared memory);
+//   warps 6-9  the scaled Q rows into TMEM once; then per tile the K tile split
+//              in place into hi/lo, the V tile transposed and split (tf32 MMAs
+//              take K-major operands only), and the fold o = o*alpha_u + O_u of
+//              an earlier tile's output into registers; finally o / l stored.
 // TMEM columns: Q hi | Q lo | S/P-hi x2 | P-lo x2 | O x2 (512).  Q and P are
 // the A operands straight from TMEM; K and the transposed V are K-major B
-// operands in shared memory.  S for tile t+2 is issued behind O for tile t, so the
-// tensor pipe works while the softmax warps do.  Every wait is bounded; on a
-// timeout the CTA records an error (cv3_tc_attention_status), drains what it
-// issued and exits.
+// operands in shared memory.  Every wait is bounded; on a timeout the CTA
+// records an error (cv3_tc_attention_status), drains what it issued and exits.
 // ---------------------------------------------------------------------------
 namespace tc {
 
@@ -233,6 +235,7 @@ constexpr int THREADS = 320;
 constexpr uint32_t C_QHI = 0, C_QLO = 64, C_S = 128, C_PLO = 256, C_O = 384;
 constexpr uint32_t ID_S = idesc_tf32(BQ, BKV);
 constexpr uint32_t ID_PV = idesc_tf32(BQ, HD);
+constexpr float LOG2E = 1.4426950408889634f;
 
 // byte offset of element (row, col) of a [rows][64] fp32 tile held as two
 // 32-column TMA boxes of [rows][128 B] with the 128-byte swizzle (16-byte
@@ -243,11 +246,13 @@ __device__ __forceinline__ uint32_t swz(int row, int col) {
 
 struct Bars {
   uint64_t kfull[STAGES], vfull[STAGES], kconv[STAGES], vconv[STAGES], kempty[STAGES], vempty[STAGES];
-  uint64_t sfull[2], pready[2], ofull[2], ofree[2];
+  uint64_t sfull[2], pready[2], ofull[2], ofree[2], aready[4];
   uint64_t qready, done;
   uint32_t tmem;
   int abort_flag;
   int issued_k[STAGES], issued_v[STAGES];
+  float alpha[4][BQ];  // rescale factor of the running output, per tile (mod 4) and row
+  float lfin[BQ];      // final softmax denominators
 };
 constexpr int SMEM = STAGES * STAGE + 1024 + (int)sizeof(Bars);
 
@@ -257,6 +262,18 @@ __device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity, int code) 
   return cv3tc::mbar_wait(bar, parity, &g_attn_err, code);
 }
 
+template <int MASK>
+__device__ __forceinline__ bool visible(const AttnArgs& a, int qi, int kj) {
+  if (MASK == 1) return kj <= qi + a.mask_a;
+  if (MASK == 2) {
+    const int c = qi / a.mask_a;
+    const int start = a.mask_b < 0 ? 0 : max((c - a.mask_b) * a.mask_a, 0);
+    return kj < (c + 1) * a.mask_a && kj >= start;
+  }
+  return true;
+}
+
+template <int MASK>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -271,9 +288,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
   const int qlast = min(a.n, q0 + BQ) - 1;
   // keys any query of this CTA may see
   int kbeg = 0, kend = a.m;
-  if (a.mask_kind == 1) {
+  if (MASK == 1) {
     kend = (int)min((long long)a.m, (long long)qlast + a.mask_a + 1);
-  } else if (a.mask_kind == 2) {
+  } else if (MASK == 2) {
     kend = (int)min((long long)a.m, ((long long)qlast / a.mask_a + 1) * a.mask_a);
     if (a.mask_b >= 0) kbeg = max((q0 / a.mask_a - a.mask_b) * a.mask_a, 0);
   }
@@ -297,6 +314,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
       mbar_init(&B.ofull[i], 1);
       mbar_init(&B.ofree[i], 4);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(&B.aready[i], 4);
     mbar_init(&B.qready, 4);
     mbar_init(&B.done, 1);
     B.abort_flag = 0;
@@ -390,170 +408,177 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
       if (!ok) *abort_flag = 1;
       mma_commit(&B.done);  // arrives once everything issued above has completed
     }
-  } else if (warp >= 6) {
-    // ---- Q into TMEM, then K/V tiles split in place --------------------------------------
+  } else if (warp < 6) {
+    // ---- softmax (warps 2-5) -------------------------------------------------------------
     const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int qi = q0 + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    float mrun = -INFINITY, l = 0.f;
+    for (int t = 0; t < nt; ++t) {
+      const int key0 = (tbeg + t) * BKV;
+      // S_t done also means O_{t-2} is done (the pipe runs in issue order), so the
+      // P-lo buffer of this parity is free again
+      bool go = !*abort_flag && bwait(&B.sfull[t & 1], (uint32_t)(t >> 1) & 1, 11);
+      go = __all_sync(0xffffffffu, go);
+      if (!go) {
+        *abort_flag = 1;
+        break;
+      }
+      fence_after();
+      float sv[BKV];
+      tmem_ld64(tmem + lane_base + C_S + 64u * (t & 1), sv);
+      if (MASK != 0 || key0 + BKV > a.m) {
+#pragma unroll
+        for (int j = 0; j < BKV; ++j)
+          if (key0 + j >= a.m || !visible<MASK>(a, qi, key0 + j)) sv[j] = -INFINITY;
+      }
+      float mx[BKV / 2];
+#pragma unroll
+      for (int j = 0; j < BKV / 2; ++j) mx[j] = fmaxf(sv[j], sv[j + BKV / 2]);
+#pragma unroll
+      for (int w = BKV / 4; w >= 1; w >>= 1)
+#pragma unroll
+        for (int j = 0; j < w; ++j) mx[j] = fmaxf(mx[j], mx[j + w]);
+      const float mnew = fmaxf(mrun, mx[0]);
+      const float mlog = mnew == -INFINITY ? 0.f : mnew * LOG2E;
+      const float alpha = mrun == -INFINITY ? 0.f : ex2(fmaf(mrun, LOG2E, -mlog));
+      float lo[BKV];
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < BKV; ++j) {
+        const float p = ex2(fmaf(sv[j], LOG2E, -mlog));
+        ps[j & 3] += p;
+        sv[j] = tf32_hi(p);
+        lo[j] = p - sv[j];
+      }
+      tmem_st64(tmem + lane_base + C_S + 64u * (t & 1), sv);
+      tmem_st64(tmem + lane_base + C_PLO + 64u * (t & 1), lo);
+      l = l * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+      mrun = mnew;
+      B.alpha[t & 3][row] = alpha;
+      if (t == nt - 1) B.lfin[row] = l;
+      tmem_st_wait();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&B.pready[t & 1]);
+        mbar_arrive(&B.aready[t & 3]);
+      }
+    }
+  } else {
+    // ---- Q into TMEM; K/V tiles split; output folds (warps 6-9) ---------------------------
+    const int quarter = warp & 3;
+    const int cw = warp - 6;          // converter warp 0..3
     const int ctid = threadIdx.x - 192;
     const int row = quarter * 32 + lane;
     const int qi = q0 + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     if (nt > 0) {
       const float* qp = a.q + (int64_t)b * a.qsb + (int64_t)h * a.qsh + (int64_t)min(qi, a.n - 1) * a.qsn;
+      float hi[HD], lo[HD];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float hi[32], lo[32];
+      for (int c4 = 0; c4 < HD / 4; ++c4) {
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (qi < a.n) x = *reinterpret_cast<const float4*>(qp + c4 * 4);
+        const float xs[4] = {x.x * a.scale, x.y * a.scale, x.z * a.scale, x.w * a.scale};
 #pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
-          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (qi < a.n) x = *reinterpret_cast<const float4*>(qp + half * 32 + c4 * 4);
-          const float xs[4] = {x.x * a.scale, x.y * a.scale, x.z * a.scale, x.w * a.scale};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            hi[c4 * 4 + e] = tf32_hi(xs[e]);
-            lo[c4 * 4 + e] = xs[e] - hi[c4 * 4 + e];
-          }
+        for (int e = 0; e < 4; ++e) {
+          hi[c4 * 4 + e] = tf32_hi(xs[e]);
+          lo[c4 * 4 + e] = xs[e] - hi[c4 * 4 + e];
         }
-        tmem_st32(tmem + lane_base + C_QHI + 32 * half, hi);
-        tmem_st32(tmem + lane_base + C_QLO + 32 * half, lo);
       }
+      tmem_st64(tmem + lane_base + C_QHI, hi);
+      tmem_st64(tmem + lane_base + C_QLO, lo);
       tmem_st_wait();
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&B.qready);
     }
-    for (int t = 0; t < nt; ++t) {
+    float o[HD];
+#pragma unroll
+    for (int c = 0; c < HD; ++c) o[c] = 0.f;
+    bool ok = true;
+    // o = o * alpha_u + O_u, then hand the O buffer back to the MMA warp
+#define CV3_FOLD(u)                                                                               \
+  {                                                                                               \
+    const int u_ = (u);                                                                           \
+    bool go_ = !*abort_flag && bwait(&B.aready[u_ & 3], (uint32_t)(u_ >> 2) & 1, 10) &&           \
+               bwait(&B.ofull[u_ & 1], (uint32_t)(u_ >> 1) & 1, 12);                              \
+    go_ = __all_sync(0xffffffffu, go_);                                                           \
+    if (!go_) {                                                                                   \
+      ok = false;                                                                                 \
+    } else {                                                                                      \
+      fence_after();                                                                              \
+      const float al_ = B.alpha[u_ & 3][row];                                                     \
+      float ov_[HD];                                                                              \
+      tmem_ld64(tmem + lane_base + C_O + 64u * (u_ & 1), ov_);                                    \
+      _Pragma("unroll") for (int c = 0; c < HD; ++c) o[c] = fmaf(o[c], al_, ov_[c]);              \
+      fence_before();                                                                             \
+      __syncwarp();                                                                               \
+      if (lane == 0) mbar_arrive(&B.ofree[u_ & 1]);                                               \
+    }                                                                                             \
+  }
+    for (int t = 0; ok && t < nt; ++t) {
       const int s = t % STAGES;
       const uint32_t r = (uint32_t)(t / STAGES);
-      float* st = reinterpret_cast<float*>(smem + s * STAGE);
+      uint8_t* st = smem + s * STAGE;
       bool go = !*abort_flag && bwait(&B.kfull[s], r & 1, 8);
       go = __all_sync(0xffffffffu, go);
       if (!go) {
-        *abort_flag = 1;
+        ok = false;
         break;
       }
-      split_tile(st, st + TILE / 4, TILE, ctid, 128);
+      split_tile(reinterpret_cast<float*>(st), reinterpret_cast<float*>(st + TILE), TILE, ctid, 128);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&B.kconv[s]);
       go = !*abort_flag && bwait(&B.vfull[s], r & 1, 9);
       go = __all_sync(0xffffffffu, go);
       if (!go) {
-        *abort_flag = 1;
+        ok = false;
         break;
       }
       {
-        // V_t arrives as [key][d]; the MMA wants V_t^T [d][key] as a K-major
-        // operand (tf32 has no MN-major form with this swizzle), so the tile is
-        // transposed while it is split: all raw reads, a barrier of the four
-        // converter warps, then the hi/lo writes over the raw tile.
-        uint8_t* vraw = reinterpret_cast<uint8_t*>(st) + 2 * TILE;
-        float rv[32];
+        // V_t arrives as [key][d]; the MMA wants V_t^T [d][key] as a K-major operand,
+        // so the tile is transposed while it is split.  Reads: float4 along d, eight
+        // consecutive keys per quarter-warp (distinct swizzled chunks); writes: a warp
+        // covers 32 consecutive keys of one d row (32 distinct banks).  All reads
+        // finish (barrier of the four converter warps) before the in-place writes.
+        uint8_t* vraw = st + 2 * TILE;
+        uint8_t* vlo = st + 3 * TILE;
+        float4 rv[2][4];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int e = ctid + 128 * i;
-          rv[i] = *reinterpret_cast<const float*>(vraw + swz(e >> 6, e & 63));
-        }
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int i4 = 0; i4 < 4; ++i4)
+            rv[kb][i4] = *reinterpret_cast<const float4*>(vraw + swz(lane + 32 * kb, 4 * (cw * 4 + i4)));
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        float* vlo = st + 3 * TILE / 4;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const uint32_t off = swz(ctid & 63, (ctid >> 6) + 2 * i);
-          const float hv = tf32_hi(rv[i]);
-          *reinterpret_cast<float*>(vraw + off) = hv;
-          *reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(vlo) + off) = rv[i] - hv;
-        }
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int i4 = 0; i4 < 4; ++i4) {
+            const float xv[4] = {rv[kb][i4].x, rv[kb][i4].y, rv[kb][i4].z, rv[kb][i4].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t off = swz(4 * (cw * 4 + i4) + e, lane + 32 * kb);
+              const float hv = tf32_hi(xv[e]);
+              *reinterpret_cast<float*>(vraw + off) = hv;
+              *reinterpret_cast<float*>(vlo + off) = xv[e] - hv;
+            }
+          }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&B.vconv[s]);
+      if (t >= 2) CV3_FOLD(t - 2);
     }
-  } else {
-    // ---- softmax and output (warps 2-5) --------------------------------------------------
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int qi = q0 + row;
-    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    float o[HD];
-#pragma unroll
-    for (int c = 0; c < HD; ++c) o[c] = 0.f;
-    float mrun = -INFINITY, l = 0.f, macc = -INFINITY, mprev = -INFINITY;
-    bool ok = true;
-    // fold O_u (relative to max mu) into the accumulator (relative to macc)
-    auto fold = [&](int u, float mu) -> bool {
-      bool go = !*abort_flag && bwait(&B.ofull[u & 1], (uint32_t)(u >> 1) & 1, 10);
-      go = __all_sync(0xffffffffu, go);
-      if (!go) return false;
-      fence_after();
-      const float c = (macc == -INFINITY) ? 0.f : expf(macc - (mu == -INFINITY ? 0.f : mu));
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float ov[32];
-        tmem_ld32(tmem + lane_base + C_O + 64u * (u & 1) + 32 * half, ov);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) o[half * 32 + j] = fmaf(o[half * 32 + j], c, ov[j]);
-      }
-      macc = mu;
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B.ofree[u & 1]);
-      return true;
-    };
-    for (int t = 0; t < nt; ++t) {
-      const int key0 = (tbeg + t) * BKV;
-      bool go = !*abort_flag && bwait(&B.sfull[t & 1], (uint32_t)(t >> 1) & 1, 11);
-      go = __all_sync(0xffffffffu, go);
-      if (!go) {
-        ok = false;
-        break;
-      }
-      fence_after();
-      float sv[BKV];
-      tmem_ld32(tmem + lane_base + C_S + 64u * (t & 1), sv);
-      tmem_ld32(tmem + lane_base + C_S + 64u * (t & 1) + 32, sv + 32);
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < BKV; ++j) {
-        const int kj = key0 + j;
-        if (kj >= a.m || !allowed(a, qi, kj)) sv[j] = -INFINITY;
-        tmax = fmaxf(tmax, sv[j]);
-      }
-      const float mnew = fmaxf(mrun, tmax);
-      const float base = mnew == -INFINITY ? 0.f : mnew;
-      float psum = 0.f;
-#pragma unroll
-      for (int j = 0; j < BKV; ++j) {
-        sv[j] = expf(sv[j] - base);
-        psum += sv[j];
-      }
-      l = (mrun == -INFINITY ? 0.f : l * expf(mrun - base)) + psum;
-      mrun = mnew;
-      // P_lo buffer (t & 1) was last read by O_{t-2}, which fold(t-2) waited for
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float lo[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float p = sv[half * 32 + j];
-          sv[half * 32 + j] = tf32_hi(p);
-          lo[j] = p - sv[half * 32 + j];
-        }
-        tmem_st32(tmem + lane_base + C_S + 64u * (t & 1) + 32 * half, sv + half * 32);
-        tmem_st32(tmem + lane_base + C_PLO + 64u * (t & 1) + 32 * half, lo);
-      }
-      tmem_st_wait();
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B.pready[t & 1]);
-      if (t >= 1 && !fold(t - 1, mprev)) {
-        ok = false;
-        break;
-      }
-      mprev = mnew;
-    }
-    if (ok && nt > 0) ok = fold(nt - 1, mprev);
+    if (ok && nt >= 2) CV3_FOLD(nt - 2);
+    if (ok && nt >= 1) CV3_FOLD(nt - 1);
+#undef CV3_FOLD
     if (!ok) *abort_flag = 1;
     if (ok && qi < a.n) {
-      const float inv = 1.0f / l;
+      const float inv = 1.0f / B.lfin[row];
       float* op = a.o + (int64_t)b * a.osb + (int64_t)h * a.osh + (int64_t)qi * a.osn;
 #pragma unroll
       for (int c4 = 0; c4 < HD / 4; ++c4)
@@ -569,11 +594,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
       if (*abort_flag) {
         // let every issued TMA copy land before the shared memory is released
         for (int s = 0; s < STAGES; ++s) {
-          if (B.issued_k[s] >= 0) bwait(&B.kfull[s], (uint32_t)B.issued_k[s] & 1, 12);
-          if (B.issued_v[s] >= 0) bwait(&B.vfull[s], (uint32_t)B.issued_v[s] & 1, 13);
+          if (B.issued_k[s] >= 0) bwait(&B.kfull[s], (uint32_t)B.issued_k[s] & 1, 13);
+          if (B.issued_v[s] >= 0) bwait(&B.vfull[s], (uint32_t)B.issued_v[s] & 1, 14);
         }
       }
-      bwait(&B.done, 0, 14);  // every MMA (and its barrier arrivals) finished
+      bwait(&B.done, 0, 15);  // every MMA (and its barrier arrivals) finished
     }
     __syncwarp();
     fence_after();
@@ -608,10 +633,11 @@ int launch(const AttnArgs& a, int64_t batch, cudaStream_t st) {
   if (rc) return rc;
   rc = make_kv_map(&vm, a.v, a.m, a.kv_heads, batch, a.vsn, a.vsh, a.vsb);
   if (rc) return rc;
-  rc = cv3::allow_smem((const void*)attn_tc_kernel, SMEM);
+  auto fn = a.mask_kind == 1 ? attn_tc_kernel<1> : (a.mask_kind == 2 ? attn_tc_kernel<2> : attn_tc_kernel<0>);
+  rc = cv3::allow_smem((const void*)fn, SMEM);
   if (rc) return rc;
   dim3 grid((unsigned)((a.n + BQ - 1) / BQ), (unsigned)(batch * a.heads));
-  attn_tc_kernel<<<grid, THREADS, SMEM, st>>>(km, vm, a);
+  fn<<<grid, THREADS, SMEM, st>>>(km, vm, a);
   return cv3::check_launch("attention_tc");
 }
 
