@@ -358,12 +358,17 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer --------------------------------------------------------------------
-    if (lane == 0) {
+    // ---- MMA issuer: the whole warp runs the loop, one elected lane issues ------------------
+    {
+      // every lane waits; the outcome is made warp-uniform before any MMA
+      auto ready = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+        const bool ok = !*abort_flag && bwait(bar, parity, code);
+        return __all_sync(0xffffffffu, ok);
+      };
       auto issue_s = [&](int t) -> bool {
         const int s = t % STAGES;
         const uint32_t r = (uint32_t)(t / STAGES);
-        if (*abort_flag || !bwait(&B.kconv[s], r & 1, 3)) return false;
+        if (!ready(&B.kconv[s], r & 1, 3)) return false;
         fence_after();
         const uint32_t khi = smem_u32(smem + s * STAGE), klo = khi + TILE;
         const uint32_t d = tmem + C_S + 64u * (t & 1);
@@ -381,9 +386,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
       auto issue_pv = [&](int t) -> bool {
         const int s = t % STAGES;
         const uint32_t r = (uint32_t)(t / STAGES);
-        if (*abort_flag || !bwait(&B.pready[t & 1], (uint32_t)(t >> 1) & 1, 4)) return false;
-        if (!bwait(&B.vconv[s], r & 1, 5)) return false;
-        if (t >= 2 && !bwait(&B.ofree[t & 1], (uint32_t)((t - 2) >> 1) & 1, 6)) return false;
+        if (!ready(&B.pready[t & 1], (uint32_t)(t >> 1) & 1, 4)) return false;
+        if (!ready(&B.vconv[s], r & 1, 5)) return false;
+        if (t >= 2 && !ready(&B.ofree[t & 1], (uint32_t)((t - 2) >> 1) & 1, 6)) return false;
         fence_after();
         const uint32_t vhi = smem_u32(smem + s * STAGE + 2 * TILE), vlo = vhi + TILE;
         const uint32_t d = tmem + C_O + 64u * (t & 1);
@@ -399,13 +404,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         mma_commit(&B.vempty[s]);
         return true;
       };
-      bool ok = nt == 0 || (!*abort_flag && bwait(&B.qready, 0, 7));
+      bool ok = nt == 0 || ready(&B.qready, 0, 7);
       if (ok && nt > 0) {
         fence_after();
         ok = issue_s(0) && (nt < 2 || issue_s(1));
         for (int t = 0; ok && t < nt; ++t) ok = issue_pv(t) && (t + 2 >= nt || issue_s(t + 2));
       }
-      if (!ok) *abort_flag = 1;
+      if (!ok && lane == 0) *abort_flag = 1;
       mma_commit(&B.done);  // arrives once everything issued above has completed
     }
   } else if (warp < 6) {

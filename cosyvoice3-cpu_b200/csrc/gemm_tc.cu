@@ -124,41 +124,41 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      bool ok = true;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t round = kb / STAGES;
-        if (*(volatile int*)abort_flag || !mbar_wait(&conv[s], round & 1, 2)) {
-          *(volatile int*)abort_flag = 1;
-          ok = false;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_hi = smem_u32(smem + s * STAGE_BYTES);
-        const uint32_t a_lo = a_hi + TILE_A;
-        const uint32_t b_hi = a_hi + 2 * TILE_A;
-        const uint32_t b_lo = b_hi + TILE_B;
-        // accumulator of this K block: K range chunk, cross terms optionally apart
-        const int chunk = kb * ep.k_chunks / nk;
-        const int first_kb = (chunk * nk + ep.k_chunks - 1) / ep.k_chunks;  // first kb of this chunk
-        const uint32_t d_main = tmem + (uint32_t)(chunk * BN);
-        const uint32_t d_cross = ep.split_cross ? tmem + (uint32_t)((ep.k_chunks + chunk) * BN) : d_main;
-#pragma unroll
-        for (int kk = 0; kk < BK / 8; ++kk) {
-          const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
-          const bool start = (kb == first_kb && kk == 0);
-          mma_tf32(d_cross, umma_desc(a_lo + off), umma_desc(b_hi + off), start ? 0u : 1u);
-          mma_tf32(d_cross, umma_desc(a_hi + off), umma_desc(b_lo + off), 1u);
-          mma_tf32(d_main, umma_desc(a_hi + off), umma_desc(b_hi + off), (start && ep.split_cross) ? 0u : 1u);
-        }
-        mma_commit(&empty[s]);
+    // the whole warp runs the MMA loop (operands warp-uniform), one elected lane issues
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t round = kb / STAGES;
+      bool go = !*(volatile int*)abort_flag && mbar_wait(&conv[s], round & 1, 2);
+      if (!__all_sync(0xffffffffu, go)) {
+        if (lane == 0) *(volatile int*)abort_flag = 1;
+        ok = false;
+        break;
       }
-      // the accumulator barrier is committed even on abort so waiters are released
-      // once whatever was issued has completed
-      mma_commit(accb);
-      (void)ok;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a_hi = smem_u32(smem + s * STAGE_BYTES);
+      const uint32_t a_lo = a_hi + TILE_A;
+      const uint32_t b_hi = a_hi + 2 * TILE_A;
+      const uint32_t b_lo = b_hi + TILE_B;
+      // accumulator of this K block: K range chunk, cross terms optionally apart
+      const int chunk = kb * ep.k_chunks / nk;
+      const int first_kb = (chunk * nk + ep.k_chunks - 1) / ep.k_chunks;  // first kb of this chunk
+      const uint32_t d_main = tmem + (uint32_t)(chunk * BN);
+      const uint32_t d_cross = ep.split_cross ? tmem + (uint32_t)((ep.k_chunks + chunk) * BN) : d_main;
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint32_t off = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
+        const bool start = (kb == first_kb && kk == 0);
+        mma_tf32(d_cross, umma_desc(a_lo + off), umma_desc(b_hi + off), start ? 0u : 1u);
+        mma_tf32(d_cross, umma_desc(a_hi + off), umma_desc(b_lo + off), 1u);
+        mma_tf32(d_main, umma_desc(a_hi + off), umma_desc(b_hi + off), (start && ep.split_cross) ? 0u : 1u);
+      }
+      mma_commit(&empty[s]);
     }
+    // the accumulator barrier is committed even on abort so waiters are released
+    // once whatever was issued has completed
+    mma_commit(accb);
+    (void)ok;
   } else {
     // converters, then the epilogue
     const int ctid = threadIdx.x - 64;  // 0..127
