@@ -65,6 +65,8 @@ SIGNATURES = {
     "cv3_reflect_left1": [P, I64, I64, P, P],
     "cv3_tc_gemm": [P, I64, P, I64, P, I64, I64, I64, I64, I32, P, P, I64, I64, P],
     "cv3_tc_gemm_status": [P],
+    "cv3_tf32_lo": [P, I64, P, P],
+    "cv3_tc_gemm_split": [P, I64, P, P, I64, P, I64, I64, I64, I64, I32, P, P, I64, I64, P],
     "cv3_tc_attention_status": [P],
     "cv3_q8_decode_gemv": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
     "cv3_tc_gemm_cfg": [P, I64, P, I64, P, I64, I64, I64, I64, I32, P, P, I64, I64, I32, I32, P],

@@ -23,6 +23,8 @@
 // Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records
 // an error code (read with cv3_tc_gemm_status), skips its remaining work, waits
 // (bounded) for its own MMAs, frees TMEM and exits.
+#include <algorithm>
+
 #include "tc_common.cuh"
 
 namespace {
@@ -125,14 +127,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     }
   } else if (warp == 1) {
     // the whole warp runs the MMA loop (operands warp-uniform), one elected lane issues
-    bool ok = true;
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % STAGES;
       const uint32_t round = kb / STAGES;
       bool go = !*(volatile int*)abort_flag && mbar_wait(&conv[s], round & 1, 2);
       if (!__all_sync(0xffffffffu, go)) {
         if (lane == 0) *(volatile int*)abort_flag = 1;
-        ok = false;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -158,7 +158,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     // the accumulator barrier is committed even on abort so waiters are released
     // once whatever was issued has completed
     mma_commit(accb);
-    (void)ok;
   } else {
     // converters, then the epilogue
     const int ctid = threadIdx.x - 64;  // 0..127
@@ -254,6 +253,261 @@ int make_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int
   return CV3_OK;
 }
 
+
+// ---------------------------------------------------------------------------
+// Pre-split variant (the DiT's linears).  B comes with its tf32 remainder
+// b_lo = b - tf32(b) (made once per weight matrix by cv3_tf32_lo); the raw B
+// is the hi operand, since kind::tf32 reads only the top 19 bits of each
+// fp32.  A never touches shared memory: the four converter warps stream their
+// rows from global memory (two K blocks in flight per thread), split them and
+// write hi/lo straight into TMEM, and the MMAs take A from TMEM.  Shared
+// memory then only carries B (TMA writes + MMA reads, ~104 B/clk at the
+// tensor rate, under the 128 B/clk the SM has).
+// TMEM: two K-range accumulators for hi*hi, one for the cross terms (the
+// tensor core truncates when it accumulates, so long sums lose bits; this
+// layout measured 1.7e-6 / 2.9e-6 of max at K = 1024 / 2048 vs fp64) and two
+// A stages of 32 hi + 32 lo columns.
+// ---------------------------------------------------------------------------
+namespace split {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 5;
+constexpr int TILE_B = BN * BK * 4;      // 16 KB
+constexpr int STAGE_BYTES = 2 * TILE_B;  // raw B | B lo
+constexpr int THREADS = 192;
+constexpr uint32_t C_MAIN0 = 0, C_MAIN1 = 128, C_CROSS = 256, C_A = 384;
+constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+
+struct Bars {
+  uint64_t bfull[STAGES], bempty[STAGES], afull[2], aempty[2], acc;
+  uint32_t tmem;
+  int abort_flag;
+  int issued[STAGES];
+};
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + (int)sizeof(Bars);
+
+__device__ __forceinline__ void load_a(float4 (&dst)[8], const float* arow, bool live, int c0, int K) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = c0 + 4 * j;
+    dst[j] = (live && c < K) ? __ldg(reinterpret_cast<const float4*>(arow + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_blo,
+                     const float* __restrict__ A, int64_t lda, int M, int N, int K, float* __restrict__ C, int64_t ldc,
+                     Epi ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars& S = *reinterpret_cast<Bars*>(smem + STAGES * STAGE_BYTES);
+  volatile int* abort_flag = &S.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int nk = (K + BK - 1) / BK;
+  const int half = (nk + 1) / 2;  // first K block of the second hi*hi accumulator (used when nk >= 2)
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.bfull[s], 1);
+      mbar_init(&S.bempty[s], 1);
+      S.issued[s] = -1;
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.afull[i], 4);
+      mbar_init(&S.aempty[i], 1);
+    }
+    mbar_init(&S.acc, 1);
+    S.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = S.tmem;
+  auto ready = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+    const bool ok = !*abort_flag && mbar_wait(bar, parity, code);
+    return __all_sync(0xffffffffu, ok);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t r = (uint32_t)(kb / STAGES);
+        if (*abort_flag || !mbar_wait(&S.bempty[s], (r & 1) ^ 1, 21)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        S.issued[s] = (int)r;
+        mbar_expect_tx(&S.bfull[s], STAGE_BYTES);
+        tma_load_2d(st, &map_b, &S.bfull[s], kb * BK, n0);
+        tma_load_2d(st + TILE_B, &map_blo, &S.bfull[s], kb * BK, n0);
+      }
+    }
+  } else if (warp == 1) {
+    bool ok = true;
+    for (int kb = 0; ok && kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t r = (uint32_t)(kb / STAGES);
+      const int a = kb & 1;
+      if (!ready(&S.bfull[s], r & 1, 22) || !ready(&S.afull[a], (uint32_t)(kb >> 1) & 1, 23)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const int chunk = (nk >= 2 && kb >= half) ? 1 : 0;
+      const int chunk_first = chunk ? half : 0;
+      const uint32_t d_main = tmem + (chunk ? C_MAIN1 : C_MAIN0), d_cross = tmem + C_CROSS;
+      const uint32_t b_raw = smem_u32(smem + s * STAGE_BYTES), b_lo = b_raw + TILE_B;
+      const uint32_t a_hi = tmem + C_A + 64u * a, a_lo = a_hi + 32;
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint32_t off = kk * 32;
+        mma_ts(d_cross, a_lo + 8 * kk, desc_k_sw128(b_raw + off), IDESC, (kb == 0 && kk == 0) ? 0u : 1u);
+        mma_ts(d_cross, a_hi + 8 * kk, desc_k_sw128(b_lo + off), IDESC, 1u);
+        mma_ts(d_main, a_hi + 8 * kk, desc_k_sw128(b_raw + off), IDESC, (kb == chunk_first && kk == 0) ? 0u : 1u);
+      }
+      mma_commit(&S.bempty[s]);
+      mma_commit(&S.aempty[a]);
+    }
+    if (!ok && lane == 0) *abort_flag = 1;
+    mma_commit(&S.acc);  // also on abort: arrives once whatever was issued has completed
+  } else {
+    // ---- A rows into TMEM (one row per thread = its TMEM lane), then the epilogue ----
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int grow = m0 + row;
+    const bool live = grow < M;
+    const float* arow = A + (int64_t)(live ? grow : 0) * lda;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    bool ok = true;
+    float4 x0[8], x1[8];
+    if (nk > 0) load_a(x0, arow, live, 0, K);
+    if (nk > 1) load_a(x1, arow, live, BK, K);
+    // split K block kb (held in x) into stage kb & 1 once the MMAs of kb - 2 are done
+#define CV3_PUT_A(xb, kb_)                                                                     \
+  {                                                                                           \
+    const int kbv = (kb_);                                                                    \
+    const int a_ = kbv & 1;                                                                   \
+    if (!ready(&S.aempty[a_], ((uint32_t)(kbv >> 1) & 1) ^ 1, 24)) {                           \
+      ok = false;                                                                             \
+    } else {                                                                                  \
+      float hi[32], lo[32];                                                                   \
+      _Pragma("unroll") for (int j = 0; j < 8; ++j) {                                         \
+        const float e4[4] = {xb[j].x, xb[j].y, xb[j].z, xb[j].w};                             \
+        _Pragma("unroll") for (int e = 0; e < 4; ++e) {                                       \
+          hi[4 * j + e] = tf32_hi(e4[e]);                                                     \
+          lo[4 * j + e] = e4[e] - hi[4 * j + e];                                              \
+        }                                                                                     \
+      }                                                                                       \
+      fence_after();                                                                          \
+      tmem_st32(tmem + lane_base + C_A + 64u * a_, hi);                                       \
+      tmem_st32(tmem + lane_base + C_A + 64u * a_ + 32, lo);                                  \
+      tmem_st_wait();                                                                         \
+      fence_before();                                                                         \
+      __syncwarp();                                                                           \
+      if (lane == 0) mbar_arrive(&S.afull[a_]);                                               \
+    }                                                                                         \
+  }
+    for (int kb = 0; ok && kb < nk; kb += 2) {
+      CV3_PUT_A(x0, kb);
+      if (ok && kb + 2 < nk) load_a(x0, arow, live, (kb + 2) * BK, K);
+      if (ok && kb + 1 < nk) {
+        CV3_PUT_A(x1, kb + 1);
+        if (ok && kb + 3 < nk) load_a(x1, arow, live, (kb + 3) * BK, K);
+      }
+    }
+#undef CV3_PUT_A
+    if (!ok) *abort_flag = 1;
+    ok = ok && ready(&S.acc, 0, 25);
+    fence_after();
+    if (ok) {
+      const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32], w[32];
+        tmem_ld32(tmem + lane_base + C_CROSS + c0, v);
+        if (nk >= 2) {
+          tmem_ld32(tmem + lane_base + C_MAIN1 + c0, w);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += w[j];
+        }
+        tmem_ld32(tmem + lane_base + C_MAIN0 + c0, w);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += w[j];
+        if (!live) continue;
+        float* crow = C + (int64_t)grow * ldc + n0 + c0;
+        const float* gate = ep.mode == 2 ? ep.gate + (ep.rows_per_group > 0 ? grow / ep.rows_per_group : 0) *
+                                                       ep.gate_stride + n0 + c0
+                                         : nullptr;
+        const int ncol = min(32, N - (n0 + c0));
+        if (ncol <= 0) continue;
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          float res[4] = {0.f, 0.f, 0.f, 0.f};
+          const bool full4 = vec && 4 * j4 + 3 < ncol;
+          if (ep.mode >= 2) {
+            if (full4) {
+              const float4 t = *reinterpret_cast<const float4*>(crow + 4 * j4);
+              res[0] = t.x; res[1] = t.y; res[2] = t.z; res[3] = t.w;
+            } else {
+              for (int e = 0; e < 4; ++e)
+                if (4 * j4 + e < ncol) res[e] = crow[4 * j4 + e];
+            }
+          }
+          float out[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = 4 * j4 + e;
+            float y = v[j];
+            if (j < ncol) {
+              if (ep.bias) y = __fadd_rn(y, ep.bias[n0 + c0 + j]);
+              if (ep.mode == 1) y = gelu_tanh(y);
+              else if (ep.mode == 2) y = __fadd_rn(res[e], __fmul_rn(gate[j], y));
+              else if (ep.mode == 3) y = __fadd_rn(res[e], y);
+            }
+            out[e] = y;
+          }
+          if (full4) {
+            *reinterpret_cast<float4*>(crow + 4 * j4) = make_float4(out[0], out[1], out[2], out[3]);
+          } else {
+            for (int e = 0; e < 4; ++e)
+              if (4 * j4 + e < ncol) crow[4 * j4 + e] = out[e];
+          }
+        }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) {
+      if (*abort_flag)
+        for (int s = 0; s < STAGES; ++s)
+          if (S.issued[s] >= 0) mbar_wait(&S.bfull[s], (uint32_t)S.issued[s] & 1, 26);
+      mbar_wait(&S.acc, 0, 27);  // every MMA (and its barrier arrivals) finished
+    }
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+  }
+}
+
+__global__ void tf32_lo_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ lo) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    lo[i] = v - tf32_hi(v);
+  }
+}
+
+}  // namespace split
+
 }  // namespace
 
 extern "C" int cv3_tc_gemm_cfg(const float* a, int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc,
@@ -307,4 +561,38 @@ extern "C" int cv3_tc_gemm_status(int* code) {
   }
   if (code) *code = v;
   return CV3_OK;
+}
+
+extern "C" int cv3_tf32_lo(const float* x, int64_t n, float* lo, void* stream) {
+  CV3_REQUIRE(n >= 0, CV3_ERR_VALUE, "tf32_lo: negative size");
+  if (n == 0) return CV3_OK;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
+  split::tf32_lo_kernel<<<(unsigned)blocks, 256, 0, cv3::as_stream(stream)>>>(x, n, lo);
+  return cv3::check_launch("tf32_lo");
+}
+
+extern "C" int cv3_tc_gemm_split(const float* a, int64_t lda, const float* b, const float* b_lo, int64_t ldb,
+                                 float* c, int64_t ldc, int64_t m, int64_t n, int64_t k, int mode, const float* bias,
+                                 const float* gate, int64_t rows_per_group, int64_t gate_stride, void* stream) {
+  CV3_REQUIRE(m >= 0 && n >= 0 && k >= 0 && mode >= 0 && mode <= 3, CV3_ERR_VALUE, "tc_gemm_split: bad arguments");
+  CV3_REQUIRE(mode != 2 || gate != nullptr, CV3_ERR_VALUE, "tc_gemm_split: gated residual needs a gate");
+  CV3_REQUIRE(lda >= k && ldb >= k && ldc >= n, CV3_ERR_VALUE, "tc_gemm_split: leading dimension too small");
+  CV3_REQUIRE(k % 4 == 0 && lda % 4 == 0 && ((uintptr_t)a & 15) == 0, CV3_ERR_VALUE,
+              "tc_gemm_split: K, lda and the A base must allow 16-byte row loads");
+  if (m == 0 || n == 0) return CV3_OK;
+  CV3_REQUIRE(k > 0 && b_lo != nullptr, CV3_ERR_VALUE, "tc_gemm_split: K must be positive and b_lo given");
+  CV3_REQUIRE(m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31), CV3_ERR_VALUE, "tc_gemm_split: too large");
+  CUtensorMap mb, mbl;
+  int rc = make_map(&mb, b, n, k, ldb, split::BN);
+  if (rc) return rc;
+  rc = make_map(&mbl, b_lo, n, k, ldb, split::BN);
+  if (rc) return rc;
+  rc = cv3::allow_smem((const void*)split::tc_gemm_split_kernel, split::SMEM_BYTES);
+  if (rc) return rc;
+  dim3 grid((unsigned)((n + split::BN - 1) / split::BN), (unsigned)((m + split::BM - 1) / split::BM));
+  CV3_REQUIRE(grid.y <= 65535, CV3_ERR_VALUE, "tc_gemm_split: too many row tiles");
+  Epi ep{1, 1, mode, bias, gate, rows_per_group, gate_stride};
+  split::tc_gemm_split_kernel<<<grid, split::THREADS, split::SMEM_BYTES, cv3::as_stream(stream)>>>(
+      mb, mbl, a, lda, (int)m, (int)n, (int)k, c, ldc, ep);
+  return cv3::check_launch("tc_gemm_split");
 }

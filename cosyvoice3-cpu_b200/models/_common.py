@@ -10,6 +10,7 @@ operands), so the per-step work is launches only.
 from __future__ import annotations
 
 import numpy as np
+import torch
 
 from .. import _dev as D
 from .._lib import call
@@ -24,7 +25,7 @@ TC_MIN_ROWS = 16   # below this many rows the fp32 GEMV/SIMT path is used
 class Lin:
     """A linear layer's device operands: q8 (payload, scales) or fp32 matrix, and bias."""
 
-    __slots__ = ("q8", "w", "scales", "n", "k", "kp", "bias", "_keep")
+    __slots__ = ("q8", "w", "scales", "n", "k", "kp", "bias", "_keep", "_lo")
 
     def __init__(self, w, bias=None):
         self._keep = [w, bias]
@@ -38,6 +39,20 @@ class Lin:
             self.n, self.k = int(w.shape[0]), int(w.shape[1])
             self.kp = self.k
         self.bias = bias.data_ptr() if bias is not None else None
+        self._lo = None
+
+    def lo(self, stream=None) -> int:
+        """Device pointer to W - tf32(W), the remainder the 3xTF32 GEMM pairs with W
+        (made on first use and kept; must first be called outside stream capture)."""
+        if self._lo is None:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("Lin.lo(): the weight remainder must be made before stream capture")
+            w = self._keep[0]
+            lo = D.empty(tuple(w.shape))
+            s = stream if stream is not None else D.stream()
+            call("cv3_tf32_lo", self.w, self.n * self.k, lo.data_ptr(), s)
+            self._lo = lo
+        return self._lo.data_ptr()
 
     def __call__(self, x: int, m: int, y: int, residual: int = None, ldx: int = None, ldy: int = None,
                  stream=None):
@@ -52,7 +67,7 @@ class Lin:
         elif m >= TC_MIN_ROWS and self.k % 4 == 0 and ldx % 4 == 0:
             if residual is not None and residual != y:
                 raise ValueError("tensor-core linear adds the residual in place (residual must alias y)")
-            call("cv3_tc_gemm", x, ldx, self.w, self.k, y, ldy, m, self.n, self.k,
+            call("cv3_tc_gemm_split", x, ldx, self.w, self.lo(s), self.k, y, ldy, m, self.n, self.k,
                  3 if residual is not None else 0, self.bias, None, 0, 0, s)
         else:
             call("cv3_f32_linear", x, m, self.k, ldx, self.w, self.n, self.k, self.bias, residual, y, ldy, s)
@@ -64,8 +79,8 @@ class Lin:
         if self.q8:
             raise ValueError("fused tensor-core epilogues need fp32 weights")
         s = stream if stream is not None else D.stream()
-        call("cv3_tc_gemm", x, self.k, self.w, self.k, y, self.n, m, self.n, self.k, mode, self.bias, gate,
-             rows_per_group, gate_stride, s)
+        call("cv3_tc_gemm_split", x, self.k, self.w, self.lo(s), self.k, y, self.n, m, self.n, self.k, mode,
+             self.bias, gate, rows_per_group, gate_stride, s)
 
 
 class DecodeGemv:

@@ -124,6 +124,9 @@ class DiT:
             B.ff2 = Lin(self._dense([b + "ff.ff.2.weight"]), self._f32(b + "ff.ff.2.bias"))
             self.blocks.append(B)
         self.proj_out = Lin(f32_of(self._wt("proj_out.weight")), self._f32("proj_out.bias"))
+        # the tf32 remainders of the tensor-core weights exist before any graph capture
+        for lin in [self.proj_in, self.proj_out] + [l for B in self.blocks for l in (B.qkv, B.out, B.ff1, B.ff2)]:
+            lin.lo()
         self.ff = self.blocks[0].ff1.n
         self._ready = True
 

@@ -5,6 +5,9 @@ Bar: max |got - ref| / max |ref| <= 1e-5 (measured 1.7e-6 at K=1024 and
 ~6e-7 on the same inputs).  Cases grow from one 128x128 tile to
 the DiT's shapes, with row/column tails, K tails and every epilogue.  After
 each case the kernel's error word (bounded-wait expiry) must be clear.
+
+Both entry points run every case: cv3_tc_gemm (B split in the kernel) and
+cv3_tc_gemm_split (B with its cv3_tf32_lo remainder, A streamed into TMEM).
 """
 
 import ctypes
@@ -17,7 +20,10 @@ from conftest import pkg, rel_err
 pytestmark = pytest.mark.gpu
 
 
-def _run(a, b, mode=0, bias=None, gate=None, c0=None, rows_per_group=0):
+KINDS = ["in_kernel_split", "presplit_b"]
+
+
+def _run(a, b, mode=0, bias=None, gate=None, c0=None, rows_per_group=0, kind="in_kernel_split"):
     import torch
     L = pkg("_lib")
     ad, bd = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
@@ -26,9 +32,17 @@ def _run(a, b, mode=0, bias=None, gate=None, c0=None, rows_per_group=0):
     c = torch.from_numpy(c0.copy()).cuda() if c0 is not None else torch.zeros(m, n, device="cuda")
     bb = torch.from_numpy(bias).cuda() if bias is not None else None
     gg = torch.from_numpy(gate).cuda() if gate is not None else None
-    L.call("cv3_tc_gemm", ad.data_ptr(), k, bd.data_ptr(), k, c.data_ptr(), n, m, n, k, mode,
-           bb.data_ptr() if bb is not None else None, gg.data_ptr() if gg is not None else None,
-           rows_per_group, n if gate is not None else 0, torch.cuda.current_stream().cuda_stream)
+    st = torch.cuda.current_stream().cuda_stream
+    bias_p = bb.data_ptr() if bb is not None else None
+    gate_p = gg.data_ptr() if gg is not None else None
+    if kind == "in_kernel_split":
+        L.call("cv3_tc_gemm", ad.data_ptr(), k, bd.data_ptr(), k, c.data_ptr(), n, m, n, k, mode,
+               bias_p, gate_p, rows_per_group, n if gate is not None else 0, st)
+    else:
+        lo = torch.empty_like(bd)
+        L.call("cv3_tf32_lo", bd.data_ptr(), n * k, lo.data_ptr(), st)
+        L.call("cv3_tc_gemm_split", ad.data_ptr(), k, bd.data_ptr(), lo.data_ptr(), k, c.data_ptr(), n, m, n, k,
+               mode, bias_p, gate_p, rows_per_group, n if gate is not None else 0, st)
     torch.cuda.synchronize()
     code = ctypes.c_int()
     L.call("cv3_tc_gemm_status", ctypes.byref(code))
@@ -42,27 +56,62 @@ def _gelu(x):
 
 @pytest.mark.parametrize("m,n,k", [(128, 128, 32), (128, 128, 64), (256, 256, 256), (37, 100, 68),
                                    (1000, 1024, 1024), (10400, 3072, 1024), (10400, 1024, 320),
-                                   (1000, 1024, 2048), (130, 80, 1024)])
-def test_plain_gemm(m, n, k):
+                                   (1000, 1024, 2048), (130, 80, 1024), (300, 200, 4)])
+@pytest.mark.parametrize("kind", KINDS)
+def test_plain_gemm(m, n, k, kind):
     rng = np.random.default_rng(m + n + k)
     a = rng.normal(size=(m, k)).astype(np.float32)
     b = (rng.normal(size=(n, k)) * 0.02).astype(np.float32)
     ref = a.astype(np.float64) @ b.astype(np.float64).T
-    assert rel_err(_run(a, b), ref) < 1e-5
+    assert rel_err(_run(a, b, kind=kind), ref) < 1e-5
 
 
-def test_epilogues():
+def test_tf32_lo_is_the_exact_remainder():
+    import torch
+    rng = np.random.default_rng(3)
+    x = np.concatenate([rng.normal(size=5000), [0.0, -0.0, 1e-38, -3e38, 1.0, -1.0]]).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    lo = torch.empty_like(xd)
+    pkg("_lib").call("cv3_tf32_lo", xd.data_ptr(), x.size, lo.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    hi = (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    assert np.array_equal(lo.cpu().numpy().view(np.uint32), (x - hi).view(np.uint32))
+
+
+def test_presplit_strided_operands():
+    """A with lda > k and C with ldc > n (column slices of wider buffers)."""
+    import torch
+    L = pkg("_lib")
+    rng = np.random.default_rng(11)
+    m, n, k, lda, ldc = 333, 200, 512, 600, 260
+    abuf = rng.normal(size=(m, lda)).astype(np.float32)
+    b = (rng.normal(size=(n, k)) * 0.05).astype(np.float32)
+    ad, bd = torch.from_numpy(abuf).cuda(), torch.from_numpy(b).cuda()
+    cd = torch.full((m, ldc), 7.0, device="cuda")
+    lo = torch.empty_like(bd)
+    st = torch.cuda.current_stream().cuda_stream
+    L.call("cv3_tf32_lo", bd.data_ptr(), n * k, lo.data_ptr(), st)
+    L.call("cv3_tc_gemm_split", ad.data_ptr(), lda, bd.data_ptr(), lo.data_ptr(), k, cd.data_ptr(), ldc, m, n, k,
+           0, None, None, 0, 0, st)
+    torch.cuda.synchronize()
+    got = cd.cpu().numpy()
+    ref = abuf[:, :k].astype(np.float64) @ b.astype(np.float64).T
+    assert rel_err(got[:, :n], ref) < 1e-5
+    assert np.all(got[:, n:] == 7.0)
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_epilogues(kind):
     rng = np.random.default_rng(7)
     m, n, k = 650, 2048, 1024
     a = rng.normal(size=(m, k)).astype(np.float32)
     b = (rng.normal(size=(n, k)) * 0.02).astype(np.float32)
     bias = rng.normal(size=n).astype(np.float32)
     y = a.astype(np.float64) @ b.astype(np.float64).T + bias
-    assert rel_err(_run(a, b, 0, bias), y) < 1e-5
-    assert rel_err(_run(a, b, 1, bias), _gelu(y)) < 1e-5
+    assert rel_err(_run(a, b, 0, bias, kind=kind), y) < 1e-5
+    assert rel_err(_run(a, b, 1, bias, kind=kind), _gelu(y)) < 1e-5
     h = rng.normal(size=(m, n)).astype(np.float32)
     gate = rng.normal(size=(2, n)).astype(np.float32)
     rows = 325
     ref = h + np.repeat(gate, rows, axis=0) * y
-    assert rel_err(_run(a, b, 2, bias, gate, h, rows_per_group=rows), ref) < 1e-5
-    assert rel_err(_run(a, b, 3, bias, None, h), h + y) < 1e-5
+    assert rel_err(_run(a, b, 2, bias, gate, h, rows_per_group=rows, kind=kind), ref) < 1e-5
+    assert rel_err(_run(a, b, 3, bias, None, h, kind=kind), h + y) < 1e-5
