@@ -258,11 +258,12 @@ int make_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int
 // Pre-split variant (the DiT's linears).  B comes with its tf32 remainder
 // b_lo = b - tf32(b) (made once per weight matrix by cv3_tf32_lo); the raw B
 // is the hi operand, since kind::tf32 reads only the top 19 bits of each
-// fp32.  A never touches shared memory: the four converter warps stream their
-// rows from global memory (two K blocks in flight per thread), split them and
-// write hi/lo straight into TMEM, and the MMAs take A from TMEM.  Shared
-// memory then only carries B (TMA writes + MMA reads, ~104 B/clk at the
-// tensor rate, under the 128 B/clk the SM has).
+// fp32.  A, B and B lo arrive by TMA in one 4-stage ring; the four converter
+// warps read their A row (one row per thread = its TMEM lane) from the
+// swizzled stage, split it and write hi/lo into TMEM, and the MMAs take A
+// from TMEM, so shared memory carries A once each way and B to the tensor
+// core.  A stage is free again when its A has been read (converters) and its
+// B consumed (MMA commit).
 // TMEM: two K-range accumulators for hi*hi, one for the cross terms (the
 // tensor core truncates when it accumulates, so long sums lose bits; this
 // layout measured 1.7e-6 / 2.9e-6 of max at K = 1024 / 2048 vs fp64) and two
@@ -270,33 +271,26 @@ int make_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int
 // ---------------------------------------------------------------------------
 namespace split {
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 5;
-constexpr int TILE_B = BN * BK * 4;      // 16 KB
-constexpr int STAGE_BYTES = 2 * TILE_B;  // raw B | B lo
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 4;
+constexpr int TILE_A = BM * BK * 4;               // 16 KB
+constexpr int TILE_B = BN * BK * 4;               // 16 KB
+constexpr int STAGE_BYTES = TILE_A + 2 * TILE_B;  // A | raw B | B lo
 constexpr int THREADS = 192;
 constexpr uint32_t C_MAIN0 = 0, C_MAIN1 = 128, C_CROSS = 256, C_A = 384;
 constexpr uint32_t IDESC = idesc_tf32(BM, BN);
 
 struct Bars {
-  uint64_t bfull[STAGES], bempty[STAGES], afull[2], aempty[2], acc;
+  uint64_t full[STAGES], empty[STAGES], afull[2], aempty[2], acc;
   uint32_t tmem;
   int abort_flag;
   int issued[STAGES];
 };
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + (int)sizeof(Bars);
 
-__device__ __forceinline__ void load_a(float4 (&dst)[8], const float* arow, bool live, int c0, int K) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int c = c0 + 4 * j;
-    dst[j] = (live && c < K) ? __ldg(reinterpret_cast<const float4*>(arow + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-}
-
 __global__ void __launch_bounds__(THREADS, 1)
-tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_blo,
-                     const float* __restrict__ A, int64_t lda, int M, int N, int K, float* __restrict__ C, int64_t ldc,
-                     Epi ep) {
+tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_blo, int M, int N, int K, float* __restrict__ C,
+                     int64_t ldc, Epi ep) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars& S = *reinterpret_cast<Bars*>(smem + STAGES * STAGE_BYTES);
@@ -308,8 +302,8 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_con
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&S.bfull[s], 1);
-      mbar_init(&S.bempty[s], 1);
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 5);  // MMA commit + four converter warps
       S.issued[s] = -1;
     }
     for (int i = 0; i < 2; ++i) {
@@ -340,15 +334,16 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_con
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % STAGES;
         const uint32_t r = (uint32_t)(kb / STAGES);
-        if (*abort_flag || !mbar_wait(&S.bempty[s], (r & 1) ^ 1, 21)) {
+        if (*abort_flag || !mbar_wait(&S.empty[s], (r & 1) ^ 1, 21)) {
           *abort_flag = 1;
           break;
         }
         uint8_t* st = smem + s * STAGE_BYTES;
         S.issued[s] = (int)r;
-        mbar_expect_tx(&S.bfull[s], STAGE_BYTES);
-        tma_load_2d(st, &map_b, &S.bfull[s], kb * BK, n0);
-        tma_load_2d(st + TILE_B, &map_blo, &S.bfull[s], kb * BK, n0);
+        mbar_expect_tx(&S.full[s], STAGE_BYTES);
+        tma_load_2d(st, &map_a, &S.full[s], kb * BK, m0);
+        tma_load_2d(st + TILE_A, &map_b, &S.full[s], kb * BK, n0);
+        tma_load_2d(st + TILE_A + TILE_B, &map_blo, &S.full[s], kb * BK, n0);
       }
     }
   } else if (warp == 1) {
@@ -357,7 +352,7 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_con
       const int s = kb % STAGES;
       const uint32_t r = (uint32_t)(kb / STAGES);
       const int a = kb & 1;
-      if (!ready(&S.bfull[s], r & 1, 22) || !ready(&S.afull[a], (uint32_t)(kb >> 1) & 1, 23)) {
+      if (!ready(&S.full[s], r & 1, 22) || !ready(&S.afull[a], (uint32_t)(kb >> 1) & 1, 23)) {
         ok = false;
         break;
       }
@@ -365,7 +360,7 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_con
       const int chunk = (nk >= 2 && kb >= half) ? 1 : 0;
       const int chunk_first = chunk ? half : 0;
       const uint32_t d_main = tmem + (chunk ? C_MAIN1 : C_MAIN0), d_cross = tmem + C_CROSS;
-      const uint32_t b_raw = smem_u32(smem + s * STAGE_BYTES), b_lo = b_raw + TILE_B;
+      const uint32_t b_raw = smem_u32(smem + s * STAGE_BYTES + TILE_A), b_lo = b_raw + TILE_B;
       const uint32_t a_hi = tmem + C_A + 64u * a, a_lo = a_hi + 32;
 #pragma unroll
       for (int kk = 0; kk < BK / 8; ++kk) {
@@ -374,7 +369,7 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_con
         mma_ts(d_cross, a_hi + 8 * kk, desc_k_sw128(b_lo + off), IDESC, 1u);
         mma_ts(d_main, a_hi + 8 * kk, desc_k_sw128(b_raw + off), IDESC, (kb == chunk_first && kk == 0) ? 0u : 1u);
       }
-      mma_commit(&S.bempty[s]);
+      mma_commit(&S.empty[s]);
       mma_commit(&S.aempty[a]);
     }
     if (!ok && lane == 0) *abort_flag = 1;
@@ -385,48 +380,45 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_con
     const int row = quarter * 32 + lane;
     const int grow = m0 + row;
     const bool live = grow < M;
-    const float* arow = A + (int64_t)(live ? grow : 0) * lda;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
-    float4 x0[8], x1[8];
-    if (nk > 0) load_a(x0, arow, live, 0, K);
-    if (nk > 1) load_a(x1, arow, live, BK, K);
-    // split K block kb (held in x) into stage kb & 1 once the MMAs of kb - 2 are done
-#define CV3_PUT_A(xb, kb_)                                                                     \
-  {                                                                                           \
-    const int kbv = (kb_);                                                                    \
-    const int a_ = kbv & 1;                                                                   \
-    if (!ready(&S.aempty[a_], ((uint32_t)(kbv >> 1) & 1) ^ 1, 24)) {                           \
-      ok = false;                                                                             \
-    } else {                                                                                  \
-      float hi[32], lo[32];                                                                   \
-      _Pragma("unroll") for (int j = 0; j < 8; ++j) {                                         \
-        const float e4[4] = {xb[j].x, xb[j].y, xb[j].z, xb[j].w};                             \
-        _Pragma("unroll") for (int e = 0; e < 4; ++e) {                                       \
-          hi[4 * j + e] = tf32_hi(e4[e]);                                                     \
-          lo[4 * j + e] = e4[e] - hi[4 * j + e];                                              \
-        }                                                                                     \
-      }                                                                                       \
-      fence_after();                                                                          \
-      tmem_st32(tmem + lane_base + C_A + 64u * a_, hi);                                       \
-      tmem_st32(tmem + lane_base + C_A + 64u * a_ + 32, lo);                                  \
-      tmem_st_wait();                                                                         \
-      fence_before();                                                                         \
-      __syncwarp();                                                                           \
-      if (lane == 0) mbar_arrive(&S.afull[a_]);                                               \
-    }                                                                                         \
-  }
-    for (int kb = 0; ok && kb < nk; kb += 2) {
-      CV3_PUT_A(x0, kb);
-      if (ok && kb + 2 < nk) load_a(x0, arow, live, (kb + 2) * BK, K);
-      if (ok && kb + 1 < nk) {
-        CV3_PUT_A(x1, kb + 1);
-        if (ok && kb + 3 < nk) load_a(x1, arow, live, (kb + 3) * BK, K);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      const int a = kb & 1;
+      if (!ready(&S.full[s], (uint32_t)(kb / STAGES) & 1, 24)) {
+        ok = false;
+        break;
       }
+      // this thread's row of the swizzled A tile: 16-byte chunk j sits at chunk j ^ (row % 8);
+      // a quarter-warp reads eight rows' chunks from eight distinct bank groups
+      const uint8_t* arow = smem + s * STAGE_BYTES + row * 128;
+      float hi[32], lo[32];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 x = *reinterpret_cast<const float4*>(arow + ((j ^ (row & 7)) << 4));
+        const float e4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          hi[4 * j + e] = tf32_hi(e4[e]);
+          lo[4 * j + e] = e4[e] - hi[4 * j + e];
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.empty[s]);  // this warp's rows of the stage are read
+      if (!ready(&S.aempty[a], ((uint32_t)(kb >> 1) & 1) ^ 1, 25)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      tmem_st32(tmem + lane_base + C_A + 64u * a, hi);
+      tmem_st32(tmem + lane_base + C_A + 64u * a + 32, lo);
+      tmem_st_wait();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.afull[a]);
     }
-#undef CV3_PUT_A
     if (!ok) *abort_flag = 1;
-    ok = ok && ready(&S.acc, 0, 25);
+    ok = ok && ready(&S.acc, 0, 26);
     fence_after();
     if (ok) {
       const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
@@ -490,8 +482,8 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_con
     if (lane == 0) {
       if (*abort_flag)
         for (int s = 0; s < STAGES; ++s)
-          if (S.issued[s] >= 0) mbar_wait(&S.bfull[s], (uint32_t)S.issued[s] & 1, 26);
-      mbar_wait(&S.acc, 0, 27);  // every MMA (and its barrier arrivals) finished
+          if (S.issued[s] >= 0) mbar_wait(&S.full[s], (uint32_t)S.issued[s] & 1, 27);
+      mbar_wait(&S.acc, 0, 28);  // every MMA (and its barrier arrivals) finished
     }
     __syncwarp();
     fence_after();
@@ -577,13 +569,14 @@ extern "C" int cv3_tc_gemm_split(const float* a, int64_t lda, const float* b, co
   CV3_REQUIRE(m >= 0 && n >= 0 && k >= 0 && mode >= 0 && mode <= 3, CV3_ERR_VALUE, "tc_gemm_split: bad arguments");
   CV3_REQUIRE(mode != 2 || gate != nullptr, CV3_ERR_VALUE, "tc_gemm_split: gated residual needs a gate");
   CV3_REQUIRE(lda >= k && ldb >= k && ldc >= n, CV3_ERR_VALUE, "tc_gemm_split: leading dimension too small");
-  CV3_REQUIRE(k % 4 == 0 && lda % 4 == 0 && ((uintptr_t)a & 15) == 0, CV3_ERR_VALUE,
-              "tc_gemm_split: K, lda and the A base must allow 16-byte row loads");
+  CV3_REQUIRE(k % 4 == 0, CV3_ERR_VALUE, "tc_gemm_split: K must be a multiple of 4 (16-byte rows)");
   if (m == 0 || n == 0) return CV3_OK;
   CV3_REQUIRE(k > 0 && b_lo != nullptr, CV3_ERR_VALUE, "tc_gemm_split: K must be positive and b_lo given");
   CV3_REQUIRE(m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31), CV3_ERR_VALUE, "tc_gemm_split: too large");
-  CUtensorMap mb, mbl;
-  int rc = make_map(&mb, b, n, k, ldb, split::BN);
+  CUtensorMap ma, mb, mbl;
+  int rc = make_map(&ma, a, m, k, lda, split::BM);
+  if (rc) return rc;
+  rc = make_map(&mb, b, n, k, ldb, split::BN);
   if (rc) return rc;
   rc = make_map(&mbl, b_lo, n, k, ldb, split::BN);
   if (rc) return rc;
@@ -593,6 +586,6 @@ extern "C" int cv3_tc_gemm_split(const float* a, int64_t lda, const float* b, co
   CV3_REQUIRE(grid.y <= 65535, CV3_ERR_VALUE, "tc_gemm_split: too many row tiles");
   Epi ep{1, 1, mode, bias, gate, rows_per_group, gate_stride};
   split::tc_gemm_split_kernel<<<grid, split::THREADS, split::SMEM_BYTES, cv3::as_stream(stream)>>>(
-      mb, mbl, a, lda, (int)m, (int)n, (int)k, c, ldc, ep);
+      ma, mb, mbl, (int)m, (int)n, (int)k, c, ldc, ep);
   return cv3::check_launch("tc_gemm_split");
 }
