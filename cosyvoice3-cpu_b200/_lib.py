@@ -68,6 +68,10 @@ SIGNATURES = {
     "cv3_tf32_lo": [P, I64, P, P],
     "cv3_tc_gemm_split": [P, I64, P, P, I64, P, I64, I64, I64, I64, I32, P, P, I64, I64, P],
     "cv3_tc_attention_status": [P],
+    "cv3_conv_weight_tc": [P, I64, I64, I64, I64, P, P, P],
+    "cv3_conv1d_tc": [P, I64, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, I64, I64, I64, P, I32, F, P,
+                      P, P, I64, I64, I64, I64, P],
+    "cv3_tc_conv_status": [P],
     "cv3_q8_decode_gemv": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
     "cv3_tc_gemm_cfg": [P, I64, P, I64, P, I64, I64, I64, I64, I32, P, P, I64, I64, I32, I32, P],
 }

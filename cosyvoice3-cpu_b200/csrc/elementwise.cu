@@ -6,36 +6,6 @@
 
 namespace {
 
-__device__ __forceinline__ float act_apply(int act, float p, float x) {
-  switch (act) {
-    case CV3_ACT_SILU: return x / (1.0f + expf(-x));
-    case CV3_ACT_SIGMOID: return 1.0f / (1.0f + expf(-x));
-    case CV3_ACT_GELU_TANH: {
-      const float c = 0.7978845608028654f;  // sqrt(2/pi)
-      const float inner = x + 0.044715f * x * x * x;
-      return 0.5f * x * (1.0f + tanhf(c * inner));
-    }
-    case CV3_ACT_GELU_ERF: {
-      // Abramowitz & Stegun 7.1.26 erf, as the reference evaluates it.
-      const float z = x / 1.4142135623730951f;
-      const float a = fabsf(z);
-      const float t = 1.0f / (1.0f + 0.3275911f * a);
-      const float poly = ((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
-                         0.254829592f;
-      const float e = copysignf(1.0f - poly * t * expf(-a * a), z);
-      return 0.5f * x * (1.0f + (z == 0.f ? 0.f : e));
-    }
-    case CV3_ACT_MISH: {
-      const float sp = x > 20.0f ? x : log1pf(expf(fminf(x, 20.0f)));
-      return x * tanhf(sp);
-    }
-    case CV3_ACT_ELU: return x > 0.f ? x : p * expm1f(fminf(x, 0.f));
-    case CV3_ACT_LEAKY_RELU: return x >= 0.f ? x : x * p;
-    case CV3_ACT_TANH: return tanhf(x);
-    case CV3_ACT_EXP: return expf(x);
-  }
-  return x;
-}
 
 __global__ void unary_kernel(int act, float p, const float* __restrict__ x, int64_t n, float* __restrict__ y) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)

@@ -83,6 +83,47 @@ class Lin:
              self.bias, gate, rows_per_group, gate_stride, s)
 
 
+class ConvTC:
+    """A conv1d weight in the tensor-core layout (``cv3_conv_weight_tc``): Wt[C_out][k][ci_pad]
+    plus the tf32 remainder when the weight is not exactly tf32 (fp16-stored weights are)."""
+
+    __slots__ = ("wt", "lo", "cout", "cin_g", "k", "groups", "ci_pad", "bias")
+
+    def __init__(self, w, bias=None, groups: int = 1, stream=None):
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("ConvTC: weights must be rearranged before stream capture")
+        self.cout, self.cin_g, self.k = (int(v) for v in w.shape)
+        self.groups = int(groups)
+        self.ci_pad = (self.cin_g + 31) // 32 * 32
+        s = stream if stream is not None else D.stream()
+        self.wt = D.empty((self.cout, self.k, self.ci_pad))
+        lo = D.empty((self.cout, self.k, self.ci_pad))
+        w = w.contiguous()
+        call("cv3_conv_weight_tc", w.data_ptr(), self.cout, self.cin_g, self.k, self.ci_pad, self.wt.data_ptr(),
+             lo.data_ptr(), s)
+        self.lo = lo if bool(torch.count_nonzero(lo)) else None
+        self.bias = bias
+
+    def __call__(self, x, y, batch: int, t_in: int, t_out: int, stride: int = 1, dilation: int = 1,
+                 pad_left: int = 0, residual=None, xs=None, ys=None, act: int = -1, act_param: float = 0.0,
+                 snake_alpha=None, stream=None):
+        """x, y device tensors (or pointers with explicit strides ``xs``/``ys`` = (s_b, s_c, s_t));
+        default strides are channel-major [batch][C][T].  Epilogue: bias, ``act`` (CV3_ACT_*),
+        snake with per-channel ``snake_alpha``, + ``residual``."""
+        s = stream if stream is not None else D.stream()
+        cin, cout = self.cin_g * self.groups, self.cout
+        xs = xs if xs is not None else (cin * t_in, t_in, 1)
+        ys = ys if ys is not None else (cout * t_out, t_out, 1)
+        xp = x if isinstance(x, int) else x.data_ptr()
+        yp = y if isinstance(y, int) else y.data_ptr()
+        rp = residual if (residual is None or isinstance(residual, int)) else residual.data_ptr()
+        call("cv3_conv1d_tc", xp, xs[0], xs[1], xs[2], batch, cin, t_in, self.wt.data_ptr(),
+             self.lo.data_ptr() if self.lo is not None else None, self.ci_pad, cout, self.k, stride, dilation,
+             self.groups, pad_left, self.bias.data_ptr() if self.bias is not None else None, int(act),
+             float(act_param), snake_alpha.data_ptr() if snake_alpha is not None else None, rp, yp,
+             ys[0], ys[1], ys[2], t_out, s)
+
+
 class DecodeGemv:
     """A q8 weight streamed by ``cv3_q8_decode_gemv`` for <= 8 activation rows.
 

@@ -21,7 +21,7 @@ import numpy as np
 from .. import _dev as D
 from .._lib import call
 from ..quant import QTensor
-from ._common import TC_MIN_ROWS, Lin, cat_rows, f32_of
+from ._common import TC_MIN_ROWS, Lin, cat_rows, f32_of, ConvTC
 
 torch = D.torch
 
@@ -59,7 +59,6 @@ class Workspace:
         self.a = D.empty((R, dim))
         self.y = D.empty((R, dim))
         self.f1 = D.empty((R, ff))
-        self.c1 = D.empty((B, dim, N))
         self.c2 = D.empty((B, dim, N))
         self.out = D.empty((R, mel))
 
@@ -104,6 +103,7 @@ class DiT:
         self.proj_in = Lin(self._dense(["input_embed.proj.weight"]), self._f32("input_embed.proj.bias"))
         self.conv = [(self._f32(f"input_embed.conv_pos_embed.{c}.0.weight"),
                       self._f32(f"input_embed.conv_pos_embed.{c}.0.bias")) for c in ("conv1", "conv2")]
+        self.conv_tc = [ConvTC(w, b, groups=self.conv_pos_groups) for w, b in self.conv]
         # all AdaLN projections read silu(temb): one stacked matrix, one GEMV per step
         names = [f"transformer_blocks.{i}.attn_norm.linear.weight" for i in range(self.depth)] + \
                 ["norm_out.linear.weight"]
@@ -161,13 +161,14 @@ class DiT:
         F = 4
         # input embedding + grouped causal conv position embedding (dit.py:92-112)
         self.proj_in(ws.cat.data_ptr(), R, ws.h.data_ptr(), stream=st)
-        call("cv3_transpose", ws.h.data_ptr(), B, N, d, ws.c1.data_ptr(), 0, st)
+        # h += mish(conv2(mish(conv1(h)))): token-major in and out, mish and the residual in
+        # the conv epilogues (no transposes)
         k = self.conv_pos_kernel
-        for (w, b), (src, dst) in zip(self.conv, ((ws.c1, ws.c2), (ws.c2, ws.c1))):
-            call("cv3_conv1d", src.data_ptr(), B, d, N, w.data_ptr(), d, k, 1, 1, self.conv_pos_groups, k - 1, 0,
-                 b.data_ptr(), dst.data_ptr(), N, st)
-            call("cv3_unary", 4, 0.0, dst.data_ptr(), dst.numel(), dst.data_ptr(), st)
-        call("cv3_transpose", ws.c1.data_ptr(), B, d, N, ws.h.data_ptr(), 1, st)
+        tm = (N * d, 1, d)
+        c1, c2 = self.conv_tc
+        c1(ws.h.data_ptr(), ws.c2.data_ptr(), B, N, N, pad_left=k - 1, xs=tm, ys=tm, act=4, stream=st)
+        c2(ws.c2.data_ptr(), ws.h.data_ptr(), B, N, N, pad_left=k - 1, xs=tm, ys=tm, act=4,
+           residual=ws.h.data_ptr(), stream=st)
         cos, sin = self.rope(N)
         scale = float(np.float32(1.0 / math.sqrt(self.dim_head)))
         mk, ma, mb = (2, self.static_chunk_size, self.num_decoding_left_chunks) if streaming else (0, 0, 0)

@@ -21,6 +21,7 @@ import numpy as np
 from .. import _dev as D
 from .. import ops
 from .._lib import call
+from ._common import ConvTC
 
 torch = D.torch
 
@@ -57,6 +58,7 @@ class HiFTGenerator:
         self.upsample_scale = int(np.prod(self.upsample_rates)) * self.hop_len
         self.window = ops.hann_window(self.n_fft)
         self._win = None
+        self._convs = {}
         self.noise_seed = int(m.get("noise_seed", 0))
         self._src_noise = None
         self._user_noise = False
@@ -77,16 +79,20 @@ class HiFTGenerator:
         return self._win
 
     # -- convolution helper ---------------------------------------------------------
-    def _conv(self, x, name, stride=1, dilation=1, pad=(0, 0)):
-        w = self._t(name + ".weight")
-        b = self._t(name + ".bias")
+    def _conv(self, x, name, stride=1, dilation=1, pad=(0, 0), act=-1, act_param=0.0, snake=None,
+              residual=None):
+        """Tensor-core conv (implicit GEMM) with the elementwise op after it fused into the
+        epilogue: activation ``act``, snake with the alphas named ``snake``, + ``residual``."""
+        cv = self._convs.get(name)
+        if cv is None:
+            cv = ConvTC(self._t(name + ".weight"), self._t(name + ".bias"))
+            self._convs[name] = cv
         B, cin, T = (int(s) for s in x.shape)
-        cout, _, k = (int(s) for s in w.shape)
-        span = dilation * (k - 1) + 1
+        span = dilation * (cv.k - 1) + 1
         t_out = (T + pad[0] + pad[1] - span) // stride + 1
-        y = D.empty((B, cout, t_out))
-        call("cv3_conv1d", x.data_ptr(), B, cin, T, w.data_ptr(), cout, k, stride, dilation, 1, pad[0], pad[1],
-             b.data_ptr(), y.data_ptr(), t_out, D.stream())
+        y = D.empty((B, cv.cout, t_out))
+        cv(x, y, B, T, t_out, stride=stride, dilation=dilation, pad_left=pad[0], residual=residual, act=act,
+           act_param=act_param, snake_alpha=self._t(snake) if snake is not None else None)
         return y
 
     @staticmethod
@@ -117,7 +123,7 @@ class HiFTGenerator:
             name = f"f0_predictor.condnet.{i}"
             k = self._k(name + ".weight")
             pad = (0, causal_pad(k)) if i == 0 else (causal_pad(k), 0)
-            x = self._unary(self._conv(x, name, pad=pad), 5, 1.0)
+            x = self._conv(x, name, pad=pad, act=5, act_param=1.0)
         B, C, T = (int(s) for s in x.shape)
         f0 = D.empty((B, T))
         call("cv3_f0_classifier", x.data_ptr(), B, C, T, self._f64("f0_predictor.classifier.weight").data_ptr(),
@@ -158,19 +164,21 @@ class HiFTGenerator:
         base = f"{group}.{idx}."
         for j, d in enumerate(dilations):
             xt = self._snake(x, base + f"activations1.{j}.alpha")
-            xt = self._conv(xt, base + f"convs1.{j}", dilation=d, pad=(causal_pad(kernel, d), 0))
-            xt = self._snake(xt, base + f"activations2.{j}.alpha")
-            xt = self._conv(xt, base + f"convs2.{j}", pad=(causal_pad(kernel, 1), 0))
-            x = self._bin(xt, x, 0)
+            xt = self._conv(xt, base + f"convs1.{j}", dilation=d, pad=(causal_pad(kernel, d), 0),
+                            snake=base + f"activations2.{j}.alpha")
+            x = self._conv(xt, base + f"convs2.{j}", pad=(causal_pad(kernel, 1), 0), residual=x)
         return x
 
     def spectral(self, mel, s_stft):
         """``[B, 80, T]``, ``[B, 18, 120T+1]`` -> ``[B, n_fft+2, 120T+1]`` (hift.py:131-168)."""
-        x = self._conv(mel, "conv_pre", pad=(0, causal_pad(self._k("conv_pre.weight"))))
+        # conv_pre's output only feeds the first leaky ReLU: fused into its epilogue
+        x = self._conv(mel, "conv_pre", pad=(0, causal_pad(self._k("conv_pre.weight"))), act=6,
+                       act_param=self.lrelu_slope)
         down_rates = [1] + self.upsample_rates[::-1][:-1]
         down_cum = list(np.cumprod(down_rates))[::-1]
         for i in range(self.num_upsamples):
-            x = self._unary(x, 6, self.lrelu_slope)
+            if i > 0:
+                x = self._unary(x, 6, self.lrelu_slope)
             x = ops.interpolate_nearest(x, self.upsample_rates[i])
             k = self._k(f"ups.{i}.weight")
             x = self._conv(x, f"ups.{i}", pad=(k - 1, 0))

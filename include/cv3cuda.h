@@ -382,6 +382,30 @@ int cv3_tc_gemm_split(const float* a, int64_t lda, const float* b, const float* 
                       int64_t ldc, int64_t m, int64_t n, int64_t k, int mode, const float* bias, const float* gate,
                       int64_t rows_per_group, int64_t gate_stride, void* stream);
 
+/* Rearrange conv weights W[C_out][C_in/groups][k] into the tensor-core
+ * layout Wt[C_out][k][ci_pad] (ci_pad = C_in/groups rounded up to 32, zero
+ * filled) and, if wt_lo is not NULL, the tf32 remainders.  Done once per
+ * weight; weights that are exact tf32 values (fp16-stored) need no remainder. */
+int cv3_conv_weight_tc(const float* w, int64_t cout, int64_t cin_g, int64_t k, int64_t ci_pad, float* wt,
+                       float* wt_lo, void* stream);
+
+/* cv3_conv1d on the tensor cores (implicit GEMM, tcgen05, 3xTF32 -- 2 products
+ * when wt_lo is NULL).  x and y are strided: element (b, c, t) at
+ * b*s_b + c*s_c + t*s_t, so channel-major and token-major signals are read and
+ * written in place; inputs outside [0, t_in) count as zero padding (t_out sets
+ * the right pad).  Epilogue, in order: + bias, activation `act` (-1 none,
+ * CV3_ACT_MISH, _ELU or _LEAKY_RELU; parameter act_param), snake with per-output-channel snake_alpha
+ * (NULL none; cv3cpu/models/hift.py Snake), + residual (y's strides, may alias
+ * y).  Replaces cv3cpu/ops.py:165-219 (conv1d) and the elementwise ops after it. */
+int cv3_conv1d_tc(const float* x, int64_t xsb, int64_t xsc, int64_t xst, int64_t batch, int64_t cin, int64_t t_in,
+                  const float* wt, const float* wt_lo, int64_t ci_pad, int64_t cout, int64_t k, int64_t stride,
+                  int64_t dilation, int64_t groups, int64_t pad_left, const float* bias, int act, float act_param,
+                  const float* snake_alpha, const float* residual, float* y, int64_t ysb, int64_t ysc, int64_t yst,
+                  int64_t t_out, void* stream);
+
+/* Error word of the tensor-core conv kernel (see cv3_tc_gemm_status). */
+int cv3_tc_conv_status(int* code);
+
 /* Error word of the tensor-core kernels (0 = none; else the code of the
  * first bounded wait that expired), read and cleared.  Synchronises. */
 int cv3_tc_gemm_status(int* code);

@@ -1,0 +1,121 @@
+"""Tensor-core conv1d (cv3_conv1d_tc) against the oracle's conv1d and activations.
+
+The kernel is an implicit GEMM on tcgen05 with 3xTF32 products (two when the
+weight is an exact tf32 value, as the vocoder's fp16-stored weights are).
+Cases: the vocoder's resblock / upsample / source-down geometries (dilation,
+stride, causal left pads), the DiT's grouped k=31 position conv in token-major
+layout, input-channel counts that are not multiples of 32, short signals, and
+each fused epilogue (activation, snake, residual in place).  Bar: max |got -
+ref| / max |ref| <= 1e-5, the fp32 bar; the error word must stay clear.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import pkg, rel_err
+
+import oracle.numerics as nx
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def _conv_tc(x, w, bias, stride=1, dilation=1, groups=1, pad=(0, 0), act=-1, act_p=0.0, alpha=None,
+             residual=None, token_major=False, fp16_weights=False):
+    """Run the device conv on host arrays x (B, C_in, T); returns (B, C_out, T_out)."""
+    import torch
+    common = pkg("models._common")
+    B, cin, T = x.shape
+    cout, cin_g, k = w.shape
+    span = dilation * (k - 1) + 1
+    t_out = (T + pad[0] + pad[1] - span) // stride + 1
+    wd = torch.from_numpy(w).cuda()
+    bd = torch.from_numpy(bias).cuda() if bias is not None else None
+    cv = common.ConvTC(wd, bd, groups=groups)
+    assert (cv.lo is None) == fp16_weights
+    if token_major:
+        xd = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 2, 1))).cuda()
+        xs = (T * cin, 1, cin)
+        y = torch.from_numpy(np.ascontiguousarray(residual.transpose(0, 2, 1))).cuda() if residual is not None \
+            else torch.full((B, t_out, cout), float("nan"), device="cuda")
+        ys = (t_out * cout, 1, cout)
+    else:
+        xd = torch.from_numpy(x).cuda()
+        xs = (cin * T, T, 1)
+        y = torch.from_numpy(residual.copy()).cuda() if residual is not None \
+            else torch.full((B, cout, t_out), float("nan"), device="cuda")
+        ys = (cout * t_out, t_out, 1)
+    ad = torch.from_numpy(alpha).cuda() if alpha is not None else None
+    cv(xd, y, B, T, t_out, stride=stride, dilation=dilation, pad_left=pad[0],
+       residual=y if residual is not None else None, xs=xs, ys=ys, act=act, act_param=act_p, snake_alpha=ad)
+    torch.cuda.synchronize()
+    code = ctypes.c_int(-1)
+    assert pkg("_lib").load().cv3_tc_conv_status(ctypes.byref(code)) == 0 and code.value == 0
+    out = y.cpu().numpy()
+    return out.transpose(0, 2, 1) if token_major else out
+
+
+def _ref(x, w, bias, stride=1, dilation=1, groups=1, pad=(0, 0)):
+    return np.stack([nx.conv1d(xb, w, bias, stride=stride, dilation=dilation, groups=groups, pad=pad) for xb in x])
+
+
+def _data(rng, B, cin, T, cout, cin_g, k, fp16=False):
+    x = rng.normal(size=(B, cin, T)).astype(np.float32)
+    w = (rng.normal(size=(cout, cin_g, k)) / np.sqrt(cin_g * k)).astype(np.float32)
+    if fp16:
+        w = w.astype(np.float16).astype(np.float32)
+    b = (rng.normal(size=cout) * 0.1).astype(np.float32)
+    return x, w, b
+
+
+@pytest.mark.parametrize("B,cin,T,cout,k,stride,dil,pad,fp16", [
+    (2, 256, 300, 256, 7, 1, 3, (18, 0), True),     # resblock conv, dilated, causal pad
+    (2, 128, 700, 128, 11, 1, 5, (50, 0), True),
+    (1, 64, 1000, 64, 3, 1, 1, (2, 0), True),       # BN = 64 tile
+    (2, 80, 120, 512, 5, 1, 1, (0, 4), False),      # conv_pre: 80 channels (not a multiple of 32), right pad
+    (2, 18, 601, 256, 14, 5, 1, (4, 0), True),      # strided source down-sampling
+    (1, 512, 50, 80, 7, 1, 1, (6, 0), False),       # few frames, C_out not a tile multiple
+    (3, 96, 129, 200, 1, 1, 1, (0, 0), False),      # 1x1, ragged frames and channels
+])
+def test_conv_tc_channel_major(B, cin, T, cout, k, stride, dil, pad, fp16):
+    rng = np.random.default_rng(cin * 7 + T)
+    x, w, b = _data(rng, B, cin, T, cout, cin, k, fp16)
+    got = _conv_tc(x, w, b, stride, dil, 1, pad, fp16_weights=fp16)
+    assert rel_err(got, _ref(x, w, b, stride, dil, 1, pad)) < TOL
+
+
+def test_conv_tc_grouped_token_major_position_conv():
+    """The DiT's conv position embedding: 1024 channels, 16 groups, k = 31, causal pad,
+    token-major (B, T, C) in and out, mish fused, residual added in place."""
+    rng = np.random.default_rng(5)
+    B, C, T, k, g = 2, 1024, 150, 31, 16
+    x, w, b = _data(rng, B, C, T, C, C // g, k)
+    h = rng.normal(size=(B, C, T)).astype(np.float32)
+    got = _conv_tc(x, w, b, groups=g, pad=(k - 1, 0), act=4, residual=h, token_major=True)
+    ref = h + nx.mish(_ref(x, w, b, groups=g, pad=(k - 1, 0)))
+    assert rel_err(got, ref) < TOL
+
+
+@pytest.mark.parametrize("act,p,fn", [(4, 0.0, nx.mish), (5, 1.0, lambda v: nx.elu(v, 1.0)),
+                                      (6, 0.1, lambda v: nx.leaky_relu(v, 0.1))])
+def test_conv_tc_fused_activation(act, p, fn):
+    rng = np.random.default_rng(act)
+    x, w, b = _data(rng, 2, 128, 200, 128, 128, 5)
+    got = _conv_tc(x, w, b, pad=(4, 0), act=act, act_p=p)
+    assert rel_err(got, fn(_ref(x, w, b, pad=(4, 0)))) < TOL
+
+
+def test_conv_tc_snake_and_residual():
+    """resblock: x + conv2(snake(conv1(...))) with the snake after conv1 and the residual fused."""
+    rng = np.random.default_rng(9)
+    x, w, b = _data(rng, 2, 128, 333, 128, 128, 7, fp16=True)
+    alpha = rng.uniform(0.2, 2.0, size=128).astype(np.float32)
+    got = _conv_tc(x, w, b, dilation=3, pad=(18, 0), alpha=alpha, fp16_weights=True)
+    ref = np.stack([nx.snake(r, alpha) for r in _ref(x, w, b, dilation=3, pad=(18, 0))])
+    assert rel_err(got, ref) < TOL
+    res = rng.normal(size=(2, 128, 333)).astype(np.float32)
+    got = _conv_tc(x, w, b, pad=(6, 0), residual=res, fp16_weights=True)
+    assert rel_err(got, res + _ref(x, w, b, pad=(6, 0))) < TOL
