@@ -72,6 +72,8 @@ SIGNATURES = {
     "cv3_conv1d_tc": [P, I64, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, I64, I64, I64, P, I32, F, P,
                       P, P, I64, I64, I64, I64, P],
     "cv3_tc_conv_status": [P],
+    "cv3_decode_steps": [P, P],
+    "cv3_decode_status": [P],
     "cv3_q8_decode_gemv": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
     "cv3_tc_gemm_cfg": [P, I64, P, I64, P, I64, I64, I64, I64, I32, P, P, I64, I64, I32, I32, P],
 }
@@ -107,6 +109,28 @@ def executed_launches() -> int:
     """Kernels of this library executed so far: direct launches plus the kernel
     nodes of every CUDA-graph replay (recording during capture is not execution)."""
     return launch_count() - _graph_books["captured"] + _graph_books["replayed"]
+
+
+class DecodeParams(ctypes.Structure):
+    """``cv3_decode_params`` (include/cv3cuda.h), field for field."""
+    _fields_ = [
+        ("layers", ctypes.c_void_p),
+        ("n_layers", ctypes.c_int32), ("batch", ctypes.c_int32), ("hidden", ctypes.c_int32),
+        ("heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("inter", ctypes.c_int32),
+        ("eps", ctypes.c_float), ("scale", ctypes.c_float),
+        ("cap", ctypes.c_int64),
+        ("cos_table", ctypes.c_void_p), ("sin_table", ctypes.c_void_p), ("final_norm", ctypes.c_void_p),
+        ("head_q", ctypes.c_void_p), ("head_s", ctypes.c_void_p),
+        ("vocab", ctypes.c_int32), ("select", ctypes.c_int32),
+        ("emb", ctypes.c_void_p), ("emb_scales", ctypes.c_void_p), ("emb_rows", ctypes.c_int32),
+        ("h", ctypes.c_void_p), ("q", ctypes.c_void_p), ("attn", ctypes.c_void_p), ("act", ctypes.c_void_p),
+        ("logits", ctypes.c_void_p), ("logp", ctypes.c_void_p),
+        ("pos", ctypes.c_void_p), ("lens", ctypes.c_void_p), ("next_ids", ctypes.c_void_p),
+        ("history", ctypes.c_void_p), ("hist_stride", ctypes.c_int64),
+        ("step", ctypes.c_void_p), ("barrier", ctypes.c_void_p),
+        ("steps", ctypes.c_int32),
+    ]
 
 
 def load(path: str = LIB_PATH) -> ctypes.CDLL:

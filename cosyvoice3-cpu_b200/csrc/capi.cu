@@ -22,9 +22,10 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
-int check_launch(const char* what) {
+int check_launch(const char* what, cudaError_t launch_result) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = launch_result;
   if (e != cudaSuccess) return fail(CV3_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
   return CV3_OK;
 }

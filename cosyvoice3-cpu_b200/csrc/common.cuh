@@ -15,8 +15,9 @@ namespace cv3 {
 // Records a message for cv3_last_error() and returns `code`.
 int fail(int code, const char* fmt, ...);
 
-// Checks the launch that just happened on this thread.
-int check_launch(const char* what);
+// Checks the launch that just happened on this thread (and, for launches made
+// through an API call that returns its own status, that status).
+int check_launch(const char* what, cudaError_t launch_result = cudaSuccess);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

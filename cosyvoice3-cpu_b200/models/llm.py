@@ -153,10 +153,12 @@ class CosyVoice3LM:
         return self._engines[key]
 
     def generate_greedy(self, prompts, n_tokens: int, cap: Optional[int] = None, use_graph: bool = True,
-                        keep_logp: bool = False):
+                        keep_logp: bool = False, persistent: bool = False):
         """Greedy-decode ``n_tokens`` speech tokens for each prompt embedding ``(T_b, H)``.
 
-        Returns the ``[B, n_tokens]`` device tensor of token ids.
+        Returns the ``[B, n_tokens]`` device tensor of token ids.  The decode steps run as one
+        CUDA graph per step (``use_graph``), eager launches, or one persistent cooperative
+        launch (``persistent``, where the model allows it).
         """
         B = len(prompts)
         need = max(int(np.shape(p)[0]) for p in prompts) + n_tokens
@@ -166,4 +168,4 @@ class CosyVoice3LM:
         eng.keep_logp = keep_logp
         if keep_logp and eng.graph is not None:
             eng.graph = None
-        return eng.run(prompts, n_tokens, use_graph=use_graph and not keep_logp)
+        return eng.run(prompts, n_tokens, use_graph=use_graph and not keep_logp, persistent=persistent)

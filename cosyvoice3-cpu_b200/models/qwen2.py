@@ -196,6 +196,10 @@ class Qwen2Model:
         return D.out(out, host)
 
 
+def pk_sm_count() -> int:
+    return int(torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count)
+
+
 class DecodeEngine:
     """Batched greedy decode, one CUDA graph per step.
 
@@ -253,6 +257,66 @@ class DecodeEngine:
                 self.fast.append(None)
         self.fast_head = DecodeGemv(head_w, norm_w=model.norm_w(), eps=c.rms_norm_eps) \
             if isinstance(head_w, QTensor) else None
+        self._mk = self._persistent_setup()
+
+    # -- persistent decode (cv3_decode_steps): every step of a run in one launch ----------
+    def _persistent_setup(self):
+        """Parameter block of the persistent decode kernel, or None where it does not apply
+        (a layer or the head not q8, head dim != 64, more than 8 sequences)."""
+        from .. import _lib
+        c, B = self.c, self.B
+        hid = c.hidden_size
+        e = self.emb
+        if (B > 8 or c.head_dim != 64 or hid != c.num_attention_heads * 64 or hid % 64 or c.intermediate_size % 64
+                or self.fast_head is None or any(F is None for F in self.fast)
+                or any(g.kp != g.k for F in self.fast for g in F) or self.fast_head.kp != hid
+                or (isinstance(e, QTensor) and e.padded_k != hid)):
+            return None
+        ptrs = []
+        for i, F in enumerate(self.fast):
+            kc, vc = self.cache.layer_ptrs(i)
+            qkv, o, gu, dn = F
+            ptrs += [qkv.q, qkv.scales, qkv.bias, qkv.norm, o.q, o.scales, gu.q, gu.scales, gu.norm, dn.q, dn.scales,
+                     kc, vc]
+        if any(v is None for v in ptrs):
+            return None
+        table = torch.tensor(ptrs, dtype=torch.int64, device="cuda")
+        barrier = torch.zeros(max(256, pk_sm_count()), dtype=torch.int32, device="cuda")
+        P = _lib.DecodeParams()
+        P.layers = table.data_ptr()
+        P.n_layers, P.batch, P.hidden = len(self.fast), B, hid
+        P.heads, P.kv_heads, P.head_dim, P.inter = (c.num_attention_heads, c.num_key_value_heads, c.head_dim,
+                                                    c.intermediate_size)
+        P.eps, P.scale, P.cap = c.rms_norm_eps, self.scale, self.cap
+        P.cos_table, P.sin_table = self.cos.data_ptr(), self.sin.data_ptr()
+        P.final_norm = self.m.norm_w().data_ptr()
+        P.head_q, P.head_s = self.fast_head.q, self.fast_head.scales
+        P.vocab, P.select = self.vocab, self.select
+        if isinstance(e, QTensor):
+            P.emb, P.emb_scales, P.emb_rows = e.q.data_ptr(), e.scales.data_ptr(), int(e.shape[0])
+        else:
+            P.emb, P.emb_scales, P.emb_rows = e.data_ptr(), None, int(e.shape[0])
+        P.h, P.q, P.attn, P.act = self.h.data_ptr(), self.q.data_ptr(), self.a.data_ptr(), self.act.data_ptr()
+        P.logits, P.logp = self.logits.data_ptr(), None
+        P.pos, P.lens, P.next_ids = self.pos.data_ptr(), self.lens.data_ptr(), self.next_ids.data_ptr()
+        P.history, P.hist_stride = self.history.data_ptr(), self.max_steps
+        P.step, P.barrier = self.step_no.data_ptr(), barrier.data_ptr()
+        return {"params": P, "keep": [table, barrier]}
+
+    @property
+    def persistent_ok(self) -> bool:
+        return self._mk is not None
+
+    def steps_persistent(self, n: int, stream=None):
+        """``n`` greedy decode steps in one cooperative launch (cv3_decode_steps)."""
+        import ctypes
+        from .. import _lib
+        if self._mk is None:
+            raise RuntimeError("persistent decode needs q8 layers and head, head dim 64, <= 8 sequences")
+        P = self._mk["params"]
+        P.logp = self.logp.data_ptr() if self.keep_logp else None
+        P.steps = int(n)
+        call("cv3_decode_steps", ctypes.byref(P), stream if stream is not None else D.stream())
 
     def launches(self, st):
         """One decode step for every sequence (all pointers fixed -> graph-capturable)."""
@@ -333,13 +397,20 @@ class DecodeEngine:
         else:
             self.graph.replay()
 
-    def run(self, prompts, n_tokens: int, use_graph: bool = True):
-        """Greedy-decode ``n_tokens`` tokens for every prompt; returns ``[B][n_tokens]`` ids (device)."""
+    def run(self, prompts, n_tokens: int, use_graph: bool = True, persistent: bool = False):
+        """Greedy-decode ``n_tokens`` tokens for every prompt; returns ``[B][n_tokens]`` ids (device).
+        The steps after the prefill run as one CUDA graph per step (``use_graph``), eager launches,
+        or -- ``persistent`` -- one cooperative launch for all of them (same tokens; measured slower
+        on B200 than the graph: 1.30 vs 0.90 ms per step at batch 1, 2.78 vs 1.50 at batch 8)."""
         if n_tokens > self.max_steps:
             raise ValueError("n_tokens exceeds max_steps")
         if max(int(np.shape(x)[0]) for x in prompts) + n_tokens > self.cap:
             raise ValueError("prompt + tokens exceed the KV cache capacity")
         self.prefill(prompts)
+        if persistent and self.persistent_ok:
+            if n_tokens > 1:
+                self.steps_persistent(n_tokens - 1)
+            return self.history[:, :n_tokens].clone()
         if use_graph and self.graph is None and n_tokens > 1:
             # capture replays from a snapshot of the state so capture's own launch has no effect
             saved = [t.clone() for t in (self.h, self.pos, self.lens, self.step_no, self.next_ids, self.history)]

@@ -406,6 +406,61 @@ int cv3_conv1d_tc(const float* x, int64_t xsb, int64_t xsc, int64_t xst, int64_t
 /* Error word of the tensor-core conv kernel (see cv3_tc_gemm_status). */
 int cv3_tc_conv_status(int* code);
 
+/* Persistent greedy decode of the Qwen2 speech LM (cv3cpu/models/qwen2.py:
+ * 139-179 per token, llm.py:114 head + greedy pick): `steps` tokens for a
+ * batch of <= 8 sequences in ONE cooperative launch -- every layer's q8 GEMVs
+ * (RMSNorm fused in, bias, RoPE + KV append, GQA attention, residuals,
+ * SwiGLU), the final norm, the head, log_softmax / first argmax over the
+ * speech tokens, bookkeeping (pos, lens, history[b][*step], *step) and the
+ * embedding of the chosen token as the next input -- separated by grid-wide
+ * barriers (bounded waits; CV3_ERR_CUDA and cv3_decode_status on expiry).
+ * State on entry is what cv3_head_select + cv3_embedding leave: h holds the
+ * embedded current token at position pos[b], lens[b] = pos[b] + 1.
+ * Every matrix is q8 ([rows][kp] int8 + fp16 scales [rows][kp/64]) with
+ * kp == its K; gate/up rows interleaved (2i gate_i, 2i+1 up_i); qkv rows =
+ * q heads, k heads, v heads.  The per-layer table has CV3_DECODE_LAYER_FIELDS
+ * device pointers per layer, in this order: */
+#define CV3_DECODE_LAYER_FIELDS 13
+/*  0 qkv q8, 1 qkv scales, 2 qkv bias (fp32), 3 input RMSNorm weight,
+ *  4 o q8, 5 o scales, 6 gate|up q8, 7 gate|up scales, 8 post-attention RMSNorm
+ *  weight, 9 down q8, 10 down scales, 11 K cache, 12 V cache
+ * (caches [batch][kv_heads][cap][head_dim] fp32). */
+typedef struct cv3_decode_params {
+  const void* const* layers; /* device array: n_layers * CV3_DECODE_LAYER_FIELDS pointers */
+  int32_t n_layers, batch, hidden, heads, kv_heads, head_dim, inter;
+  float eps, scale;       /* RMSNorm eps; attention scale (1/sqrt(head_dim), fp32) */
+  int64_t cap;            /* KV cache capacity (positions) */
+  const float* cos_table; /* [cap][head_dim] */
+  const float* sin_table;
+  const float* final_norm;
+  const int8_t* head_q;   /* [vocab][hidden] q8 */
+  const uint16_t* head_s;
+  int32_t vocab, select;  /* head rows; tokens eligible for the greedy pick */
+  const void* emb;        /* next-token embedding table: fp32 [rows][hidden] or q8 */
+  const uint16_t* emb_scales; /* NULL for fp32 */
+  int32_t emb_rows;
+  float* h;               /* [batch][hidden] residual stream / input */
+  float* q;               /* [batch][heads][head_dim] scratch */
+  float* attn;            /* [batch][heads*head_dim] scratch */
+  float* act;             /* [batch][inter] scratch */
+  float* logits;          /* [batch][vocab] */
+  float* logp;            /* [batch][vocab] log-probs of the last step, or NULL */
+  int32_t* pos;
+  int32_t* lens;
+  int64_t* next_ids;
+  int64_t* history;       /* [batch][hist_stride] */
+  int64_t hist_stride;
+  int32_t* step;          /* history column of the next token */
+  uint32_t* barrier;      /* one word per SM (>= 256 words; the call zeroes them on its stream) */
+  int32_t steps;
+} cv3_decode_params;
+
+int cv3_decode_steps(const cv3_decode_params* params, void* stream);
+
+/* Error word of the persistent decode kernel (see cv3_tc_gemm_status): 1 a
+ * barrier wait expired, 2 a position past the cache, 3 a step past the history. */
+int cv3_decode_status(int* code);
+
 /* Error word of the tensor-core kernels (0 = none; else the code of the
  * first bounded wait that expired), read and cleared.  Synchronises. */
 int cv3_tc_gemm_status(int* code);

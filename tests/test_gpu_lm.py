@@ -51,8 +51,8 @@ def test_graph_decode_equals_eager_and_oracle(small_weights, profile):
         sp = rng.integers(0, 256, size=4).tolist()
         prompts.append(lm.prompt_embedding(text, (), sp))
         oprompts.append(olm.prompt_embedding(text, (), sp))
-    graph = lm.generate_greedy(prompts, 20).cpu().numpy()
-    eager = lm.generate_greedy(prompts, 20, use_graph=False).cpu().numpy()
+    graph = lm.generate_greedy(prompts, 20, persistent=False).cpu().numpy()
+    eager = lm.generate_greedy(prompts, 20, use_graph=False, persistent=False).cpu().numpy()
     assert np.array_equal(graph, eager)
     for b in range(3):
         toks, _ = olm.generate_greedy(oprompts[b], 20)
@@ -91,3 +91,54 @@ def test_full_size_lm_teacher_forced():
         eng.step()
         got.append(eng.logp[0].cpu().numpy().copy())
     assert rel_err(np.stack(got), ref_logp) < 1e-4
+
+
+def _decode_status_clear():
+    import ctypes
+    code = ctypes.c_int(-1)
+    assert pkg("_lib").load().cv3_decode_status(ctypes.byref(code)) == 0 and code.value == 0
+
+
+def test_persistent_decode_equals_graph_steps():
+    """cv3_decode_steps (every step in one cooperative launch) against the per-step graph at
+    the released geometry (every layer q8, as the persistent kernel requires): identical
+    greedy ids for a ragged batch, per-step log-probs within 1e-5."""
+    W = pkg("synth").synthetic_weights("balanced", stages=("llm",))
+    lm = pkg("models.llm").CosyVoice3LM(_device(W))
+    rng = np.random.default_rng(11)
+    hid = lm.cfg.hidden_size
+    prompts = [(rng.normal(size=(n, hid)) * 0.1).astype(np.float32) for n in (9, 30, 17)]
+    eng = lm.engine(3, 256, 24)
+    assert eng.persistent_ok
+    mk = eng.run(prompts, 24, persistent=True).cpu().numpy()
+    _decode_status_clear()
+    gr = eng.run(prompts, 24, persistent=False).cpu().numpy()
+    assert np.array_equal(mk, gr)
+    # step by step with log-probs
+    eng.keep_logp = True
+    eng.prefill(prompts)
+    a = []
+    for _ in range(6):
+        eng.steps_persistent(1)
+        a.append(eng.logp.cpu().numpy().copy())
+    eng.graph = None
+    eng.prefill(prompts)
+    b = []
+    for _ in range(6):
+        eng.step()
+        b.append(eng.logp.cpu().numpy().copy())
+    assert rel_err(np.stack(a), np.stack(b)) < 1e-5
+    _decode_status_clear()
+
+
+def test_persistent_decode_bench_batch():
+    """Eight sequences (the benchmark's batch) at the released geometry: the persistent
+    launch reproduces the graph's 40 greedy tokens exactly."""
+    W = pkg("synth").synthetic_weights("balanced", stages=("llm",))
+    lm = pkg("models.llm").CosyVoice3LM(_device(W))
+    rng = np.random.default_rng(3)
+    prompts = [(rng.normal(size=(60 + 3 * i, 896)) * 0.1).astype(np.float32) for i in range(8)]
+    mk = lm.generate_greedy(prompts, 40, persistent=True).cpu().numpy()
+    gr = lm.generate_greedy(prompts, 40, persistent=False).cpu().numpy()
+    assert np.array_equal(mk, gr)
+    _decode_status_clear()
