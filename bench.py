@@ -240,10 +240,21 @@ def dominant_kernel_roofline(tts, peaks):
     flops = 2.0 * M * blk.n * blk.k
     achieved = flops / (ms * 1e-3) / 1e12
     peak = peaks.get("bf16_tflops")
-    return {"kernel": "DiT ff1 GEMM (M=%d, N=%d, K=%d, fp32)" % (M, blk.n, blk.k), "bound": "tensor",
+    # 3xTF32: every fp32 product is three tf32 MMA products on the tensor pipe; its own
+    # measured dense tf32 rate is the ceiling of that pipe
+    import ctypes
+    tf32 = ctypes.c_double(0.0)
+    L.call("cv3_tc_tf32_peak", ctypes.byref(tf32), st.cuda_stream)
+    return {"kernel": "DiT ff1 GEMM (M=%d, N=%d, K=%d, fp32 via 3xTF32)" % (M, blk.n, blk.k), "bound": "tensor",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
-            "peak_source": "measured bf16 dense (MEASURED_PEAKS.json, burst)", "traffic": None,
-            "avg_launch_ms": ms}
+            "peak_source": "measured bf16 dense (MEASURED_PEAKS.json, burst)",
+            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this shape (ncu --set
+            # full of `bench.py --kernel ff1`, profiles/hot_kernels_ncu_full.md); algorithmic 144.6 MB
+            "traffic": 59.5e6 + 43.0e6, "traffic_unit": "bytes per launch",
+            "avg_launch_ms": ms,
+            "tensor_pipe": {"tf32_tflops_issued": 3.0 * achieved, "tf32_peak_measured": tf32.value,
+                            "frac_of_measured": 3.0 * achieved / tf32.value if tf32.value else None,
+                            "peak_source": "cv3_tc_tf32_peak (this run)"}}
 
 
 def run_cuda(args, rank: int, world: int) -> None:
@@ -357,9 +368,55 @@ def run_slice(args) -> None:
     print("slice done", flush=True)
 
 
+def run_kernel(args) -> None:
+    """One hot kernel alone at its bench shape, five launches (the small, self-contained
+    case the ncu captures under profiles/ use): ``ff1`` the DiT FF GEMM, ``attention`` the
+    DiT attention, ``conv`` the largest vocoder resblock conv, ``gemv`` the LM gate/up
+    decode GEMV (batch 8)."""
+    import math
+    import numpy as np
+    import torch
+    L = pkg("_lib")
+    common = pkg("models._common")
+    st = torch.cuda.current_stream().cuda_stream
+    torch.manual_seed(0)
+    if args.kernel == "ff1":
+        M, N, K = 2 * UTTS * 2 * (PROMPT_TOKENS + TOKENS), 2048, 1024
+        a, b, c = torch.randn(M, K, device="cuda"), torch.randn(N, K, device="cuda") * 0.03, \
+            torch.empty(M, N, device="cuda")
+        lin = common.Lin(b)
+        fn = lambda: lin.tc(a.data_ptr(), M, c.data_ptr(), 0, stream=st)
+    elif args.kernel == "attention":
+        B, H, N, D = 2 * UTTS, 16, 2 * (PROMPT_TOKENS + TOKENS), 64
+        qkv, o = torch.randn(B, N, 3 * H * D, device="cuda"), torch.empty(B, N, H * D, device="cuda")
+        q = qkv.data_ptr()
+        sb, sn = N * 3 * H * D, 3 * H * D
+        fn = lambda: L.call("cv3_attention", q, sb, D, sn, q + H * D * 4, sb, D, sn, q + 2 * H * D * 4, sb, D, sn,
+                            o.data_ptr(), N * H * D, D, H * D, B, H, H, N, N, D, 1.0 / math.sqrt(D), 0, 0, 0, st)
+    elif args.kernel == "conv":
+        C, T, k = 64, 120 * 2 * TOKENS, 7   # the 64-channel resolution: 120 samples per mel frame
+        x, y = torch.randn(UTTS, C, T, device="cuda"), torch.empty(UTTS, C, T, device="cuda")
+        cv = common.ConvTC((torch.randn(C, C, k, device="cuda") / math.sqrt(C * k)).half().float(),
+                           torch.randn(C, device="cuda"))
+        fn = lambda: cv(x, y, UTTS, T, T, dilation=3, pad_left=3 * (k - 1), stream=st)
+    else:  # gemv
+        quant = pkg("quant")
+        w = (np.random.default_rng(0).normal(size=(9728, 896)) * 0.02).astype(np.float32)
+        g = common.DecodeGemv(quant.make_qtensor(w).to_device(), None, torch.ones(896, device="cuda"), 1e-6,
+                              swiglu=True)
+        x, y = torch.randn(8, 896, device="cuda"), torch.empty(8, 4864, device="cuda")
+        fn = lambda: g(x.data_ptr(), 8, y.data_ptr(), stream=st)
+    for _ in range(5):
+        fn()
+    torch.cuda.synchronize()
+    print("kernel %s: 5 launches done" % args.kernel, flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--slice", action="store_true", help="profiling slice (see run_slice)")
+    ap.add_argument("--kernel", choices=["ff1", "attention", "conv", "gemv"],
+                    help="run one hot kernel alone at its bench shape (for ncu captures)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
@@ -374,7 +431,9 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     try:
-        if args.slice:
+        if args.kernel:
+            run_kernel(args)
+        elif args.slice:
             run_slice(args)
         elif args.impl == "reference":
             run_reference(args, rank, world)

@@ -461,6 +461,10 @@ int cv3_decode_steps(const cv3_decode_params* params, void* stream);
  * barrier wait expired, 2 a position past the cache, 3 a step past the history. */
 int cv3_decode_status(int* code);
 
+/* Measures the dense kind::tf32 tensor-pipe rate of this GPU (every SM
+ * issuing 128x256x8 MMAs back to back) in TFLOP/s.  Synchronises. */
+int cv3_tc_tf32_peak(double* tflops, void* stream);
+
 /* Error word of the tensor-core kernels (0 = none; else the code of the
  * first bounded wait that expired), read and cleared.  Synchronises. */
 int cv3_tc_gemm_status(int* code);
