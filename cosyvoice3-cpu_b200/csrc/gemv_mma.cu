@@ -1,0 +1,305 @@
+// Decode GEMV for q8 weights on the tensor cores (the LM's per-token linears,
+// up to 8 activation rows):  y[m][row] = epilogue( sum_k xn[m][k] * q[row][k] * s[row][k/64] ).
+//
+// Why tensor cores for a GEMV: with 8 sequences every weight byte needs 8
+// multiply-adds, which on CUDA cores makes the kernel instruction-bound well
+// below HBM speed.  Here a warp-level MMA (m16n8k16, bf16 in, fp32 out) does
+// them: A = 16 weight rows x 16 k (int8 values are exact in bf16), B = 16 k x
+// 8 sequences of the activations split exactly into three bf16 parts
+// (x = hi + mid + lo to fp32 precision), so each product is exact and the
+// per-64-group fp16 scale is applied to the group's partial sum in fp32.
+//
+// K order inside a 64-wide scale group is permuted (the same way for both
+// operands, so the dot product is unchanged) so that lane (g, c) of a warp --
+// g = lane / 4, c = lane % 4 -- needs bytes 16c .. 16c+15 of weight rows g and
+// g+8 and activations 16c .. 16c+15 of sequence g: one 16-byte load per row per
+// group, straight into the MMA fragments.
+//
+// CTA = 16 x RT weight rows x all of K, 8 warps (warp w takes row tile w % RT
+// and every (8 / RT)-th scale group); all of a warp's weight loads are issued
+// first, then the activations are copied to shared memory asynchronously
+// (cp.async: every 16-byte piece in flight at once, no registers), RMSNorm
+// is applied there, and the warps' partial sums are added in a fixed order in
+// shared memory (deterministic).  Epilogues: bias, residual add
+// (y may alias it), SwiGLU of interleaved gate/up rows (cv3cpu/models/qwen2.py:
+// 155-177, llm.py:74-78).
+#include "common.cuh"
+
+namespace {
+
+constexpr int NWARP = 8, MAXB = 8;
+
+struct MmaArgs {
+  const float* x;
+  int64_t ldx;
+  int m, k;
+  const int8_t* q;
+  const uint16_t* sc;
+  int n;
+  const float* bias;
+  const float* residual;
+  float* y;
+  int64_t ldy;
+  const float* norm_w;
+  float eps;
+  int swiglu;
+  int gsplit;        // scale groups per K split (all of them when not split)
+  float* partial;    // [splits][n][MAXB] when split
+  int* counter;      // [row tiles], zero on entry and left zero
+};
+
+__device__ __forceinline__ void widen16(const int4 w, float f[16]) {
+  const uint32_t words[4] = {(uint32_t)w.x ^ 0x80808080u, (uint32_t)w.y ^ 0x80808080u,
+                             (uint32_t)w.z ^ 0x80808080u, (uint32_t)w.w ^ 0x80808080u};
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) f[4 * i + b] = __int_as_float(__byte_perm(words[i], 0x4B000000u, 0x7440u | b)) - 8388736.0f;
+}
+
+// two floats that are exact bf16 values (low 16 bits zero) as one bf16x2
+// register, `lo` in the low half (the lower k index): their top halves
+__device__ __forceinline__ uint32_t pack(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+}
+
+__device__ __forceinline__ float bf16_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFF0000u); }
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// RT: 16-row tiles per CTA; GMAX: most scale groups one warp takes
+// (K <= 64 * (NWARP / RT) * GMAX)
+template <int RT, int GMAX>
+__global__ void __launch_bounds__(NWARP * 32)
+q8_gemv_mma_kernel(MmaArgs a) {
+  constexpr int ROWS = 16 * RT, GSTEP = NWARP / RT;
+  extern __shared__ float xs[];  // [MAXB][k] staged (and normalised) activations, rows >= m zero
+  __shared__ float red[NWARP][16][MAXB];
+  __shared__ float rn[MAXB];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int tile = warp % RT, gw = warp / RT;
+  const int row0 = blockIdx.x * ROWS + 16 * tile;
+  const int ks = a.k >> 6;
+  // this CTA's K split: scale groups [g0, g0 + ng); x columns [64 g0, 64 (g0 + ng))
+  const int g0 = blockIdx.y * a.gsplit;
+  const int ng = min(a.gsplit, ks - g0);
+  const int kw = 64 * ng;  // staged row width
+  const int r0 = min(row0 + g, a.n - 1), r1 = min(row0 + g + 8, a.n - 1);
+
+  // -- weights first: they do not depend on x --------------------------------------------
+  int4 w0[GMAX], w1[GMAX];
+  float s0[GMAX], s1[GMAX];
+#pragma unroll
+  for (int i = 0; i < GMAX; ++i) {
+    const int G = gw + GSTEP * i;
+    const bool in = G < ng;
+    w0[i] = in ? ld_stream16(a.q + (int64_t)r0 * a.k + 64 * (g0 + G) + 16 * c) : make_int4(0, 0, 0, 0);
+    w1[i] = in ? ld_stream16(a.q + (int64_t)r1 * a.k + 64 * (g0 + G) + 16 * c) : make_int4(0, 0, 0, 0);
+    s0[i] = in ? h2f(a.sc[(int64_t)r0 * ks + g0 + G]) : 0.f;
+    s1[i] = in ? h2f(a.sc[(int64_t)r1 * ks + g0 + G]) : 0.f;
+  }
+
+  // -- stage x asynchronously (all pieces in flight at once), optional RMSNorm -----------
+  const int k4 = kw >> 2;
+  for (int i = tid; i < MAXB * k4; i += NWARP * 32) {
+    const int mr = i / k4;
+    float4* dst = reinterpret_cast<float4*>(xs) + i;
+    if (mr < a.m) {
+      const float* src = a.x + (int64_t)mr * a.ldx + 64 * g0 + 4 * (i - mr * k4);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                   "l"(src)
+                   : "memory");
+    } else {
+      *dst = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  if (a.norm_w) {
+    if (warp < a.m) {
+      float s = 0.f;
+      for (int cc = lane; cc < kw; cc += 32) {  // not split when normalised: kw == k
+        const float v = xs[warp * kw + cc];
+        s += v * v;
+      }
+      s = warp_sum(s);
+      if (lane == 0) rn[warp] = 1.0f / sqrtf(s / (float)a.k + a.eps);
+    }
+    __syncthreads();
+    for (int i = tid; i < a.m * k4; i += NWARP * 32) {
+      const int mr = i / k4, c4 = i - mr * k4;
+      const float r = rn[mr];
+      const float4 w4 = reinterpret_cast<const float4*>(a.norm_w)[c4];
+      float4 v = reinterpret_cast<float4*>(xs)[i];
+      v.x = (v.x * r) * w4.x;
+      v.y = (v.y * r) * w4.y;
+      v.z = (v.z * r) * w4.z;
+      v.w = (v.w * r) * w4.w;
+      reinterpret_cast<float4*>(xs)[i] = v;
+    }
+    __syncthreads();
+  }
+
+  // -- per scale group: 4 k-steps x 3 activation parts = 12 MMAs, then * scale ------------
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < GMAX; ++i) {
+    const int G = gw + GSTEP * i;
+    if (G < ng) {
+      float xv[16];
+      const float4* xp = reinterpret_cast<const float4*>(xs + g * kw + 64 * G + 16 * c);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const float4 t = xp[v];
+        xv[4 * v] = t.x;
+        xv[4 * v + 1] = t.y;
+        xv[4 * v + 2] = t.z;
+        xv[4 * v + 3] = t.w;
+      }
+      // x = hi + mid + lo exactly: hi = x truncated to bf16, mid = the remainder
+      // truncated, lo = what is left (<= 8 significant bits, itself a bf16 value)
+      float part[3][16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float hi = bf16_trunc(xv[e]);
+        const float r1v = xv[e] - hi;
+        const float mid = bf16_trunc(r1v);
+        part[0][e] = hi;
+        part[1][e] = mid;
+        part[2][e] = bf16_trunc(r1v - mid);
+      }
+      float f0[16], f1[16];
+      widen16(w0[i], f0);
+      widen16(w1[i], f1);
+      // one accumulator chain per part (three independent MMA chains of four)
+      float t[3][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t A0 = pack(f0[4 * j], f0[4 * j + 1]);      // row g,     k 2c, 2c+1
+        const uint32_t A1 = pack(f1[4 * j], f1[4 * j + 1]);      // row g + 8, k 2c, 2c+1
+        const uint32_t A2 = pack(f0[4 * j + 2], f0[4 * j + 3]);  // row g,     k 2c+8, 2c+9
+        const uint32_t A3 = pack(f1[4 * j + 2], f1[4 * j + 3]);  // row g + 8, k 2c+8, 2c+9
+#pragma unroll
+        for (int pp = 0; pp < 3; ++pp)
+          mma_bf16(t[pp], A0, A1, A2, A3, pack(part[pp][4 * j], part[pp][4 * j + 1]),
+                   pack(part[pp][4 * j + 2], part[pp][4 * j + 3]));
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float v = (t[2][e] + t[1][e]) + t[0][e];  // small parts first
+        acc[e] = fmaf(v, e < 2 ? s0[i] : s1[i], acc[e]);
+      }
+    }
+  }
+  // D fragment: rows g / g+8 of the warp's tile, sequences 2c, 2c+1
+  red[warp][g][2 * c] = acc[0];
+  red[warp][g][2 * c + 1] = acc[1];
+  red[warp][g + 8][2 * c] = acc[2];
+  red[warp][g + 8][2 * c + 1] = acc[3];
+  __syncthreads();
+
+  // -- reduce the warps of each tile in a fixed order, then the K splits ---------------------
+  __shared__ float tot[16 * RT][MAXB];
+  __shared__ int last_cta;
+  const int rt = tid / MAXB, bb = tid - rt * MAXB;  // rt: row inside the CTA
+  const int row = blockIdx.x * ROWS + rt;
+  if (tid < ROWS * MAXB) {
+    const int tl = rt / 16, rr = rt % 16;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < GSTEP; ++w) v += red[tl + RT * w][rr][bb];
+    tot[rt][bb] = v;
+  }
+  if (gridDim.y > 1) {
+    // deterministic split reduction: every split parks its sums, the last CTA of
+    // the row tile to arrive adds them in split order and runs the epilogue
+    if (tid < ROWS * MAXB && row < a.n)
+      __stcg(a.partial + ((int64_t)blockIdx.y * a.n + row) * MAXB + bb, tot[rt][bb]);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_cta = atomicAdd(&a.counter[blockIdx.x], 1) == (int)gridDim.y - 1;
+    __syncthreads();
+    if (!last_cta) return;
+    __threadfence();
+    if (tid < ROWS * MAXB && row < a.n) {
+      float v = 0.f;
+      for (int sp = 0; sp < (int)gridDim.y; ++sp) v += __ldcg(a.partial + ((int64_t)sp * a.n + row) * MAXB + bb);
+      tot[rt][bb] = v;
+    }
+    if (tid == 0) a.counter[blockIdx.x] = 0;  // ready for the next launch
+  }
+  __syncthreads();
+  if (tid < ROWS * MAXB) {
+    const int rr = rt % 16;
+    float v = tot[rt][bb];
+    if (row < a.n && bb < a.m) {
+      if (a.bias) v += a.bias[row];
+      if (a.swiglu) {
+        if ((rr & 1) == 0) {  // rows 2i (gate) and 2i+1 (up)
+          float up = tot[rt + 1][bb];
+          if (a.bias) up += a.bias[row + 1];
+          a.y[(int64_t)bb * a.ldy + row / 2] = (v / (1.0f + expf(-v))) * up;
+        }
+      } else {
+        float* yp = a.y + (int64_t)bb * a.ldy + row;
+        if (a.residual) v = v + a.residual[(int64_t)bb * a.ldy + row];
+        *yp = v;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
+                                      const uint16_t* scales, int64_t n, int64_t kp, const float* bias,
+                                      const float* residual, const float* norm_w, float eps, int swiglu, float* y,
+                                      int64_t ldy, int64_t splits, float* workspace, int64_t workspace_floats,
+                                      int* counters, void* stream) {
+  CV3_REQUIRE(m >= 1 && m <= MAXB, CV3_ERR_VALUE, "q8_decode_gemv_mma: 1..8 rows per call (got %lld)", (long long)m);
+  CV3_REQUIRE(n > 0 && k > 0 && k % 64 == 0 && kp == k, CV3_ERR_VALUE,
+              "q8_decode_gemv_mma: K must be a multiple of 64 with no padding (K %lld, padded %lld)", (long long)k,
+              (long long)kp);
+  CV3_REQUIRE(k <= 64 * NWARP * 10 && n < (1LL << 30), CV3_ERR_VALUE, "q8_decode_gemv_mma: K up to 5120");
+  CV3_REQUIRE(ldx >= k && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)q & 15) == 0, CV3_ERR_VALUE,
+              "q8_decode_gemv_mma: x rows and the payload must be 16-byte aligned");
+  CV3_REQUIRE(swiglu ? (n % 2 == 0 && ldy >= n / 2 && !residual) : ldy >= n, CV3_ERR_VALUE,
+              "q8_decode_gemv_mma: bad output layout");
+  CV3_REQUIRE(!norm_w || ((uintptr_t)norm_w & 15) == 0, CV3_ERR_VALUE, "q8_decode_gemv_mma: norm weight alignment");
+  CV3_REQUIRE(splits >= 1 && splits <= 16 && (splits == 1 || !norm_w), CV3_ERR_VALUE,
+              "q8_decode_gemv_mma: 1..16 K splits, and no split with a fused RMSNorm");
+  const int ngroups = (int)(k / 64);
+  const int gsplit = (ngroups + (int)splits - 1) / (int)splits;
+  const int nsplit = (ngroups + gsplit - 1) / gsplit;
+  // big matrices: 32-row CTAs (one wave on 148 SMs for 9728 rows); small ones 16
+  const bool wide = n >= 4096;
+  const int rows = wide ? 32 : 16;
+  const int tiles = (int)((n + rows - 1) / rows);
+  if (nsplit > 1) {
+    CV3_REQUIRE(workspace && counters && workspace_floats >= (int64_t)nsplit * n * MAXB, CV3_ERR_VALUE,
+                "q8_decode_gemv_mma: K splits need a workspace of splits*n*8 floats and zeroed counters "
+                "(one per %d-row tile)", rows);
+  }
+  MmaArgs a{x, ldx, (int)m, (int)k, q, scales, (int)n, bias, residual, y, ldy, norm_w, eps, swiglu,
+            gsplit, workspace, counters};
+  const int smem = MAXB * 64 * gsplit * 4;
+  dim3 grid((unsigned)tiles, (unsigned)nsplit);
+  cudaStream_t st = cv3::as_stream(stream);
+  void (*fn)(MmaArgs);
+  if (wide) fn = (gsplit <= 4 * 4) ? q8_gemv_mma_kernel<2, 4> : q8_gemv_mma_kernel<2, 20>;
+  else fn = (gsplit <= 8 * 2) ? q8_gemv_mma_kernel<1, 2> : q8_gemv_mma_kernel<1, 10>;
+  if (smem > 48 * 1024) {
+    int rc = cv3::allow_smem((const void*)fn, smem);
+    if (rc) return rc;
+  }
+  fn<<<grid, NWARP * 32, smem, st>>>(a);
+  return cv3::check_launch("q8_decode_gemv_mma");
+}

@@ -143,10 +143,17 @@ class DecodeGemv:
         self.norm = norm_w.data_ptr() if norm_w is not None else None
         self.eps = float(eps)
         self.swiglu = 1 if swiglu else 0
-        tiles = -(-self.n // 32)
-        self.splits = max(1, min(64, -(-target_ctas // tiles), self.kp // 64))
-        kps = -(-(self.kp // self.splits) // 16) * 16
-        eff = -(-self.kp // kps)
+        # the tensor-core kernel takes every unpadded K up to 5120 (all of Qwen2's linears),
+        # unsplit (a K split measured slower for the LM's down projection: 15 vs 12 us)
+        self.mma = self.kp == self.k and self.k % 64 == 0 and self.k <= 5120
+        if self.mma:
+            tiles = -(-self.n // (32 if self.n >= 4096 else 16))
+            self.splits = eff = 1
+        else:
+            tiles = -(-self.n // 32)
+            self.splits = max(1, min(64, -(-target_ctas // tiles), self.kp // 64))
+            kps = -(-(self.kp // self.splits) // 16) * 16
+            eff = -(-self.kp // kps)
         self.ws = D.empty((eff * 8 * self.n,)) if eff > 1 else None
         self.cnt = torch.zeros(tiles, dtype=torch.int32, device="cuda") if eff > 1 else None
 
@@ -155,6 +162,14 @@ class DecodeGemv:
         s = stream if stream is not None else D.stream()
         ldx = self.k if ldx is None else ldx
         ldy = (self.n // 2 if self.swiglu else self.n) if ldy is None else ldy
+        if self.mma:
+            if ldx % 4 or x % 16:
+                raise ValueError("DecodeGemv: x must be 16-byte aligned rows")
+            call("cv3_q8_decode_gemv_mma", x, m, self.k, ldx, self.q, self.scales, self.n, self.kp, self.bias,
+                 residual, self.norm, self.eps, self.swiglu, y, ldy, self.splits,
+                 self.ws.data_ptr() if self.ws is not None else None, self.ws.numel() if self.ws is not None else 0,
+                 self.cnt.data_ptr() if self.cnt is not None else None, s)
+            return
         call("cv3_q8_decode_gemv", x, m, self.k, ldx, self.q, self.scales, self.n, self.kp, self.bias, residual,
              self.norm, self.eps, self.swiglu, y, ldy, self.splits,
              self.ws.data_ptr() if self.ws is not None else None, self.ws.numel() if self.ws is not None else 0,

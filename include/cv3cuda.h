@@ -86,6 +86,19 @@ int cv3_q8_decode_gemv(const float* x, int64_t m, int64_t k, int64_t ldx, const 
                        int64_t ldy, int64_t splits, float* workspace, int64_t workspace_floats,
                        int* counters, void* stream);
 
+/* cv3_q8_decode_gemv on the tensor cores (warp MMA m16n8k16: int8 weights are
+ * exact bf16, the activations enter as three exact bf16 parts, the fp16 group
+ * scale multiplies each 64-wide group's fp32 partial sum).  Same operands,
+ * fusions and output as cv3_q8_decode_gemv; needs K a multiple of 64 with no
+ * padding (kp == k), K <= 5120, 16-byte aligned x rows.  `splits` > 1 (no
+ * fused RMSNorm) spreads K over that many CTAs per row tile with a
+ * deterministic reduction: workspace >= splits*n*8 floats and counters (one
+ * per 16-row tile, or 32-row when n >= 4096) zeroed once, left zeroed. */
+int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
+                           const uint16_t* scales, int64_t n, int64_t kp, const float* bias, const float* residual,
+                           const float* norm_w, float eps, int swiglu, float* y, int64_t ldy, int64_t splits,
+                           float* workspace, int64_t workspace_floats, int* counters, void* stream);
+
 /* Same contract for an fp32 weight W[n][k] (row stride ldw); replaces the
  * plain-array branch of cv3cpu/quant.py:165-170. fp32-exact SIMT math. */
 int cv3_f32_linear(const float* x, int64_t m, int64_t k, int64_t ldx,

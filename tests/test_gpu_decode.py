@@ -88,3 +88,29 @@ def test_engine_fused_path_matches_oracle(small_weights):
     for b in range(2):
         ref, _ = olm.generate_greedy(oprompts[b], 16)
         assert toks[b].tolist() == ref
+
+
+@pytest.mark.parametrize("n,k", [(1152, 896), (896, 4864), (6761, 896), (9728, 896), (48, 128)])
+@pytest.mark.parametrize("m", [1, 8])
+def test_tensor_core_and_cuda_core_gemvs_agree(n, k, m):
+    """cv3_q8_decode_gemv_mma (warp MMA, three exact bf16 parts of x) against the CUDA-core
+    kernel and the oracle on the same operands, with the RMSNorm fused in."""
+    import torch
+    L = pkg("_lib")
+    rng = np.random.default_rng(n * 7 + k + m)
+    w = (rng.normal(size=(n, k)) * 0.02).astype(np.float32)
+    hq = pkg("quant").make_qtensor(w)
+    qt = hq.to_device()
+    nw = (1 + 0.1 * rng.normal(size=k)).astype(np.float32)
+    x = (rng.normal(size=(m, k)) * 3.0).astype(np.float32)
+    ref = nx.qmatmul(nx.rms_norm(x, nw, 1e-6), nx.QTensor("q8", hq.q, hq.scales, hq.shape, 64))
+    xd, nwd = torch.from_numpy(x).cuda(), torch.from_numpy(nw).cuda()
+    st = torch.cuda.current_stream().cuda_stream
+    y1, y2 = torch.empty(m, n, device="cuda"), torch.empty(m, n, device="cuda")
+    L.call("cv3_q8_decode_gemv_mma", xd.data_ptr(), m, k, k, qt.q.data_ptr(), qt.scales.data_ptr(), n, k, None, None,
+           nwd.data_ptr(), 1e-6, 0, y1.data_ptr(), n, 1, None, 0, None, st)
+    L.call("cv3_q8_decode_gemv", xd.data_ptr(), m, k, k, qt.q.data_ptr(), qt.scales.data_ptr(), n, k, None, None,
+           nwd.data_ptr(), 1e-6, 0, y2.data_ptr(), n, 1, None, 0, None, st)
+    torch.cuda.synchronize()
+    assert rel_err(y1.cpu().numpy(), ref) < 1e-5
+    assert rel_err(y1.cpu().numpy(), y2.cpu().numpy()) < 1e-5
