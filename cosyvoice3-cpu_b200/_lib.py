@@ -72,6 +72,8 @@ SIGNATURES = {
     "cv3_conv1d_tc": [P, I64, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, I64, I64, I64, P, I32, F, P,
                       P, P, I64, I64, I64, I64, P],
     "cv3_tc_conv_status": [P],
+    "cv3_conv_tc_set_window": [I32],
+    "cv3_conv_tc_last_path": [P],
     "cv3_decode_steps": [P, P],
     "cv3_decode_status": [P],
     "cv3_tc_tf32_peak": [P, P],

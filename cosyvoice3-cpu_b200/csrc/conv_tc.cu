@@ -9,25 +9,44 @@
 // (cv3cpu/ops.py:165-219; zero padding implicit: inputs outside [0, T_in) read
 // as zero, so t_out fixes the right pad.)  GEMM view per (batch, group):
 // rows = output frames (M), columns = output channels (N), reduction =
-// (tap, input channel) pairs, tap-major: K block kb covers 32 input channels of
-// one tap.  The weights are rearranged once (cv3_conv_weight_tc) into
-// Wt[co][j][ci_pad], the K-major B operand, with an optional tf32 remainder
-// (weights stored as fp16 -- the vocoder's -- are exact tf32 values and need
-// none: two products per element instead of three).
+// (input channel, tap) pairs, channel-block major: K block kb = cb * k + j covers
+// input channels [32 cb, 32 cb + 32) of tap j.  The weights are rearranged once
+// (cv3_conv_weight_tc) into Wt[co][cb][j][32], the K-major B operand, with an
+// optional tf32 remainder (weights stored as fp16 -- the vocoder's -- are exact
+// tf32 values and need none: two products per element instead of three).
 //
-// CTA = 128 output frames x 64 channels, 6 warps:
+// Two kernels share that layout and the epilogue.
+//
+// Window kernel (stride 1: the vocoder's and the DiT's convs).  Persistent CTAs
+// walk 128-frame x 64-channel tiles.  For each channel block, the input window
+// -- 32 channels x the 128 + (k-1) dil frames all k taps of the tile touch -- is
+// staged ONCE in shared memory as a K-major, 128 B-swizzled [frames][32] tile
+// (and its tf32 remainder beside it); tap j's A operand is then the same tile
+// shifted down by j*dil rows: a shared-memory descriptor whose start moves by
+// j*dil*128 bytes.  So the k taps of a channel block cost k x 4 tcgen05.mma per
+// product and no per-tap data movement.  12 warps:
 //   warp 0     TMA: Wt (and Wt lo) tiles into a 4-stage ring;
-//   warp 1     MMA issuer (converged warp, elect.sync): A from TMEM, B from smem;
-//   warps 2-5  one output frame per thread (= its TMEM lane): gather the 32
-//              (tap, channel) inputs of each K block straight from global memory
-//              (channel-major x: lanes read consecutive frames, coalesced), the
-//              next block in flight while the current one is split into tf32
-//              hi/lo and stored to TMEM; they also fold the finished TMEM
-//              accumulators into fp32 registers, then run the epilogue.
-// TMEM: two main accumulator sets and one remainder accumulator (64 columns
-// each), two A stages (32 hi + 32 lo columns each).  Every wait is bounded (error
-// word: cv3_tc_conv_status).
+//   warp 1     MMA issuer (converged warp, elect.sync): A and B from shared memory;
+//   warp 2     TMA: token-major input windows, straight into the swizzled A tile
+//              (one 3-D box per channel block);
+//   warps 4-7  builders: load a channel-major window from global memory
+//              (lanes on consecutive frames, coalesced; issued before the wait for
+//              a free A tile so the latency hides behind it) and transpose it into
+//              the A tile; write the remainder tile (x - tf32(x)) for both layouts;
+//   warps 8-11 drainers: fold each K block's TMEM accumulator into fp32
+//              registers (round-to-nearest adds; the tensor core's own adds
+//              truncate), then the tile's epilogue -- while the MMA warp already
+//              runs the next tile into the other accumulator sets.
+// TMEM: six main accumulator sets (one per K block in flight) and two remainder
+// accumulators (one per tile parity), 64 columns each.
+//
+// Gather kernel (any stride and layout): A from TMEM; warps 2-5 load each
+// thread's 32 inputs of a K block straight from global memory, split them into
+// tf32 hi/lo and store them to TMEM.
+//
+// Every wait is bounded (error word: cv3_tc_conv_status).
 #include <algorithm>
+#include <cstring>
 
 #include "tc_common.cuh"
 
@@ -35,13 +54,20 @@ namespace {
 
 using namespace cv3tc;
 
-constexpr int BM = 128, BK = 32, STAGES = 4, THREADS = 192;
-constexpr uint32_t C_A = 384;
+constexpr int BM = 128, BN = 64, BK = 32;
+constexpr int TILE_B = BN * BK * 4;      // one 64 x 32 weight tile
+constexpr int STAGE_BYTES = 2 * TILE_B;  // W | W lo
+constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+constexpr int SMEM_MAX = 232448;  // opt-in shared memory per block
 
 __device__ int g_conv_err = 0;
 
 __device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity, int code) {
   return cv3tc::mbar_wait(bar, parity, &g_conv_err, code);
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
 struct ConvArgs {
@@ -56,9 +82,98 @@ struct ConvArgs {
   float act_p;
   int cin_g, t_in, cout_g, t_out;
   int k, stride, dil, pad_l, groups;
-  int cblocks;  // ceil(cin_g / 32): K blocks per tap
+  int cblocks;  // ceil(cin_g / 32): channel blocks
   int has_lo;
 };
+
+// bias, activation, snake of one accumulator value (channel parameters passed in)
+template <int ACT, bool SNAKE>
+__device__ __forceinline__ float epilogue_value(const ConvArgs& a, float acc, float bias, float alpha) {
+  float o = acc;
+  if (a.bias) o = __fadd_rn(o, bias);
+  if (ACT >= 0) o = act_apply(ACT, a.act_p, o);
+  if (SNAKE) {  // snake (cv3cpu/models/hift.py: x + 1/(alpha + 1e-9) * sin(alpha x)^2)
+    const float sn = sinf(alpha * o);
+    o = o + (1.0f / (alpha + 1e-9f)) * (sn * sn);
+  }
+  return o;
+}
+
+// Epilogue of one output frame t (this thread's row): 64 channels from co0 of group g.
+// Works in chunks of 16 channels whose bias / alpha / residual loads are all issued
+// before the chunk's stores: y may alias the residual, so a load placed after a store
+// could not be hoisted and every channel would pay a full load latency.
+template <int ACT, bool SNAKE>
+__device__ __forceinline__ void store_row(const ConvArgs& a, const float (&acc)[BN], int b, int g, int co0, int t) {
+  constexpr int CH = 16;
+  const bool yvec = a.ysc == 1 && a.yst % 4 == 0 && ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0) &&
+                    (a.ysb % 4 == 0) && (a.cout_g % 4 == 0) &&
+                    (!a.res || (reinterpret_cast<uintptr_t>(a.res) & 15) == 0);
+  const int ch0 = g * a.cout_g + co0;  // first output channel (global index)
+  const int64_t ybase = (int64_t)b * a.ysb + (int64_t)ch0 * a.ysc + (int64_t)t * a.yst;
+  const int nco = min(BN, a.cout_g - co0);
+#pragma unroll
+  for (int c0 = 0; c0 < BN; c0 += CH) {
+    float bv[CH], av[CH], rv[CH];
+#pragma unroll
+    for (int e = 0; e < CH; ++e) {
+      const bool in = c0 + e < nco;
+      bv[e] = (a.bias && in) ? __ldg(a.bias + ch0 + c0 + e) : 0.f;
+      av[e] = (SNAKE && in) ? __ldg(a.alpha + ch0 + c0 + e) : 0.f;
+    }
+    if (yvec && nco == BN) {
+      // token-major y: this thread's channels are contiguous
+      if (a.res) {
+#pragma unroll
+        for (int q = 0; q < CH / 4; ++q) {
+          const float4 r4 = *reinterpret_cast<const float4*>(a.res + ybase + c0 + 4 * q);
+          rv[4 * q] = r4.x;
+          rv[4 * q + 1] = r4.y;
+          rv[4 * q + 2] = r4.z;
+          rv[4 * q + 3] = r4.w;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < CH / 4; ++q) {
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = c0 + 4 * q + e;
+          o[e] = epilogue_value<ACT, SNAKE>(a, acc[c], bv[4 * q + e], av[4 * q + e]);
+          if (a.res) o[e] = __fadd_rn(o[e], rv[4 * q + e]);
+        }
+        *reinterpret_cast<float4*>(a.y + ybase + c0 + 4 * q) = make_float4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+      // channel-major y: lanes write consecutive frames of each channel
+      if (a.res) {
+#pragma unroll
+        for (int e = 0; e < CH; ++e) rv[e] = c0 + e < nco ? a.res[ybase + (int64_t)(c0 + e) * a.ysc] : 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < CH; ++e) {
+        if (c0 + e < nco) {
+          float o = epilogue_value<ACT, SNAKE>(a, acc[c0 + e], bv[e], av[e]);
+          if (a.res) o = __fadd_rn(o, rv[e]);
+          a.y[ybase + (int64_t)(c0 + e) * a.ysc] = o;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Gather kernel
+// ---------------------------------------------------------------------------------
+namespace gk {
+
+constexpr int STAGES = 4, THREADS = 192;
+constexpr uint32_t C_A = 384;
+// main (hi*W) accumulator of K block kb at 64 (kb & 1); the remainder products
+// (2^-11 of the main terms, so their own truncation is harmless) accumulate over
+// the whole reduction in one accumulator at 128
+constexpr uint32_t C_CROSS = 128;
+constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 
 struct Bars {
   uint64_t full[STAGES], empty[STAGES], afull[2], aempty[2], accfull[2], drained[2], done;
@@ -66,30 +181,15 @@ struct Bars {
   int abort_flag;
   int issued[STAGES];
 };
-
-// 128 frames x 64 channels per CTA (TS MMAs with N = 64 run at the full tensor rate)
-constexpr int BN = 64;
-constexpr int TILE_B = BN * BK * 4;
-constexpr int STAGE_BYTES = 2 * TILE_B;  // W | W lo
-constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + (int)sizeof(Bars);
-#ifndef CV3_CONV_GROUP
-#define CV3_CONV_GROUP 1
-#endif
-constexpr int GROUP = CV3_CONV_GROUP;  // K blocks summed in one TMEM accumulator before it is drained
-constexpr uint32_t IDESC = idesc_tf32(BM, BN);
-// main (hi*W) accumulator set q at 64q; the remainder products (2^-11 of the
-// main terms, so their own truncation is harmless) accumulate over the whole
-// reduction in one accumulator at 128
-__device__ __forceinline__ uint32_t c_main(int set) { return (uint32_t)(64 * set); }
-constexpr uint32_t C_CROSS = 128;
+static_assert(sizeof(Bars) <= 256, "gather kernel barriers");
 
 // the 32 inputs of K block kb for output frame t (zero outside the signal / channels).
 // Channel-major x: lane-consecutive frames, one coalesced row per channel.  Token-major
 // x (vec): the thread's 32 channels are contiguous, read as float4.
 // (offsets inside one (batch, group) slab fit 31 bits; the host checks)
 __device__ __forceinline__ void gather(float (&v)[32], const ConvArgs& a, const float* xg, int t, int kb, bool vec) {
-  const int j = kb / a.cblocks;
-  const int ci0 = (kb - j * a.cblocks) * 32;
+  const int cb = kb / a.k, j = kb - cb * a.k;
+  const int ci0 = cb * 32;
   const int ti = t * a.stride + j * a.dil - a.pad_l;
   const bool ok = t < a.t_out && ti >= 0 && ti < a.t_in;
   const int xsc = (int)a.xsc;
@@ -115,34 +215,16 @@ __device__ __forceinline__ void gather(float (&v)[32], const ConvArgs& a, const 
   }
 }
 
-template <int ACT, bool SNAKE>
-__device__ __forceinline__ float epilogue_value(const ConvArgs& a, int ch, float acc) {
-  float o = acc;
-  if (a.bias) o = __fadd_rn(o, a.bias[ch]);
-  if (ACT >= 0) o = act_apply(ACT, a.act_p, o);
-  if (SNAKE) {  // snake (cv3cpu/models/hift.py: x + 1/(alpha + 1e-9) * sin(alpha x)^2)
-    const float al = a.alpha[ch];
-    const float sn = sinf(al * o);
-    o = o + (1.0f / (al + 1e-9f)) * (sn * sn);
-  }
-  return o;
-}
-
 // Accuracy: the tensor core truncates when it adds into an fp32 accumulator, so
-// a sum over thousands of products drifts (~K/8 truncations).  Here every
-// accumulator sums only GROUP K blocks; two sets alternate, and the converter
-// warps drain each finished set into fp32 registers (round-to-nearest adds)
-// while the tensor core fills the other.  Measured on the full f32 vocoder
-// (dozens of chained convs, then exp() in the iSTFT) against the oracle:
-// GROUP 4 / 2 / 1 -> 1.2e-5 / 8.9e-6 / 8.1e-6 of max (fp32 CUDA-core convs:
-// 7.6e-6), for a 5% time difference; 1 is the default.
-// ACT: the activation (CV3_ACT_*, -1 none) and SNAKE compiled in, so each
-// instantiation carries only its own epilogue
+// a sum over thousands of products drifts (~K/8 truncations).  Here every main
+// accumulator sums one K block; two alternate, and the converter warps drain
+// each finished one into fp32 registers (round-to-nearest adds) while the tensor
+// core fills the other.
 template <int ACT, bool SNAKE>
 __global__ void __launch_bounds__(THREADS, 1)
-conv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_wlo, ConvArgs a) {
+conv_gather_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_wlo, ConvArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align1024(smem_raw);
   Bars& S = *reinterpret_cast<Bars*>(smem + STAGES * STAGE_BYTES);
   volatile int* abort_flag = &S.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -151,7 +233,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   const int b = blockIdx.z / a.groups, g = blockIdx.z - b * a.groups;
   const int wrow0 = g * a.cout_g + co0;  // first row of Wt
   const int nk = a.k * a.cblocks;
-  const int ngroups = (nk + GROUP - 1) / GROUP;
   const uint32_t tx_bytes = (uint32_t)(a.has_lo ? STAGE_BYTES : TILE_B);
 
   if (threadIdx.x == 0) {
@@ -207,10 +288,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       const int s = kb % STAGES;
       const uint32_t r = (uint32_t)(kb / STAGES);
       const int as = kb & 1;
-      const int q = kb / GROUP, set = q & 1;
-      const bool first = kb == q * GROUP, last = kb == nk - 1 || kb == (q + 1) * GROUP - 1;
-      // a set is reused once its previous group has been drained
-      if (first && q >= 2 && !ready(&S.drained[set], ((uint32_t)(q >> 1) & 1) ^ 1, 8)) {
+      // an accumulator is reused once its previous K block has been drained
+      if (kb >= 2 && !ready(&S.drained[as], ((uint32_t)(kb >> 1) & 1) ^ 1, 8)) {
         ok = false;
         break;
       }
@@ -219,20 +298,19 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
         break;
       }
       fence_after();
-      const uint32_t d_main = tmem + c_main(set), d_cross = tmem + C_CROSS;
+      const uint32_t d_main = tmem + 64u * as, d_cross = tmem + C_CROSS;
       const uint32_t w_raw = smem_u32(smem + s * STAGE_BYTES), w_lo = w_raw + TILE_B;
       const uint32_t a_hi = tmem + C_A + 64u * as, a_lo = a_hi + 32;
 #pragma unroll
       for (int kk = 0; kk < BK / 8; ++kk) {
         const uint32_t off = kk * 32;
-        const uint32_t acc = (first && kk == 0) ? 0u : 1u;
         mma_ts(d_cross, a_lo + 8 * kk, desc_k_sw128(w_raw + off), IDESC, (kb == 0 && kk == 0) ? 0u : 1u);
         if (a.has_lo) mma_ts(d_cross, a_hi + 8 * kk, desc_k_sw128(w_lo + off), IDESC, 1u);
-        mma_ts(d_main, a_hi + 8 * kk, desc_k_sw128(w_raw + off), IDESC, acc);
+        mma_ts(d_main, a_hi + 8 * kk, desc_k_sw128(w_raw + off), IDESC, kk == 0 ? 0u : 1u);
       }
       mma_commit(&S.empty[s]);
       mma_commit(&S.aempty[as]);
-      if (last) mma_commit(&S.accfull[set]);
+      mma_commit(&S.accfull[as]);
     }
     if (!ok && lane == 0) *abort_flag = 1;
     mma_commit(&S.done);  // also on abort: arrives once whatever was issued has completed
@@ -248,16 +326,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     float acc[BN];
 #pragma unroll
     for (int c = 0; c < BN; ++c) acc[c] = 0.f;
-    // fold accumulator set q into acc and hand it back to the MMA warp
+    // fold K block q's accumulator into acc and hand it back to the MMA warp
     auto drain = [&](int q) -> bool {
       const int set = q & 1;
       if (!ready(&S.accfull[set], (uint32_t)(q >> 1) & 1, 5)) return false;
       fence_after();
       float m[BN];
-      tmem_ld64(tmem + lane_base + c_main(set), m);
+      tmem_ld64(tmem + lane_base + 64u * set, m);
 #pragma unroll
       for (int j = 0; j < BN; ++j) acc[j] = __fadd_rn(acc[j], m[j]);
-      if (q == ngroups - 1) {  // the last group's MMAs are the last ones: the remainder sum is final
+      if (q == nk - 1) {  // the last block's MMAs are the last ones: the remainder sum is final
         tmem_ld64(tmem + lane_base + C_CROSS, m);
 #pragma unroll
         for (int j = 0; j < BN; ++j) acc[j] = __fadd_rn(acc[j], m[j]);
@@ -269,7 +347,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     };
     float cur[32], nxt[32];
     if (nk > 0) gather(cur, a, xg, t, 0, vec);
-    int drained = 0;  // groups folded so far
+    int drained = 0;  // K blocks folded so far
     for (int kb = 0; kb < nk; ++kb) {
       if (kb + 1 < nk) gather(nxt, a, xg, t, kb + 1, vec);  // in flight while this block is stored
       const int as = kb & 1;
@@ -290,8 +368,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.afull[as]);
-      // once the A of group q is all stored, group q - 1 is (or soon is) complete
-      if ((kb == nk - 1 || (kb + 1) % GROUP == 0) && kb / GROUP >= 1) {
+      // once block kb's A is stored, block kb - 1 is (or soon is) complete
+      if (kb >= 1) {
         if (!drain(drained)) {
           ok = false;
           break;
@@ -301,49 +379,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
 #pragma unroll
       for (int c = 0; c < 32; ++c) cur[c] = nxt[c];
     }
-    while (ok && drained < ngroups) {
+    while (ok && drained < nk) {
       if (!drain(drained)) ok = false;
       ++drained;
     }
     if (!ok) *abort_flag = 1;
-    if (ok && t < a.t_out) {
-      const bool yvec = a.ysc == 1 && a.yst % 4 == 0 && ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0) &&
-                        (a.ysb % 4 == 0) && (a.cout_g % 4 == 0) &&
-                        (!a.res || (reinterpret_cast<uintptr_t>(a.res) & 15) == 0);
-      const int64_t ybase = (int64_t)b * a.ysb + (int64_t)(g * a.cout_g) * a.ysc + (int64_t)t * a.yst;
-      if (yvec && co0 + BN <= a.cout_g) {
-        // token-major y: this thread's channels are contiguous
-        float* yp = a.y + ybase + co0;
-        const float* rp = a.res ? a.res + ybase + co0 : nullptr;
-#pragma unroll
-        for (int j4 = 0; j4 < BN / 4; ++j4) {
-          float o[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            o[e] = epilogue_value<ACT, SNAKE>(a, g * a.cout_g + co0 + 4 * j4 + e, acc[4 * j4 + e]);
-          if (rp) {
-            const float4 r4 = *reinterpret_cast<const float4*>(rp + 4 * j4);
-            o[0] = __fadd_rn(o[0], r4.x);
-            o[1] = __fadd_rn(o[1], r4.y);
-            o[2] = __fadd_rn(o[2], r4.z);
-            o[3] = __fadd_rn(o[3], r4.w);
-          }
-          *reinterpret_cast<float4*>(yp + 4 * j4) = make_float4(o[0], o[1], o[2], o[3]);
-        }
-      } else {
-        // channel-major y: lanes write consecutive frames of each channel
-#pragma unroll
-        for (int j = 0; j < BN; ++j) {
-          const int co = co0 + j;
-          if (co < a.cout_g) {
-            float o = epilogue_value<ACT, SNAKE>(a, g * a.cout_g + co, acc[j]);
-            const int64_t idx = ybase + (int64_t)co * a.ysc;
-            if (a.res) o = __fadd_rn(o, a.res[idx]);
-            a.y[idx] = o;
-          }
-        }
-      }
-    }
+    if (ok && t < a.t_out) store_row<ACT, SNAKE>(a, acc, b, g, co0, t);
   }
   fence_before();
   __syncthreads();
@@ -360,6 +401,359 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   }
 }
 
+}  // namespace gk
+
+// ---------------------------------------------------------------------------------
+// Window kernel
+// ---------------------------------------------------------------------------------
+namespace wk {
+
+constexpr int THREADS = 384;
+constexpr int MAX_STAGES = 8;            // weight ring (as many stages as shared memory leaves, >= 2)
+constexpr int NSET = 6;                  // main accumulators: K blocks in flight between MMA and drain
+constexpr uint32_t C_CROSS = NSET * 64;  // remainder accumulators of even / odd tiles at 384 / 448
+constexpr int FMAX = 256;                // window rows (TMA box limit)
+
+struct Bars {
+  uint64_t full[MAX_STAGES], empty[MAX_STAGES];
+  uint64_t afull[2], aempty[2];      // A tile pair nb: built / free again
+  uint64_t winfull[2];               // token-major window nb landed in A tile nb
+  uint64_t accfull[NSET], drained[NSET];
+  uint64_t crossdrained[2];
+  uint64_t done;
+  uint32_t tmem;
+  int abort_flag;
+  int issued[MAX_STAGES];
+  int issued_win[2];
+};
+
+struct WinArgs {
+  ConvArgs c;
+  int frames;   // window rows F = 128 + (k - 1) dil
+  int abytes;   // bytes of one A tile (F x 128 B, rounded up to the 1024 B swizzle period)
+  int nx, ny, ntiles;
+  int nstages;      // weight ring depth
+  int stage_bytes;  // 8 KB (W) or 16 KB (W | W lo)
+};
+
+// smem: [W ring | A hi 0 | A hi 1 | A lo 0 | A lo 1 | Bars]
+__host__ __device__ inline int bars_at(int abytes, int nstages, int stage_bytes) {
+  return nstages * stage_bytes + 4 * abytes;
+}
+
+// The A operands are descriptors of the window tiles advanced by whole 128 B rows.
+// The 128 B swizzle is a function of the absolute shared-memory address (chunk bits
+// 4-6 XOR row bits 7-9), the same rule TMA and the builders write with, so such a
+// start needs no base-offset field (measured: filling that field with the row phase
+// scrambles the products).
+
+// byte offset of (frame f, channels 4q..4q+3) in a [frames][32] tile with the 128 B swizzle
+__device__ __forceinline__ int sw_off(int f, int q) { return f * 128 + ((q ^ (f & 7)) << 4); }
+
+__device__ __forceinline__ float4 split_lo(float4 h) {
+  return make_float4(h.x - tf32_hi(h.x), h.y - tf32_hi(h.y), h.z - tf32_hi(h.z), h.w - tf32_hi(h.w));
+}
+
+// LAYOUT 1: channel-major x (frames contiguous); 2: token-major x (channels contiguous)
+template <int ACT, bool SNAKE, int LAYOUT>
+__global__ void __launch_bounds__(THREADS, 1)
+conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_wlo,
+                   const __grid_constant__ CUtensorMap map_x, WinArgs p) {
+  const ConvArgs& a = p.c;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* const abase = smem + p.nstages * p.stage_bytes;  // A hi 0, A hi 1, A lo 0, A lo 1
+  Bars& S = *reinterpret_cast<Bars*>(smem + bars_at(p.abytes, p.nstages, p.stage_bytes));
+  const int ns = p.nstages;
+  volatile int* abort_flag = &S.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = a.k * a.cblocks;
+  const uint32_t tx_bytes = (uint32_t)(a.has_lo ? 2 * TILE_B : TILE_B);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+      S.issued[s] = -1;
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.afull[i], 4);
+      mbar_init(&S.aempty[i], 1);
+      mbar_init(&S.winfull[i], 1);
+      mbar_init(&S.crossdrained[i], 4);
+      S.issued_win[i] = -1;
+    }
+    for (int i = 0; i < NSET; ++i) {
+      mbar_init(&S.accfull[i], 1);
+      mbar_init(&S.drained[i], 4);
+    }
+    mbar_init(&S.done, 1);
+    S.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = S.tmem;
+  // warp-uniform wait: one try_wait and a vote when the phase has completed already
+  auto ready = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+    if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
+    const bool ok = !*abort_flag && bwait(bar, parity, code);
+    return __all_sync(0xffffffffu, ok);
+  };
+  // tile -> first frame, first channel (in the group), batch, group; consecutive tiles
+  // run along time, so CTAs working at the same time share weight tiles in L2
+  auto tile_of = [&](int tile, int& t0, int& co0, int& b, int& g) {
+    const int tx = tile % p.nx, rest = tile / p.nx;
+    const int ty = rest % p.ny, z = rest / p.ny;
+    t0 = tx * BM;
+    co0 = ty * BN;
+    b = z / a.groups;
+    g = z - b * a.groups;
+  };
+
+  if (warp == 0) {
+    // weight tiles, K block by K block, tile after tile
+    if (lane == 0) {
+      int s = 0, r = 0;  // ring slot, and how many times the ring has wrapped
+      bool go = true;
+      for (int tile = blockIdx.x; go && tile < p.ntiles; tile += gridDim.x) {
+        int t0, co0, b, g;
+        tile_of(tile, t0, co0, b, g);
+        const int wrow0 = g * a.cout_g + co0;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (*abort_flag || !bwait(&S.empty[s], (uint32_t)(r & 1) ^ 1, 1)) {
+            *abort_flag = 1;
+            go = false;
+            break;
+          }
+          uint8_t* st = smem + s * p.stage_bytes;
+          S.issued[s] = r;
+          mbar_expect_tx(&S.full[s], tx_bytes);
+          tma_load_2d(st, &map_w, &S.full[s], kb * BK, wrow0);
+          if (a.has_lo) tma_load_2d(st + TILE_B, &map_wlo, &S.full[s], kb * BK, wrow0);
+          if (++s == ns) s = 0, ++r;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    bool ok = true;
+    int gkb = 0, gcb = 0, it = 0, s = 0, r = 0;
+    for (int tile = blockIdx.x; ok && tile < p.ntiles; tile += gridDim.x, ++it) {
+      const int cp = it & 1;
+      // this tile's remainder accumulator was last used two tiles ago: drained by now?
+      if (it >= 2 && !ready(&S.crossdrained[cp], ((uint32_t)(it >> 1) & 1) ^ 1, 12)) {
+        ok = false;
+        break;
+      }
+      const uint32_t d_cross = tmem + C_CROSS + 64u * cp;
+      for (int cb = 0; ok && cb < a.cblocks; ++cb, ++gcb) {
+        const int nb = gcb & 1;
+        if (!ready(&S.afull[nb], (uint32_t)(gcb >> 1) & 1, 3)) {
+          ok = false;
+          break;
+        }
+        // descriptors advance in 16 B units of their start-address field: + 8 per window
+        // row (tap shift), + 2 per k-step of 8 tf32 (the field cannot carry: smem < 256 KB)
+        const uint64_t d_ahi = desc_k_sw128(smem_u32(abase + nb * p.abytes));
+        const uint64_t d_alo = desc_k_sw128(smem_u32(abase + (2 + nb) * p.abytes));
+        for (int j = 0; j < a.k; ++j, ++gkb) {
+          const int set = gkb % NSET;
+          if (gkb >= NSET && !ready(&S.drained[set], ((uint32_t)(gkb / NSET) & 1) ^ 1, 8)) {
+            ok = false;
+            break;
+          }
+          if (!ready(&S.full[s], (uint32_t)r & 1, 2)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t d_main = tmem + 64u * set;
+          const uint64_t d_w = desc_k_sw128(smem_u32(smem + s * p.stage_bytes)), d_wlo = d_w + (TILE_B >> 4);
+          const uint64_t shift = (uint64_t)(j * a.dil) * 8;  // tap j reads the window shifted by j*dil frames
+          const uint32_t first = (cb == 0 && j == 0) ? 0u : 1u;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            mma_ss(d_main, d_ahi + shift + 2 * kk, d_w + 2 * kk, IDESC, kk == 0 ? 0u : 1u);
+            mma_ss(d_cross, d_alo + shift + 2 * kk, d_w + 2 * kk, IDESC, kk == 0 ? first : 1u);
+            if (a.has_lo) mma_ss(d_cross, d_ahi + shift + 2 * kk, d_wlo + 2 * kk, IDESC, 1u);
+          }
+          mma_commit(&S.empty[s]);
+          mma_commit(&S.accfull[set]);
+          if (++s == ns) s = 0, ++r;
+        }
+        if (!ok) break;
+        mma_commit(&S.aempty[nb]);
+      }
+    }
+    if (!ok && lane == 0) *abort_flag = 1;
+    mma_commit(&S.done);  // also on abort: arrives once whatever was issued has completed
+  } else if (warp == 2) {
+    // token-major input windows
+    if (LAYOUT == 2 && lane == 0) {
+      int gcb = 0;
+      bool go = true;
+      for (int tile = blockIdx.x; go && tile < p.ntiles; tile += gridDim.x) {
+        int t0, co0, b, g;
+        tile_of(tile, t0, co0, b, g);
+        const int wstart = t0 - a.pad_l;  // window row 0 = input frame of output t0, tap 0
+        const int ch0 = g * a.cin_g;
+        for (int cb = 0; cb < a.cblocks; ++cb, ++gcb) {
+          const int nb = gcb & 1;
+          if (*abort_flag || !bwait(&S.aempty[nb], ((uint32_t)(gcb >> 1) & 1) ^ 1, 9)) {
+            *abort_flag = 1;
+            go = false;
+            break;
+          }
+          S.issued_win[nb] = gcb >> 1;
+          mbar_expect_tx(&S.winfull[nb], (uint32_t)(p.frames * 128));
+          tma_load_3d(abase + nb * p.abytes, &map_x, &S.winfull[nb], ch0 + 32 * cb, wstart, b);
+        }
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // builders: window frames tid and tid + 128
+    const int tid = threadIdx.x - 128;
+    int gcb = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.ntiles; tile += gridDim.x) {
+      int t0, co0, b, g;
+      tile_of(tile, t0, co0, b, g);
+      const int wstart = t0 - a.pad_l;
+      const int ch0 = g * a.cin_g;
+      for (int cb = 0; cb < a.cblocks; ++cb, ++gcb) {
+        const int nb = gcb & 1;
+        const int nval = a.cin_g - 32 * cb;  // channels of this block inside the group (>= 32: all)
+        uint8_t* hb = abase + nb * p.abytes;
+        uint8_t* lb = abase + (2 + nb) * p.abytes;
+        if (LAYOUT == 1) {
+          // the block's inputs for frames tid and tid + 128, in flight during the wait below
+          const float* xc = a.x + (int64_t)b * a.xsb + (int64_t)(ch0 + 32 * cb) * a.xsc;
+          float v0[32], v1[32];
+          const int f1 = tid + 128;
+          const bool has1 = f1 < p.frames;
+          const int t0f = wstart + tid, t1f = wstart + f1;
+          const bool in0 = t0f >= 0 && t0f < a.t_in, in1 = has1 && t1f >= 0 && t1f < a.t_in;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float* pc = xc + (int64_t)c * a.xsc;
+            v0[c] = (in0 && c < nval) ? __ldg(pc + t0f) : 0.f;
+            v1[c] = (in1 && c < nval) ? __ldg(pc + t1f) : 0.f;
+          }
+          if (!ready(&S.aempty[nb], ((uint32_t)(gcb >> 1) & 1) ^ 1, 4)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 h = make_float4(v0[4 * q], v0[4 * q + 1], v0[4 * q + 2], v0[4 * q + 3]);
+            *reinterpret_cast<float4*>(hb + sw_off(tid, q)) = h;
+            *reinterpret_cast<float4*>(lb + sw_off(tid, q)) = split_lo(h);
+          }
+          if (has1) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 h = make_float4(v1[4 * q], v1[4 * q + 1], v1[4 * q + 2], v1[4 * q + 3]);
+              *reinterpret_cast<float4*>(hb + sw_off(f1, q)) = h;
+              *reinterpret_cast<float4*>(lb + sw_off(f1, q)) = split_lo(h);
+            }
+          }
+        } else {
+          if (!ready(&S.aempty[nb], ((uint32_t)(gcb >> 1) & 1) ^ 1, 4) ||
+              !ready(&S.winfull[nb], (uint32_t)(gcb >> 1) & 1, 10)) {
+            ok = false;
+            break;
+          }
+          for (int f = tid; f < p.frames; f += 128) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float4 h = *reinterpret_cast<const float4*>(hb + sw_off(f, q));
+              if (4 * q >= nval) {  // the next group's channels (or nothing): zero
+                h = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4*>(hb + sw_off(f, q)) = h;
+              }
+              *reinterpret_cast<float4*>(lb + sw_off(f, q)) = split_lo(h);
+            }
+          }
+        }
+        // order these generic-proxy writes before the tensor core's reads
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.afull[nb]);
+      }
+    }
+    if (!ok) *abort_flag = 1;
+  } else if (warp >= 8) {
+    // drainers + epilogue: thread = output frame t0 + row (its TMEM lane)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    int gkb = 0, it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.ntiles; tile += gridDim.x, ++it) {
+      int t0, co0, b, g;
+      tile_of(tile, t0, co0, b, g);
+      const int cp = it & 1;
+      float acc[BN];
+#pragma unroll
+      for (int c = 0; c < BN; ++c) acc[c] = 0.f;
+      for (int kb = 0; kb < nk; ++kb, ++gkb) {
+        const int set = gkb % NSET;
+        if (!ready(&S.accfull[set], (uint32_t)(gkb / NSET) & 1, 5)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        float m[BN];
+        tmem_ld64(tmem + lane_base + 64u * set, m);
+#pragma unroll
+        for (int j = 0; j < BN; ++j) acc[j] = __fadd_rn(acc[j], m[j]);
+        const bool last = kb == nk - 1;  // its MMAs are the tile's last: the remainder sum is final
+        if (last) {
+          tmem_ld64(tmem + lane_base + C_CROSS + 64u * cp, m);
+#pragma unroll
+          for (int j = 0; j < BN; ++j) acc[j] = __fadd_rn(acc[j], m[j]);
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&S.drained[set]);
+          if (last) mbar_arrive(&S.crossdrained[cp]);
+        }
+      }
+      if (!ok) break;
+      const int t = t0 + row;
+      if (t < a.t_out) store_row<ACT, SNAKE>(a, acc, b, g, co0, t);
+    }
+    if (!ok) *abort_flag = 1;
+  }
+  fence_before();
+  __syncthreads();
+  if (LAYOUT == 2 && warp == 2 && lane == 0 && *abort_flag) {  // window loads still in flight land first
+    for (int i = 0; i < 2; ++i)
+      if (S.issued_win[i] >= 0) bwait(&S.winfull[i], (uint32_t)S.issued_win[i] & 1, 11);
+  }
+  if (warp == 0) {
+    if (lane == 0) {
+      if (*abort_flag)
+        for (int s = 0; s < ns; ++s)
+          if (S.issued[s] >= 0) bwait(&S.full[s], (uint32_t)S.issued[s] & 1, 6);
+      bwait(&S.done, 0, 7);
+    }
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+  }
+}
+
+}  // namespace wk
+
 int make_w_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t kp, int box_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
   CV3_REQUIRE(encode != nullptr, CV3_ERR_CUDA, "conv1d_tc: cuTensorMapEncodeTiled is unavailable");
@@ -375,17 +769,55 @@ int make_w_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t kp, int
   return CV3_OK;
 }
 
+// Token-major x as (channels, frames, batch) with boxes of 32 channels x `frames`,
+// 128 B-swizzled: the window lands as the kernel's A tile.  False when the strides
+// are not 16-byte multiples.
+bool make_x_map_tokens(CUtensorMap* map, const float* x, int64_t xsb, int64_t xst, int64_t batch, int64_t cin,
+                       int64_t t_in, int frames) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  if (!encode || ((uintptr_t)x & 15)) return false;
+  const int64_t sb = batch > 1 ? xsb : xst * t_in;
+  if (xst % 4 || sb % 4 || xst <= 0 || sb <= 0) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)cin, (cuuint64_t)t_in, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(xst * 4), (cuuint64_t)(sb * 4)};
+  cuuint32_t box[3] = {32, (cuuint32_t)frames, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)x, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int g_window_enabled = 1;
+int g_last_path = -1;  // kernel of the last launch: 0 gather, 1 / 2 window (channel- / token-major)
+
 __global__ void conv_weight_kernel(const float* __restrict__ w, int cout, int cin_g, int k, int ci_pad,
                                    float* __restrict__ wt, float* __restrict__ wt_lo) {
   const int64_t total = (int64_t)cout * k * ci_pad;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int ci = (int)(i % ci_pad);
-    const int j = (int)((i / ci_pad) % k);
+    // Wt[co][cb][j][32]
+    const int ci = (int)((i / (32 * k)) % (ci_pad / 32)) * 32 + (int)(i % 32);
+    const int j = (int)((i / 32) % k);
     const int co = (int)(i / ((int64_t)ci_pad * k));
     const float v = ci < cin_g ? w[((int64_t)co * cin_g + ci) * k + j] : 0.f;
     wt[i] = v;
     if (wt_lo) wt_lo[i] = v - tf32_hi(v);
   }
+}
+
+using GatherFn = void (*)(const CUtensorMap, const CUtensorMap, ConvArgs);
+using WindowFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, wk::WinArgs);
+
+template <int ACT>
+GatherFn gather_fn(bool sn) {
+  return sn ? gk::conv_gather_kernel<ACT, true> : gk::conv_gather_kernel<ACT, false>;
+}
+
+// token-major inputs come from the DiT (no snake): that layout is built without one
+template <int ACT>
+WindowFn window_fn(bool sn, int layout) {
+  if (layout == 1) return sn ? wk::conv_window_kernel<ACT, true, 1> : wk::conv_window_kernel<ACT, false, 1>;
+  return sn ? nullptr : wk::conv_window_kernel<ACT, false, 2>;
 }
 
 }  // namespace
@@ -418,36 +850,90 @@ extern "C" int cv3_conv1d_tc(const float* x, int64_t xsb, int64_t xsc, int64_t x
   if (batch == 0 || t_out == 0) return CV3_OK;
   CV3_REQUIRE(t_in < (1LL << 30) && t_out < (1LL << 30) && k * ci_pad < (1LL << 30), CV3_ERR_VALUE,
               "conv1d_tc: too large");
+  CV3_REQUIRE(act == -1 || act == CV3_ACT_MISH || act == CV3_ACT_ELU || act == CV3_ACT_LEAKY_RELU,
+              CV3_ERR_UNSUPPORTED, "conv1d_tc: activation %d not built into the conv epilogue", act);
+  const int64_t nx = (t_out + BM - 1) / BM, ny = (cout_g + BN - 1) / BN, nz = batch * groups;
+  CV3_REQUIRE(ny <= 65535 && nz <= 65535, CV3_ERR_VALUE, "conv1d_tc: grid too large");
+  CV3_REQUIRE(cin_g * xsc < (1LL << 31) && t_in * xst + cin * xsc < (1LL << 31), CV3_ERR_VALUE,
+              "conv1d_tc: one (batch, group) slab of x must span < 2^31 elements");
   CUtensorMap mw, mwl;
   int rc = make_w_map(&mw, wt, cout, k * ci_pad, BN);
   if (rc) return rc;
   rc = make_w_map(&mwl, wt_lo ? wt_lo : wt, cout, k * ci_pad, BN);
   if (rc) return rc;
-  CV3_REQUIRE(act >= -1 && act <= CV3_ACT_EXP, CV3_ERR_VALUE, "conv1d_tc: unknown activation %d", act);
-  ConvArgs a{x, xsb, xsc, xst, y, ysb, ysc, yst, bias, snake_alpha, residual, act, act_param,
-             (int)cin_g, (int)t_in, (int)cout_g, (int)t_out,
-             (int)k, (int)stride, (int)dilation, (int)pad_left, (int)groups, (int)(ci_pad / 32), wt_lo ? 1 : 0};
-  dim3 grid((unsigned)((t_out + BM - 1) / BM), (unsigned)((cout_g + BN - 1) / BN), (unsigned)(batch * groups));
-  CV3_REQUIRE(grid.y <= 65535 && grid.z <= 65535, CV3_ERR_VALUE, "conv1d_tc: grid too large");
-  CV3_REQUIRE(cin_g * xsc < (1LL << 31) && t_in * xst + cin * xsc < (1LL << 31), CV3_ERR_VALUE,
-              "conv1d_tc: one (batch, group) slab of x must span < 2^31 elements");
-  using Fn = void (*)(const CUtensorMap, const CUtensorMap, ConvArgs);
-  Fn fn = nullptr;
+  const ConvArgs a{x, xsb, xsc, xst, y, ysb, ysc, yst, bias, snake_alpha, residual, act, act_param,
+                   (int)cin_g, (int)t_in, (int)cout_g, (int)t_out,
+                   (int)k, (int)stride, (int)dilation, (int)pad_left, (int)groups, (int)(ci_pad / 32), wt_lo ? 1 : 0};
   const bool sn = snake_alpha != nullptr;
-  switch (act) {
-    case -1: fn = sn ? conv_tc_kernel<-1, true> : conv_tc_kernel<-1, false>; break;
-    case CV3_ACT_MISH: fn = sn ? conv_tc_kernel<CV3_ACT_MISH, true> : conv_tc_kernel<CV3_ACT_MISH, false>; break;
-    case CV3_ACT_ELU: fn = sn ? conv_tc_kernel<CV3_ACT_ELU, true> : conv_tc_kernel<CV3_ACT_ELU, false>; break;
-    case CV3_ACT_LEAKY_RELU:
-      fn = sn ? conv_tc_kernel<CV3_ACT_LEAKY_RELU, true> : conv_tc_kernel<CV3_ACT_LEAKY_RELU, false>;
-      break;
-    default: break;
+
+  // window kernel: stride 1 and a window of <= 256 rows
+  const int64_t frames = BM + (k - 1) * dilation;
+  const int64_t ntiles = nx * ny * nz;
+  if (g_window_enabled && stride == 1 && ntiles < (1LL << 31)) {
+    wk::WinArgs p{};
+    CUtensorMap mx;
+    std::memset(&mx, 0, sizeof(mx));
+    int layout = 0;
+    if (xst == 1 && frames <= wk::FMAX) {
+      layout = 1;
+    } else if (xsc == 1 && frames <= wk::FMAX && cin_g % 4 == 0 &&
+               make_x_map_tokens(&mx, x, xsb, xst, batch, cin, t_in, (int)frames)) {
+      layout = 2;
+    }
+    WindowFn fn = nullptr;
+    if (layout) {
+      switch (act) {
+        case -1: fn = window_fn<-1>(sn, layout); break;
+        case CV3_ACT_MISH: fn = window_fn<CV3_ACT_MISH>(sn, layout); break;
+        case CV3_ACT_ELU: fn = window_fn<CV3_ACT_ELU>(sn, layout); break;
+        default: fn = window_fn<CV3_ACT_LEAKY_RELU>(sn, layout); break;
+      }
+    }
+    p.c = a;
+    p.frames = (int)frames;
+    p.abytes = (int)((frames * 128 + 1023) / 1024 * 1024);
+    p.nx = (int)nx;
+    p.ny = (int)ny;
+    p.ntiles = (int)ntiles;
+    // the weight ring takes what the windows leave: deep rings hide the L2 latency of
+    // one 8 KB (16 KB with the remainder) tile per K block
+    p.stage_bytes = wt_lo ? 2 * TILE_B : TILE_B;
+    const int fixed = wk::bars_at(p.abytes, 0, 0) + (int)sizeof(wk::Bars) + 1024;
+    p.nstages = std::min(wk::MAX_STAGES, (SMEM_MAX - fixed) / p.stage_bytes);
+    const int smem = fixed + p.nstages * p.stage_bytes;
+    if (fn && p.nstages >= 2) {
+      rc = cv3::allow_smem((const void*)fn, smem);
+      if (rc) return rc;
+      const int grid = (int)std::min<int64_t>(ntiles, cv3::sm_count());
+      g_last_path = layout;
+      fn<<<grid, wk::THREADS, smem, cv3::as_stream(stream)>>>(mw, mwl, mx, p);
+      return cv3::check_launch("conv1d_tc");
+    }
   }
-  CV3_REQUIRE(fn != nullptr, CV3_ERR_UNSUPPORTED, "conv1d_tc: activation %d not built into the conv epilogue", act);
-  rc = cv3::allow_smem((const void*)fn, SMEM);
+
+  GatherFn fn;
+  switch (act) {
+    case -1: fn = gather_fn<-1>(sn); break;
+    case CV3_ACT_MISH: fn = gather_fn<CV3_ACT_MISH>(sn); break;
+    case CV3_ACT_ELU: fn = gather_fn<CV3_ACT_ELU>(sn); break;
+    default: fn = gather_fn<CV3_ACT_LEAKY_RELU>(sn); break;
+  }
+  rc = cv3::allow_smem((const void*)fn, gk::SMEM);
   if (rc) return rc;
-  fn<<<grid, THREADS, SMEM, cv3::as_stream(stream)>>>(mw, mwl, a);
+  g_last_path = 0;
+  dim3 grid((unsigned)nx, (unsigned)ny, (unsigned)nz);
+  fn<<<grid, gk::THREADS, gk::SMEM, cv3::as_stream(stream)>>>(mw, mwl, a);
   return cv3::check_launch("conv1d_tc");
+}
+
+extern "C" int cv3_conv_tc_set_window(int enable) {
+  g_window_enabled = enable ? 1 : 0;
+  return CV3_OK;
+}
+
+extern "C" int cv3_conv_tc_last_path(int* path) {
+  if (path) *path = g_last_path;
+  return CV3_OK;
 }
 
 extern "C" int cv3_tc_conv_status(int* code) {

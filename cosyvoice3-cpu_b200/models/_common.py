@@ -84,7 +84,7 @@ class Lin:
 
 
 class ConvTC:
-    """A conv1d weight in the tensor-core layout (``cv3_conv_weight_tc``): Wt[C_out][k][ci_pad]
+    """A conv1d weight in the tensor-core layout (``cv3_conv_weight_tc``): Wt[C_out][ci_pad/32][k][32]
     plus the tf32 remainder when the weight is not exactly tf32 (fp16-stored weights are)."""
 
     __slots__ = ("wt", "lo", "cout", "cin_g", "k", "groups", "ci_pad", "bias")
@@ -96,8 +96,8 @@ class ConvTC:
         self.groups = int(groups)
         self.ci_pad = (self.cin_g + 31) // 32 * 32
         s = stream if stream is not None else D.stream()
-        self.wt = D.empty((self.cout, self.k, self.ci_pad))
-        lo = D.empty((self.cout, self.k, self.ci_pad))
+        self.wt = D.empty((self.cout, self.ci_pad // 32, self.k, 32))
+        lo = D.empty((self.cout, self.ci_pad // 32, self.k, 32))
         w = w.contiguous()
         call("cv3_conv_weight_tc", w.data_ptr(), self.cout, self.cin_g, self.k, self.ci_pad, self.wt.data_ptr(),
              lo.data_ptr(), s)

@@ -396,7 +396,7 @@ int cv3_tc_gemm_split(const float* a, int64_t lda, const float* b, const float* 
                       int64_t rows_per_group, int64_t gate_stride, void* stream);
 
 /* Rearrange conv weights W[C_out][C_in/groups][k] into the tensor-core
- * layout Wt[C_out][k][ci_pad] (ci_pad = C_in/groups rounded up to 32, zero
+ * layout Wt[C_out][ci_pad/32][k][32] (ci_pad = C_in/groups rounded up to 32, zero
  * filled) and, if wt_lo is not NULL, the tf32 remainders.  Done once per
  * weight; weights that are exact tf32 values (fp16-stored) need no remainder. */
 int cv3_conv_weight_tc(const float* w, int64_t cout, int64_t cin_g, int64_t k, int64_t ci_pad, float* wt,
@@ -418,6 +418,16 @@ int cv3_conv1d_tc(const float* x, int64_t xsb, int64_t xsc, int64_t xst, int64_t
 
 /* Error word of the tensor-core conv kernel (see cv3_tc_gemm_status). */
 int cv3_tc_conv_status(int* code);
+
+/* Input path of cv3_conv1d_tc: 1 (default) stages each channel block's input
+ * window in shared memory by TMA when the strides allow it (16-byte multiples)
+ * and the window fits 256 frames, else gathers from global memory; 0 always
+ * gathers.  Both give the same results; the switch exists to test both paths. */
+int cv3_conv_tc_set_window(int enable);
+
+/* Input path the last cv3_conv1d_tc launch took: 0 gather, 1 channel-major
+ * window, 2 token-major window (-1 before the first launch). */
+int cv3_conv_tc_last_path(int* path);
 
 /* Persistent greedy decode of the Qwen2 speech LM (cv3cpu/models/qwen2.py:
  * 139-179 per token, llm.py:114 head + greedy pick): `steps` tokens for a

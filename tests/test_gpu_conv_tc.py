@@ -5,8 +5,11 @@ weight is an exact tf32 value, as the vocoder's fp16-stored weights are).
 Cases: the vocoder's resblock / upsample / source-down geometries (dilation,
 stride, causal left pads), the DiT's grouped k=31 position conv in token-major
 layout, input-channel counts that are not multiples of 32, short signals, and
-each fused epilogue (activation, snake, residual in place).  Bar: max |got -
-ref| / max |ref| <= 1e-5, the fp32 bar; the error word must stay clear.
+each fused epilogue (activation, snake, residual in place).  Both kernels
+run: the window kernel (stride 1 with a window of 128 + (k-1) dil <= 256
+frames; A operands are shifted views of one staged window) and the gather kernel (forced with cv3_conv_tc_set_window(0),
+and taken by itself otherwise); each case checks which kernel ran.  Bar: max |got - ref| / max |ref| <= 1e-5, the
+fp32 bar; the error word must stay clear.
 """
 
 import ctypes
@@ -23,9 +26,34 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-5
 
 
+@pytest.fixture(params=[1, 0], ids=["window", "gather"])
+def window(request):
+    lib = pkg("_lib").load()
+    lib.cv3_conv_tc_set_window(request.param)
+    yield request.param
+    lib.cv3_conv_tc_set_window(1)
+
+
+def _last_path():
+    p = ctypes.c_int(-9)
+    pkg("_lib").load().cv3_conv_tc_last_path(ctypes.byref(p))
+    return p.value
+
+
+def _window_path(T, t_out, k, stride, dil, token_major, cin_g):
+    """The kernel the host dispatch should pick with windows enabled (see cv3_conv1d_tc)."""
+    frames = 128 + (k - 1) * dil
+    if stride != 1:
+        return 0
+    if not token_major:
+        return 1 if frames <= 256 else 0
+    return 2 if frames <= 256 and cin_g % 4 == 0 else 0
+
+
 def _conv_tc(x, w, bias, stride=1, dilation=1, groups=1, pad=(0, 0), act=-1, act_p=0.0, alpha=None,
-             residual=None, token_major=False, fp16_weights=False):
-    """Run the device conv on host arrays x (B, C_in, T); returns (B, C_out, T_out)."""
+             residual=None, token_major=False, fp16_weights=False, window=None):
+    """Run the device conv on host arrays x (B, C_in, T); returns (B, C_out, T_out).
+    With ``window`` given (the fixture's switch), checks the input path the launch took."""
     import torch
     common = pkg("models._common")
     B, cin, T = x.shape
@@ -52,6 +80,9 @@ def _conv_tc(x, w, bias, stride=1, dilation=1, groups=1, pad=(0, 0), act=-1, act
     cv(xd, y, B, T, t_out, stride=stride, dilation=dilation, pad_left=pad[0],
        residual=y if residual is not None else None, xs=xs, ys=ys, act=act, act_param=act_p, snake_alpha=ad)
     torch.cuda.synchronize()
+    if window is not None:
+        want = _window_path(T, t_out, k, stride, dilation, token_major, cin_g) if window else 0
+        assert _last_path() == want
     code = ctypes.c_int(-1)
     assert pkg("_lib").load().cv3_tc_conv_status(ctypes.byref(code)) == 0 and code.value == 0
     out = y.cpu().numpy()
@@ -73,30 +104,57 @@ def _data(rng, B, cin, T, cout, cin_g, k, fp16=False):
 
 @pytest.mark.parametrize("B,cin,T,cout,k,stride,dil,pad,fp16", [
     (2, 256, 300, 256, 7, 1, 3, (18, 0), True),     # resblock conv, dilated, causal pad
-    (2, 128, 700, 128, 11, 1, 5, (50, 0), True),
+    (2, 128, 700, 128, 11, 1, 5, (50, 0), True),    # window: 178 frames, negative first coordinate
     (1, 64, 1000, 64, 3, 1, 1, (2, 0), True),       # BN = 64 tile
     (2, 80, 120, 512, 5, 1, 1, (0, 4), False),      # conv_pre: 80 channels (not a multiple of 32), right pad
-    (2, 18, 601, 256, 14, 5, 1, (4, 0), True),      # strided source down-sampling
-    (1, 512, 50, 80, 7, 1, 1, (6, 0), False),       # few frames, C_out not a tile multiple
+    (2, 18, 601, 256, 14, 5, 1, (4, 0), True),      # strided source down-sampling (gather kernel)
+    (1, 512, 50, 80, 7, 1, 1, (6, 0), False),       # few frames (odd row pitch), C_out not a tile multiple
     (3, 96, 129, 200, 1, 1, 1, (0, 0), False),      # 1x1, ragged frames and channels
+    (2, 64, 1004, 64, 16, 1, 1, (15, 0), True),     # upsample conv (k = 16), last tile partial
+    (1, 40, 200, 72, 3, 2, 1, (1, 0), False),       # stride 2 (gather kernel), 40 channels
+    (2, 128, 64, 128, 11, 1, 5, (50, 0), True),     # one short tile
+    (2, 64, 30001, 64, 11, 1, 5, (50, 0), True),    # vocoder's last stage: odd frame count, many tiles per CTA
+    (1, 32, 500, 32, 3, 1, 65, (130, 0), True),     # window of 128 + 130 = 258 frames: gather kernel
+    (1, 32, 500, 32, 3, 1, 64, (128, 0), True),     # 128 + 128 = 256 frames: the widest window
 ])
-def test_conv_tc_channel_major(B, cin, T, cout, k, stride, dil, pad, fp16):
+def test_conv_tc_channel_major(B, cin, T, cout, k, stride, dil, pad, fp16, window):
     rng = np.random.default_rng(cin * 7 + T)
     x, w, b = _data(rng, B, cin, T, cout, cin, k, fp16)
-    got = _conv_tc(x, w, b, stride, dil, 1, pad, fp16_weights=fp16)
+    got = _conv_tc(x, w, b, stride, dil, 1, pad, fp16_weights=fp16, window=window)
     assert rel_err(got, _ref(x, w, b, stride, dil, 1, pad)) < TOL
 
 
-def test_conv_tc_grouped_token_major_position_conv():
+def test_conv_tc_grouped_token_major_position_conv(window):
     """The DiT's conv position embedding: 1024 channels, 16 groups, k = 31, causal pad,
     token-major (B, T, C) in and out, mish fused, residual added in place."""
     rng = np.random.default_rng(5)
     B, C, T, k, g = 2, 1024, 150, 31, 16
     x, w, b = _data(rng, B, C, T, C, C // g, k)
     h = rng.normal(size=(B, C, T)).astype(np.float32)
-    got = _conv_tc(x, w, b, groups=g, pad=(k - 1, 0), act=4, residual=h, token_major=True)
+    got = _conv_tc(x, w, b, groups=g, pad=(k - 1, 0), act=4, residual=h, token_major=True, window=window)
     ref = h + nx.mish(_ref(x, w, b, groups=g, pad=(k - 1, 0)))
     assert rel_err(got, ref) < TOL
+
+
+@pytest.mark.parametrize("B,C,T,k,g,act", [
+    (1, 1024, 333, 31, 16, -1),   # three CTAs along time, no activation
+    (3, 256, 40, 5, 4, 4),        # short signal, 64-channel groups
+    (2, 96, 200, 3, 2, -1),       # 48-channel groups: the second channel block is partly masked
+])
+def test_conv_tc_token_major_shapes(B, C, T, k, g, act, window):
+    rng = np.random.default_rng(T + k)
+    x, w, b = _data(rng, B, C, T, C, C // g, k)
+    got = _conv_tc(x, w, b, groups=g, pad=(k - 1, 0), act=act, token_major=True, window=window)
+    ref = _ref(x, w, b, groups=g, pad=(k - 1, 0))
+    assert rel_err(got, nx.mish(ref) if act == 4 else ref) < TOL
+
+
+def test_conv_tc_grouped_channel_major(window):
+    """Groups in channel-major layout: each group's window starts at its own channel."""
+    rng = np.random.default_rng(21)
+    x, w, b = _data(rng, 2, 96, 260, 64, 48, 5)
+    got = _conv_tc(x, w, b, groups=2, pad=(4, 0), window=window)
+    assert rel_err(got, _ref(x, w, b, groups=2, pad=(4, 0))) < TOL
 
 
 @pytest.mark.parametrize("act,p,fn", [(4, 0.0, nx.mish), (5, 1.0, lambda v: nx.elu(v, 1.0)),
