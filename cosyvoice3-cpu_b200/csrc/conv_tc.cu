@@ -450,6 +450,65 @@ __host__ __device__ inline int bars_at(int abytes, int nstages, int stage_bytes)
 // byte offset of (frame f, channels 4q..4q+3) in a [frames][32] tile with the 128 B swizzle
 __device__ __forceinline__ int sw_off(int f, int q) { return f * 128 + ((q ^ (f & 7)) << 4); }
 
+// One K block of the window kernel from one elected thread: for k-steps kk = 0..3
+// (descriptor start + 2 kk), main += A hi x W (fresh at kk = 0) and remainder +=
+// A lo x W (+ A hi x W lo with LO), then the two commits (weight slot free, K block's
+// accumulator complete).  One asm block: a single elect and no per-MMA bookkeeping
+// between the eight (twelve) issues.
+template <bool LO>
+__device__ __forceinline__ void issue_kblock(uint32_t d_main, uint32_t d_cross, uint64_t a_hi, uint64_t a_lo,
+                                             uint64_t w, uint64_t w_lo, uint32_t cross_acc, uint64_t* bar_empty,
+                                             uint64_t* bar_acc) {
+  if (LO) {
+    asm volatile(
+        "{\n\t.reg .pred e, pf, pt, pc;\n\t.reg .b64 h1, h2, h3, l1, l2, l3, w1, w2, w3, v0, v1, v2, v3;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 pf, %4, %4;\n\tsetp.eq.b32 pt, %4, %4;\n\tsetp.ne.b32 pc, %4, 0;\n\t"
+        "add.s64 h1, %5, 2;\n\tadd.s64 h2, %5, 4;\n\tadd.s64 h3, %5, 6;\n\t"
+        "add.s64 l1, %6, 2;\n\tadd.s64 l2, %6, 4;\n\tadd.s64 l3, %6, 6;\n\t"
+        "add.s64 w1, %7, 2;\n\tadd.s64 w2, %7, 4;\n\tadd.s64 w3, %7, 6;\n\t"
+        "mov.b64 v0, %8;\n\tadd.s64 v1, %8, 2;\n\tadd.s64 v2, %8, 4;\n\tadd.s64 v3, %8, 6;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %5, %7, %2, pf;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], %6, %7, %2, pc;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], %5, v0, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], h1, w1, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l1, w1, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], h1, v1, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], h2, w2, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l2, w2, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], h2, v2, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], h3, w3, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l3, w3, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], h3, v3, %2, pt;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%3];\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%9];\n\t}" ::"r"(d_main),
+        "r"(d_cross), "r"(IDESC), "r"(smem_u32(bar_empty)), "r"(cross_acc), "l"(a_hi), "l"(a_lo), "l"(w), "l"(w_lo),
+        "r"(smem_u32(bar_acc))
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e, pf, pt, pc;\n\t.reg .b64 h1, h2, h3, l1, l2, l3, w1, w2, w3;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 pf, %4, %4;\n\tsetp.eq.b32 pt, %4, %4;\n\tsetp.ne.b32 pc, %4, 0;\n\t"
+        "add.s64 h1, %5, 2;\n\tadd.s64 h2, %5, 4;\n\tadd.s64 h3, %5, 6;\n\t"
+        "add.s64 l1, %6, 2;\n\tadd.s64 l2, %6, 4;\n\tadd.s64 l3, %6, 6;\n\t"
+        "add.s64 w1, %7, 2;\n\tadd.s64 w2, %7, 4;\n\tadd.s64 w3, %7, 6;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %5, %7, %2, pf;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], %6, %7, %2, pc;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], h1, w1, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l1, w1, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], h2, w2, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l2, w2, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], h3, w3, %2, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l3, w3, %2, pt;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%3];\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%8];\n\t}" ::"r"(d_main),
+        "r"(d_cross), "r"(IDESC), "r"(smem_u32(bar_empty)), "r"(cross_acc), "l"(a_hi), "l"(a_lo), "l"(w),
+        "r"(smem_u32(bar_acc))
+        : "memory");
+  }
+}
+
 __device__ __forceinline__ float4 split_lo(float4 h) {
   return make_float4(h.x - tf32_hi(h.x), h.y - tf32_hi(h.y), h.z - tf32_hi(h.z), h.w - tf32_hi(h.w));
 }
@@ -544,6 +603,7 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
     }
   } else if (warp == 1) {
     bool ok = true;
+    const bool has_lo = a.has_lo != 0;
     int gkb = 0, gcb = 0, it = 0, s = 0, r = 0;
     for (int tile = blockIdx.x; ok && tile < p.ntiles; tile += gridDim.x, ++it) {
       const int cp = it & 1;
@@ -578,14 +638,12 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
           const uint64_t d_w = desc_k_sw128(smem_u32(smem + s * p.stage_bytes)), d_wlo = d_w + (TILE_B >> 4);
           const uint64_t shift = (uint64_t)(j * a.dil) * 8;  // tap j reads the window shifted by j*dil frames
           const uint32_t first = (cb == 0 && j == 0) ? 0u : 1u;
-#pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            mma_ss(d_main, d_ahi + shift + 2 * kk, d_w + 2 * kk, IDESC, kk == 0 ? 0u : 1u);
-            mma_ss(d_cross, d_alo + shift + 2 * kk, d_w + 2 * kk, IDESC, kk == 0 ? first : 1u);
-            if (a.has_lo) mma_ss(d_cross, d_ahi + shift + 2 * kk, d_wlo + 2 * kk, IDESC, 1u);
-          }
-          mma_commit(&S.empty[s]);
-          mma_commit(&S.accfull[set]);
+          if (has_lo)
+            issue_kblock<true>(d_main, d_cross, d_ahi + shift, d_alo + shift, d_w, d_wlo, first, &S.empty[s],
+                               &S.accfull[set]);
+          else
+            issue_kblock<false>(d_main, d_cross, d_ahi + shift, d_alo + shift, d_w, d_wlo, first, &S.empty[s],
+                                &S.accfull[set]);
           if (++s == ns) s = 0, ++r;
         }
         if (!ok) break;

@@ -271,21 +271,86 @@ int make_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int
 // ---------------------------------------------------------------------------
 namespace split {
 
+// Pre-split GEMM: B comes with its tf32 remainder (cv3_tf32_lo, once per weight);
+// A's remainder is made on the fly.  The tensor core truncates its fp32 inputs to
+// tf32, so the raw TMA tiles serve as the hi operands.  (Splitting B on the fly
+// too halves the TMA bytes of B but doubles the converters' work per K block;
+// measured 8% slower.)
+//
+// MMA cost model (measured on B200, M = 128, K = 8 tf32 per instruction): an
+// MMA into an accumulator that the previous one also wrote waits ~130 cycles;
+// independent accumulators interleaved round-robin bring it to ~77 cycles with
+// four of them, for N = 64 and 128 alike.  So the twelve MMAs of a K block go to
+// four accumulators in turn: hi*hi of even K blocks, hi*hi of odd K blocks, lo*hi,
+// hi*lo.  Splitting hi*hi over two accumulators also halves the sum each one
+// holds, which bounds the tensor core's truncating adds (the reason the split was
+// introduced; the epilogue adds the four in fp32).  All four live in TMEM (512
+// columns), so A's remainder goes to shared memory and every MMA is the SS form.
+//
+// Persistent CTAs (one per SM) walk 128 x 128 output tiles; 14 warps:
+//   warp 0     TMA: A, B, B lo tiles into a 4-stage ring, tile after tile;
+//   warp 1     MMA issuer (converged warp, one elected thread, one asm block per
+//              K block);
+//   warps 2-5  converters: A lo = A - tf32(A) of each landed stage into a
+//              2-buffer ring in the same swizzled layout;
+//   warps 6-13 epilogue, two per TMEM lane quarter (64 columns each): as soon
+//              as a tile's MMAs finish, fold its four accumulators into fp32
+//              registers and hand TMEM back, then run bias / GELU / gated
+//              residual and the stores while the MMA warp already works on the
+//              next tile.
 constexpr int BM = 128, BN = 128, BK = 32, STAGES = 4;
 constexpr int TILE_A = BM * BK * 4;               // 16 KB
 constexpr int TILE_B = BN * BK * 4;               // 16 KB
-constexpr int STAGE_BYTES = TILE_A + 2 * TILE_B;  // A | raw B | B lo
-constexpr int THREADS = 192;
-constexpr uint32_t C_MAIN0 = 0, C_MAIN1 = 128, C_CROSS = 256, C_A = 384;
+constexpr int STAGE_BYTES = TILE_A + 2 * TILE_B;  // A | B | B lo
+constexpr int LO_AT = STAGES * STAGE_BYTES;       // A lo ring (2 x 16 KB)
+constexpr int LO_BYTES = TILE_A;
+constexpr int THREADS = 448;
+constexpr int EPI_COLS = 64;  // columns per epilogue warp
+constexpr uint32_t C_MAIN0 = 0, C_MAIN1 = 128, C_CROSS_A = 256, C_CROSS_B = 384;
 constexpr uint32_t IDESC = idesc_tf32(BM, BN);
 
 struct Bars {
-  uint64_t full[STAGES], empty[STAGES], afull[2], aempty[2], acc;
+  uint64_t full[STAGES], empty[STAGES], lofull[2], loempty[2], accfull, accempty, done;
   uint32_t tmem;
   int abort_flag;
   int issued[STAGES];
 };
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + (int)sizeof(Bars);
+constexpr int SMEM_BYTES = LO_AT + 2 * LO_BYTES + 1024 + (int)sizeof(Bars);
+
+// One K block: k-steps kk = 0..3 (descriptor start + 2 kk), main (hi*hi) into m,
+// then lo*hi and hi*lo into the two remainder accumulators, round-robin; then the
+// commits that free the stage and the A lo buffer.  fm / fx: first use of the main
+// / the remainder accumulators (they start from zero).
+__device__ __forceinline__ void issue_kblock(uint32_t m, uint32_t xa, uint32_t xb, uint64_t a, uint64_t alo, uint64_t b,
+                                             uint64_t blo, uint32_t fm, uint32_t fx, uint64_t* bar_stage,
+                                             uint64_t* bar_lo) {
+  asm volatile(
+      "{\n\t.reg .pred e, pt, pm, px;\n\t"
+      ".reg .b64 a1, a2, a3, l1, l2, l3, b1, b2, b3, c1, c2, c3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.eq.b32 pt, %7, %7;\n\tsetp.eq.b32 pm, %7, 0;\n\tsetp.eq.b32 px, %8, 0;\n\t"
+      "add.s64 a1, %3, 2;\n\tadd.s64 a2, %3, 4;\n\tadd.s64 a3, %3, 6;\n\t"
+      "add.s64 l1, %4, 2;\n\tadd.s64 l2, %4, 4;\n\tadd.s64 l3, %4, 6;\n\t"
+      "add.s64 b1, %5, 2;\n\tadd.s64 b2, %5, 4;\n\tadd.s64 b3, %5, 6;\n\t"
+      "add.s64 c1, %6, 2;\n\tadd.s64 c2, %6, 4;\n\tadd.s64 c3, %6, 6;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %3, %5, %9, pm;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], %4, %5, %9, px;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%2], %3, %6, %9, px;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], a1, b1, %9, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l1, b1, %9, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%2], a1, c1, %9, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], a2, b2, %9, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l2, b2, %9, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%2], a2, c2, %9, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], a3, b3, %9, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l3, b3, %9, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%2], a3, c3, %9, pt;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%10];\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%11];\n\t}" ::"r"(m),
+      "r"(xa), "r"(xb), "l"(a), "l"(alo), "l"(b), "l"(blo), "r"(fm), "r"(fx), "r"(IDESC), "r"(smem_u32(bar_stage)),
+      "r"(smem_u32(bar_lo))
+      : "memory");
+}
 
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -293,12 +358,12 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
                      int64_t ldc, Epi ep) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars& S = *reinterpret_cast<Bars*>(smem + STAGES * STAGE_BYTES);
+  Bars& S = *reinterpret_cast<Bars*>(smem + LO_AT + 2 * LO_BYTES);
   volatile int* abort_flag = &S.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
   const int nk = (K + BK - 1) / BK;
-  const int half = (nk + 1) / 2;  // first K block of the second hi*hi accumulator (used when nk >= 2)
+  const int tiles_n = (N + BN - 1) / BN;
+  const int ntiles = tiles_n * ((M + BM - 1) / BM);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -307,10 +372,12 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
       S.issued[s] = -1;
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&S.afull[i], 4);
-      mbar_init(&S.aempty[i], 1);
+      mbar_init(&S.lofull[i], 4);
+      mbar_init(&S.loempty[i], 1);
     }
-    mbar_init(&S.acc, 1);
+    mbar_init(&S.accfull, 1);
+    mbar_init(&S.accempty, 8);
+    mbar_init(&S.done, 1);
     S.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -324,157 +391,198 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
   __syncthreads();
   fence_after();
   const uint32_t tmem = S.tmem;
+  // warp-uniform wait: one try_wait and a vote when the phase has completed already
   auto ready = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+    if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
     const bool ok = !*abort_flag && mbar_wait(bar, parity, code);
     return __all_sync(0xffffffffu, ok);
   };
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t r = (uint32_t)(kb / STAGES);
-        if (*abort_flag || !mbar_wait(&S.empty[s], (r & 1) ^ 1, 21)) {
-          *abort_flag = 1;
-          break;
+      int g = 0;  // K blocks loaded so far (all tiles)
+      bool go = true;
+      for (int tile = blockIdx.x; go && tile < ntiles; tile += gridDim.x) {
+        const int n0 = (tile % tiles_n) * BN, m0 = (tile / tiles_n) * BM;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t r = (uint32_t)(g / STAGES);
+          if (*abort_flag || !mbar_wait(&S.empty[s], (r & 1) ^ 1, 21)) {
+            *abort_flag = 1;
+            go = false;
+            break;
+          }
+          uint8_t* st = smem + s * STAGE_BYTES;
+          S.issued[s] = (int)r;
+          mbar_expect_tx(&S.full[s], STAGE_BYTES);
+          tma_load_2d(st, &map_a, &S.full[s], kb * BK, m0);
+          tma_load_2d(st + TILE_A, &map_b, &S.full[s], kb * BK, n0);
+          tma_load_2d(st + TILE_A + TILE_B, &map_blo, &S.full[s], kb * BK, n0);
         }
-        uint8_t* st = smem + s * STAGE_BYTES;
-        S.issued[s] = (int)r;
-        mbar_expect_tx(&S.full[s], STAGE_BYTES);
-        tma_load_2d(st, &map_a, &S.full[s], kb * BK, m0);
-        tma_load_2d(st + TILE_A, &map_b, &S.full[s], kb * BK, n0);
-        tma_load_2d(st + TILE_A + TILE_B, &map_blo, &S.full[s], kb * BK, n0);
       }
     }
   } else if (warp == 1) {
     bool ok = true;
-    for (int kb = 0; ok && kb < nk; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t r = (uint32_t)(kb / STAGES);
-      const int a = kb & 1;
-      if (!ready(&S.full[s], r & 1, 22) || !ready(&S.afull[a], (uint32_t)(kb >> 1) & 1, 23)) {
+    int g = 0, it = 0;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+      // the accumulators are free once the epilogue has folded the previous tile
+      if (it >= 1 && !ready(&S.accempty, (uint32_t)(it - 1) & 1, 29)) {
         ok = false;
         break;
       }
       fence_after();
-      const int chunk = (nk >= 2 && kb >= half) ? 1 : 0;
-      const int chunk_first = chunk ? half : 0;
-      const uint32_t d_main = tmem + (chunk ? C_MAIN1 : C_MAIN0), d_cross = tmem + C_CROSS;
-      const uint32_t b_raw = smem_u32(smem + s * STAGE_BYTES + TILE_A), b_lo = b_raw + TILE_B;
-      const uint32_t a_hi = tmem + C_A + 64u * a, a_lo = a_hi + 32;
-#pragma unroll
-      for (int kk = 0; kk < BK / 8; ++kk) {
-        const uint32_t off = kk * 32;
-        mma_ts(d_cross, a_lo + 8 * kk, desc_k_sw128(b_raw + off), IDESC, (kb == 0 && kk == 0) ? 0u : 1u);
-        mma_ts(d_cross, a_hi + 8 * kk, desc_k_sw128(b_lo + off), IDESC, 1u);
-        mma_ts(d_main, a_hi + 8 * kk, desc_k_sw128(b_raw + off), IDESC, (kb == chunk_first && kk == 0) ? 0u : 1u);
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int s = g % STAGES;
+        const uint32_t r = (uint32_t)(g / STAGES);
+        const int l = g & 1;
+        if (!ready(&S.full[s], r & 1, 22) || !ready(&S.lofull[l], (uint32_t)(g >> 1) & 1, 23)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint64_t d_a = desc_k_sw128(smem_u32(smem + s * STAGE_BYTES));
+        const uint64_t d_b = d_a + (TILE_A >> 4), d_blo = d_b + (TILE_B >> 4);
+        const uint64_t d_alo = desc_k_sw128(smem_u32(smem + LO_AT + l * LO_BYTES));
+        issue_kblock(tmem + ((kb & 1) ? C_MAIN1 : C_MAIN0), tmem + C_CROSS_A, tmem + C_CROSS_B, d_a, d_alo, d_b,
+                     d_blo, kb < 2 ? 1u : 0u, kb == 0 ? 1u : 0u, &S.empty[s], &S.loempty[l]);
       }
-      mma_commit(&S.empty[s]);
-      mma_commit(&S.aempty[a]);
+      if (ok) mma_commit(&S.accfull);
     }
     if (!ok && lane == 0) *abort_flag = 1;
-    mma_commit(&S.acc);  // also on abort: arrives once whatever was issued has completed
+    mma_commit(&S.done);  // also on abort: arrives once whatever was issued has completed
+  } else if (warp < 6) {
+    // ---- converters: A lo of each stage.  Elementwise, so each 16-byte chunk goes to the
+    // same physical place in the lo tile as in the A tile (no need to know the swizzle);
+    // lanes visit the chunks in the order j ^ (row % 8) so a quarter-warp's eight rows hit
+    // eight bank groups ----
+    const int row = (warp & 3) * 32 + lane;
+    bool ok = true;
+    int g = 0;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int s = g % STAGES;
+        const int l = g & 1;
+        if (!ready(&S.full[s], (uint32_t)(g / STAGES) & 1, 24)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* arow = smem + s * STAGE_BYTES + row * 128;
+        float4 lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 x = *reinterpret_cast<const float4*>(arow + ((j ^ (row & 7)) << 4));
+          lo[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.empty[s]);  // this warp's rows of the stage are read
+        if (!ready(&S.loempty[l], ((uint32_t)(g >> 1) & 1) ^ 1, 25)) {
+          ok = false;
+          break;
+        }
+        uint8_t* lrow = smem + LO_AT + l * LO_BYTES + row * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) *reinterpret_cast<float4*>(lrow + ((j ^ (row & 7)) << 4)) = lo[j];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.lofull[l]);
+      }
+    }
+    if (!ok) *abort_flag = 1;
   } else {
-    // ---- A rows into TMEM (one row per thread = its TMEM lane), then the epilogue ----
+    // ---- epilogue: thread = output row (its TMEM lane), columns [cbase, cbase + 64) ----
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int grow = m0 + row;
-    const bool live = grow < M;
-    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int cbase = (warp - 6) / 4 * EPI_COLS;
+    const uint32_t lane_base = ((uint32_t)(quarter * 32) << 16) + (uint32_t)cbase;
+    const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
     bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES;
-      const int a = kb & 1;
-      if (!ready(&S.full[s], (uint32_t)(kb / STAGES) & 1, 24)) {
-        ok = false;
-        break;
-      }
-      // this thread's row of the swizzled A tile: 16-byte chunk j sits at chunk j ^ (row % 8);
-      // a quarter-warp reads eight rows' chunks from eight distinct bank groups
-      const uint8_t* arow = smem + s * STAGE_BYTES + row * 128;
-      float hi[32], lo[32];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 x = *reinterpret_cast<const float4*>(arow + ((j ^ (row & 7)) << 4));
-        const float e4[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          hi[4 * j + e] = tf32_hi(e4[e]);
-          lo[4 * j + e] = e4[e] - hi[4 * j + e];
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.empty[s]);  // this warp's rows of the stage are read
-      if (!ready(&S.aempty[a], ((uint32_t)(kb >> 1) & 1) ^ 1, 25)) {
+    int it = 0;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+      const int n0 = (tile % tiles_n) * BN, m0 = (tile / tiles_n) * BM;
+      if (!ready(&S.accfull, (uint32_t)it & 1, 26)) {
         ok = false;
         break;
       }
       fence_after();
-      tmem_st32(tmem + lane_base + C_A + 64u * a, hi);
-      tmem_st32(tmem + lane_base + C_A + 64u * a + 32, lo);
-      tmem_st_wait();
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.afull[a]);
-    }
-    if (!ok) *abort_flag = 1;
-    ok = ok && ready(&S.acc, 0, 26);
-    fence_after();
-    if (ok) {
-      const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        float v[32], w[32];
-        tmem_ld32(tmem + lane_base + C_CROSS + c0, v);
+      // fold (lo*hi + hi*lo) + hi*hi(odd K blocks) + hi*hi(even K blocks) in fp32
+      float v[EPI_COLS];
+#pragma unroll
+      for (int c0 = 0; c0 < EPI_COLS; c0 += 32) {
+        float w[32];
+        tmem_ld32(tmem + lane_base + C_CROSS_A + c0, v + c0);
+        tmem_ld32(tmem + lane_base + C_CROSS_B + c0, w);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[c0 + j] += w[j];
         if (nk >= 2) {
           tmem_ld32(tmem + lane_base + C_MAIN1 + c0, w);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += w[j];
+          for (int j = 0; j < 32; ++j) v[c0 + j] += w[j];
         }
         tmem_ld32(tmem + lane_base + C_MAIN0 + c0, w);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] += w[j];
-        if (!live) continue;
-        float* crow = C + (int64_t)grow * ldc + n0 + c0;
-        const float* gate = ep.mode == 2 ? ep.gate + (ep.rows_per_group > 0 ? grow / ep.rows_per_group : 0) *
-                                                       ep.gate_stride + n0 + c0
-                                         : nullptr;
-        const int ncol = min(32, N - (n0 + c0));
-        if (ncol <= 0) continue;
+        for (int j = 0; j < 32; ++j) v[c0 + j] += w[j];
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.accempty);
+      const int grow = m0 + row;
+      if (grow >= M) continue;
+      float* crow = C + (int64_t)grow * ldc + n0 + cbase;
+      const float* gate = ep.mode == 2 ? ep.gate + (ep.rows_per_group > 0 ? grow / ep.rows_per_group : 0) *
+                                                     ep.gate_stride + n0 + cbase
+                                       : nullptr;
+      const int ncol = min(EPI_COLS, N - n0 - cbase);
+      if (ncol <= 0) continue;
+      const bool full = vec && ncol == EPI_COLS;
+      // chunks of 16 columns with every load (bias, gate, residual row) before the chunk's
+      // stores: the residual is C itself, so loads after a store could not be hoisted
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          float res[4] = {0.f, 0.f, 0.f, 0.f};
-          const bool full4 = vec && 4 * j4 + 3 < ncol;
-          if (ep.mode >= 2) {
-            if (full4) {
-              const float4 t = *reinterpret_cast<const float4*>(crow + 4 * j4);
-              res[0] = t.x; res[1] = t.y; res[2] = t.z; res[3] = t.w;
-            } else {
-              for (int e = 0; e < 4; ++e)
-                if (4 * j4 + e < ncol) res[e] = crow[4 * j4 + e];
-            }
-          }
-          float out[4];
+      for (int c0 = 0; c0 < EPI_COLS; c0 += 16) {
+        float bv[16], gv[16], rv[16];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = 4 * j4 + e;
-            float y = v[j];
-            if (j < ncol) {
-              if (ep.bias) y = __fadd_rn(y, ep.bias[n0 + c0 + j]);
-              if (ep.mode == 1) y = gelu_tanh(y);
-              else if (ep.mode == 2) y = __fadd_rn(res[e], __fmul_rn(gate[j], y));
-              else if (ep.mode == 3) y = __fadd_rn(res[e], y);
+        for (int j = 0; j < 16; ++j) {
+          const bool in = c0 + j < ncol;
+          bv[j] = (ep.bias && in) ? __ldg(ep.bias + n0 + cbase + c0 + j) : 0.f;
+          gv[j] = (ep.mode == 2 && in) ? __ldg(gate + c0 + j) : 0.f;
+          rv[j] = 0.f;
+        }
+        if (ep.mode >= 2) {
+          if (full) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 t = *reinterpret_cast<const float4*>(crow + c0 + 4 * q);
+              rv[4 * q] = t.x;
+              rv[4 * q + 1] = t.y;
+              rv[4 * q + 2] = t.z;
+              rv[4 * q + 3] = t.w;
             }
-            out[e] = y;
-          }
-          if (full4) {
-            *reinterpret_cast<float4*>(crow + 4 * j4) = make_float4(out[0], out[1], out[2], out[3]);
           } else {
-            for (int e = 0; e < 4; ++e)
-              if (4 * j4 + e < ncol) crow[4 * j4 + e] = out[e];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) rv[j] = c0 + j < ncol ? crow[c0 + j] : 0.f;
           }
+        }
+        float o[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float y = v[c0 + j];
+          if (ep.bias) y = __fadd_rn(y, bv[j]);
+          if (ep.mode == 1) y = gelu_tanh(y);
+          else if (ep.mode == 2) y = __fadd_rn(rv[j], __fmul_rn(gv[j], y));
+          else if (ep.mode == 3) y = __fadd_rn(rv[j], y);
+          o[j] = y;
+        }
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<float4*>(crow + c0 + 4 * q) = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < ncol) crow[c0 + j] = o[j];
         }
       }
     }
+    if (!ok) *abort_flag = 1;
   }
   fence_before();
   __syncthreads();
@@ -483,7 +591,7 @@ tc_gemm_split_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
       if (*abort_flag)
         for (int s = 0; s < STAGES; ++s)
           if (S.issued[s] >= 0) mbar_wait(&S.full[s], (uint32_t)S.issued[s] & 1, 27);
-      mbar_wait(&S.acc, 0, 28);  // every MMA (and its barrier arrivals) finished
+      mbar_wait(&S.done, 0, 28);  // every MMA (and its barrier arrivals) finished
     }
     __syncwarp();
     fence_after();
@@ -582,8 +690,9 @@ extern "C" int cv3_tc_gemm_split(const float* a, int64_t lda, const float* b, co
   if (rc) return rc;
   rc = cv3::allow_smem((const void*)split::tc_gemm_split_kernel, split::SMEM_BYTES);
   if (rc) return rc;
-  dim3 grid((unsigned)((n + split::BN - 1) / split::BN), (unsigned)((m + split::BM - 1) / split::BM));
-  CV3_REQUIRE(grid.y <= 65535, CV3_ERR_VALUE, "tc_gemm_split: too many row tiles");
+  const int64_t ntiles = ((n + split::BN - 1) / split::BN) * ((m + split::BM - 1) / split::BM);
+  CV3_REQUIRE(ntiles < (1LL << 31), CV3_ERR_VALUE, "tc_gemm_split: too many tiles");
+  const int grid = (int)std::min<int64_t>(ntiles, cv3::sm_count());  // persistent: one CTA per SM
   Epi ep{1, 1, mode, bias, gate, rows_per_group, gate_stride};
   split::tc_gemm_split_kernel<<<grid, split::THREADS, split::SMEM_BYTES, cv3::as_stream(stream)>>>(
       ma, mb, mbl, (int)m, (int)n, (int)k, c, ldc, ep);

@@ -387,10 +387,12 @@ int cv3_tc_gemm_cfg(const float* a, int64_t lda, const float* b, int64_t ldb, fl
  * exact remainder the 3xTF32 products need.  Made once per weight matrix. */
 int cv3_tf32_lo(const float* x, int64_t n, float* lo, void* stream);
 
-/* cv3_tc_gemm with B given as its fp32 values plus the remainders of
- * cv3_tf32_lo (same ldb): the form the DiT's fixed weights use.  A is split
- * into TMEM by the kernel; same operand rules (k % 4 == 0, 16-byte aligned
- * rows), epilogue modes and accuracy as cv3_tc_gemm. */
+/* The DiT's GEMM: cv3_tc_gemm's contract (same operand rules -- k % 4 == 0,
+ * 16-byte aligned rows --, epilogue modes and 3xTF32 accuracy) with B given as
+ * its fp32 values plus the remainders of cv3_tf32_lo (same ldb), on persistent
+ * CTAs that split A on the fly, spread the products over four TMEM
+ * accumulators (hi*hi of even and of odd K blocks, lo*hi, hi*lo) and overlap
+ * each tile's epilogue with the next tile's MMAs. */
 int cv3_tc_gemm_split(const float* a, int64_t lda, const float* b, const float* b_lo, int64_t ldb, float* c,
                       int64_t ldc, int64_t m, int64_t n, int64_t k, int mode, const float* bias, const float* gate,
                       int64_t rows_per_group, int64_t gate_stride, void* stream);

@@ -7,7 +7,8 @@ the DiT's shapes, with row/column tails, K tails and every epilogue.  After
 each case the kernel's error word (bounded-wait expiry) must be clear.
 
 Both entry points run every case: cv3_tc_gemm (B split in the kernel) and
-cv3_tc_gemm_split (B with its cv3_tf32_lo remainder, A streamed into TMEM).
+cv3_tc_gemm_split (B with its cv3_tf32_lo remainder; persistent tiles, four
+accumulators, each tile's epilogue overlapped with the next tile's MMAs).
 """
 
 import ctypes
