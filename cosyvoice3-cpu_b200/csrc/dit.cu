@@ -65,6 +65,51 @@ __global__ void ln_modulate_kernel(const float* __restrict__ h, int dim, float e
   }
 }
 
+// ln_modulate_kernel for dim = 128 * V: one warp per row, the row in registers (V
+// float4 per lane, one coalesced read), mean and variance by warp shuffles (no
+// block barriers), same formulas; 8 rows per CTA.
+template <int V>
+__global__ void __launch_bounds__(256) ln_modulate_warp_kernel(const float* __restrict__ h, int64_t rows, float eps,
+                                                               const float* __restrict__ scale,
+                                                               const float* __restrict__ shift,
+                                                               int64_t rows_per_group, int64_t mod_stride,
+                                                               float* __restrict__ y) {
+  constexpr int DIM = 128 * V;
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float4* x4 = reinterpret_cast<const float4*>(h + r * DIM);
+  float4 v[V];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    v[j] = x4[lane + 32 * j];
+    s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+  }
+  const float mu = warp_sum(s) / (float)DIM;
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const float a = v[j].x - mu, b = v[j].y - mu, c = v[j].z - mu, d = v[j].w - mu;
+    q += (a * a + b * b) + (c * c + d * d);
+  }
+  const float sd = sqrtf(warp_sum(q) / (float)DIM + eps);
+  const int64_t g = rows_per_group > 0 ? r / rows_per_group : 0;
+  const float4* sc4 = reinterpret_cast<const float4*>(scale + g * mod_stride);
+  const float4* sh4 = reinterpret_cast<const float4*>(shift + g * mod_stride);
+  float4* o4 = reinterpret_cast<float4*>(y + r * DIM);
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const float4 sc = __ldg(sc4 + lane + 32 * j), sh = __ldg(sh4 + lane + 32 * j);
+    float4 o;
+    o.x = add(mul((v[j].x - mu) / sd, add(1.0f, sc.x)), sh.x);
+    o.y = add(mul((v[j].y - mu) / sd, add(1.0f, sc.y)), sh.y);
+    o.z = add(mul((v[j].z - mu) / sd, add(1.0f, sc.z)), sh.z);
+    o.w = add(mul((v[j].w - mu) / sd, add(1.0f, sc.w)), sh.w);
+    o4[lane + 32 * j] = o;
+  }
+}
+
 // h += gate * y  (dit.py:170, :173): rows of width dim, gate per group of rows.
 __global__ void gate_residual_kernel(float* __restrict__ h, const float* __restrict__ y, const float* __restrict__ gate,
                                      int64_t rows, int dim, int64_t rows_per_group, int64_t gate_stride) {
@@ -178,6 +223,17 @@ extern "C" int cv3_ln_modulate(const float* h, int64_t rows, int64_t dim, float 
                                void* stream) {
   CV3_REQUIRE(rows >= 0 && dim > 0 && rows < (1LL << 31), CV3_ERR_VALUE, "ln_modulate: bad shape");
   if (rows == 0) return CV3_OK;
+  const bool al = (((uintptr_t)h | (uintptr_t)y | (uintptr_t)scale | (uintptr_t)shift) & 15) == 0 && mod_stride % 4 == 0;
+  if (al && (dim == 1024 || dim == 512)) {
+    const unsigned grid = (unsigned)((rows + 7) / 8);
+    if (dim == 1024)
+      ln_modulate_warp_kernel<8><<<grid, 256, 0, cv3::as_stream(stream)>>>(h, rows, eps, scale, shift, rows_per_group,
+                                                                           mod_stride, y);
+    else
+      ln_modulate_warp_kernel<4><<<grid, 256, 0, cv3::as_stream(stream)>>>(h, rows, eps, scale, shift, rows_per_group,
+                                                                           mod_stride, y);
+    return cv3::check_launch("ln_modulate");
+  }
   ln_modulate_kernel<<<(unsigned)rows, row_threads(dim), 0, cv3::as_stream(stream)>>>(
       h, (int)dim, eps, scale, shift, rows_per_group, mod_stride, y);
   return cv3::check_launch("ln_modulate");

@@ -221,3 +221,22 @@ def test_rand_and_shared_generator_bit_exact():
     assert np.array_equal(g.randn((1000,)), nx.randn((1000,), gen=h))
     assert np.array_equal(g.randn((1000,)), nx.randn((1000,), gen=h))
     assert np.array_equal(g.random_float32(37), h.random_float32(37))
+
+
+@pytest.mark.parametrize("rows,dim,rpg", [(10400, 1024, 650), (37, 1024, 0), (300, 512, 100), (50, 80, 25)])
+def test_ln_modulate(rng, rows, dim, rpg):
+    """cv3_ln_modulate (the DiT's AdaLN: layer_norm(h) * (1 + scale[g]) + shift[g], g = row //
+    rows_per_group) against the oracle's layer_norm: the warp-per-row kernel (dim 512 / 1024,
+    aligned) and the generic one (dim 80)."""
+    import torch
+    L = pkg("_lib")
+    groups = rows // rpg if rpg else 1
+    h = (rng.normal(size=(rows, dim)) * 3 + 0.5).astype(np.float32)
+    mods = rng.normal(size=(groups, 2, dim)).astype(np.float32) * 0.2   # [g][scale | shift]
+    hd, md = torch.from_numpy(h).cuda(), torch.from_numpy(mods).cuda()
+    y = torch.empty_like(hd)
+    L.call("cv3_ln_modulate", hd.data_ptr(), rows, dim, 1e-6, md.data_ptr(), md.data_ptr() + dim * 4, rpg,
+           2 * dim, y.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    g = np.arange(rows) // rpg if rpg else np.zeros(rows, dtype=np.int64)
+    ref = nx.layer_norm(h, eps=1e-6) * (np.float32(1) + mods[g, 0]) + mods[g, 1]
+    assert rel_err(y.cpu().numpy(), ref) < TOL
