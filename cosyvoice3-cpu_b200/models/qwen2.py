@@ -196,6 +196,60 @@ class Qwen2Model:
         return D.out(out, host)
 
 
+    def forward_batch(self, xs, cache: KVCache):
+        """Prefill of several sequences in one pass: ``xs[b]`` ``(T_b, hidden)`` device
+        embeddings of sequence b (cache row b, appended from position 0).  Rows of all
+        sequences are stacked, so every GEMM runs once over all of them (each row's result
+        is the same as in :meth:`forward`: a row's products do not depend on the other
+        rows); RoPE and the cache append take per-row sequence ids and positions, and the
+        causal attention runs per sequence.  Returns the final hidden states of each
+        sequence's last row, ``(len(xs), hidden)``."""
+        c = self.cfg
+        H, Hk, hd, hid = c.num_attention_heads, c.num_key_value_heads, c.head_dim, c.hidden_size
+        lens = [int(x.shape[0]) for x in xs]
+        if max(lens) > cache.cap:
+            raise ValueError(f"KV cache capacity {cache.cap} exceeded ({max(lens)})")
+        offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+        T = int(offs[-1])
+        h = torch.cat([D.dev(x) for x in xs], 0).contiguous()
+        cos, sin = self.rope(max(lens))
+        st = D.stream()
+        n = D.empty((T, hid))
+        qkv = D.empty((T, (H + 2 * Hk) * hd))
+        q = D.empty((T, H * hd))
+        a = D.empty((T, H * hd))
+        gu = D.empty((T, 2 * c.intermediate_size))
+        act = D.empty((T, c.intermediate_size))
+        seqs = torch.cat([torch.full((t,), b, dtype=torch.int32) for b, t in enumerate(lens)]).cuda()
+        pos = torch.cat([torch.arange(t, dtype=torch.int32) for t in lens]).cuda()
+        scale = float(np.float32(1.0 / np.sqrt(hd)))
+        for i, L in enumerate(self.layers()):
+            lq, lo, lg, ld = (L.qkv, L.o, L.gu, L.down) if T <= 8 else self._wide(L)
+            kc, vc = cache.layer_ptrs(i)
+            call("cv3_rms_norm", h.data_ptr(), L.ln1.data_ptr(), T, hid, c.rms_norm_eps, n.data_ptr(), st)
+            lq(n.data_ptr(), T, qkv.data_ptr(), stream=st)
+            call("cv3_rope_qkv_append", qkv.data_ptr(), T, qkv.shape[1], cos.data_ptr(), sin.data_ptr(),
+                 seqs.data_ptr(), pos.data_ptr(), H, Hk, hd, q.data_ptr(), kc, vc, cache.cap, st)
+            for b, t in enumerate(lens):
+                kseq = b * Hk * cache.cap * hd * 4
+                row = int(offs[b]) * H * hd * 4
+                call("cv3_attention", q.data_ptr() + row, 0, hd, H * hd,
+                     kc + kseq, 0, cache.cap * hd, hd, vc + kseq, 0, cache.cap * hd, hd,
+                     a.data_ptr() + row, 0, hd, H * hd, 1, H, Hk, t, t, hd, scale, 1 if t > 1 else 0, 0, 0, st)
+            lo(a.data_ptr(), T, h.data_ptr(), residual=h.data_ptr(), stream=st)
+            call("cv3_rms_norm", h.data_ptr(), L.ln2.data_ptr(), T, hid, c.rms_norm_eps, n.data_ptr(), st)
+            lg(n.data_ptr(), T, gu.data_ptr(), stream=st)
+            call("cv3_swiglu", gu.data_ptr(), T, c.intermediate_size, act.data_ptr(), st)
+            ld(act.data_ptr(), T, h.data_ptr(), residual=h.data_ptr(), stream=st)
+        last = h[torch.as_tensor(offs[1:] - 1, device="cuda")].contiguous()
+        out = D.empty((len(xs), hid))
+        call("cv3_rms_norm", last.data_ptr(), self.norm_w().data_ptr(), len(xs), hid, c.rms_norm_eps,
+             out.data_ptr(), st)
+        for b, t in enumerate(lens):
+            cache.lengths[b] = t
+        return out
+
+
 def pk_sm_count() -> int:
     return int(torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count)
 
@@ -374,11 +428,8 @@ class DecodeEngine:
         """Run each sequence's prompt rows, pick its first token, set positions."""
         if len(prompts) != self.B:
             raise ValueError(f"{len(prompts)} prompts for a batch of {self.B}")
-        last = D.empty((self.B, self.c.hidden_size))
         self.cache.lengths = [0] * self.B          # a new batch overwrites the cache from position 0
-        for b, x in enumerate(prompts):
-            hb = self.m.forward(D.dev(x), self.cache, seq=b)
-            last[b].copy_(hb[-1])
+        last = self.m.forward_batch([D.dev(x) for x in prompts], self.cache)
         T = torch.tensor([int(np.shape(x)[0]) for x in prompts], dtype=torch.int32, device="cuda")
         self.pos.copy_(T - 1)       # head_select advances pos/lens by one
         self.lens.copy_(T)
