@@ -73,6 +73,7 @@ SIGNATURES = {
                       P, P, I64, I64, I64, I64, P],
     "cv3_tc_conv_status": [P],
     "cv3_conv_tc_set_window": [I32],
+    "cv3_set_dependent_launch": [I32],
     "cv3_conv_tc_last_path": [P],
     "cv3_decode_steps": [P, P],
     "cv3_decode_status": [P],

@@ -64,6 +64,15 @@ extern "C" const char* cv3_last_error(void) { return cv3::g_last_error.c_str(); 
 
 extern "C" int cv3_abi_version(void) { return CV3_ABI_VERSION; }
 
+static int g_dependent_launch = 1;
+
+bool cv3::dependent_launch_enabled() { return g_dependent_launch != 0; }
+
+extern "C" int cv3_set_dependent_launch(int enable) {
+  g_dependent_launch = enable ? 1 : 0;
+  return CV3_OK;
+}
+
 extern "C" unsigned long long cv3_launch_count(void) { return cv3::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int cv3_device_info(int* sm, int* major, int* minor) {

@@ -8,6 +8,8 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <utility>
+
 #include "../../include/cv3cuda.h"
 
 namespace cv3 {
@@ -27,7 +29,35 @@ int sm_count();
 // Sets the dynamic shared memory limit of a kernel once per (kernel, size).
 int allow_smem(const void* fn, int bytes);
 
+// Programmatic dependent launch (cv3_set_dependent_launch, on by default) for the
+// LM decode step's chain of small kernels: such a launch may start while the
+// previous kernel on the stream still runs.  Every kernel launched this way calls
+// dep_wait() before it touches anything the previous kernels write (its earlier
+// part only reads weights), then dep_release() so that the NEXT kernel may start --
+// after the wait, so at most one kernel waits ahead of the running one.
+bool dependent_launch_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dep(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = dependent_launch_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 }  // namespace cv3
+
+// the device side of launch_dep (no-ops for kernels launched normally)
+__device__ __forceinline__ void dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void dep_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 #define CV3_REQUIRE(cond, code, ...)                  \
   do {                                                \

@@ -12,6 +12,8 @@ namespace {
 __global__ void embed_kernel(const void* __restrict__ table, int kind, const uint16_t* __restrict__ sc, int64_t rows,
                              int64_t dim, int64_t kp, const int64_t* __restrict__ ids, int64_t n,
                              float* __restrict__ out, int64_t ldo, int* bad) {
+  dep_wait();
+  dep_release();
   const int64_t i = blockIdx.x;
   if (i >= n) return;
   const int64_t r = ids[i];
@@ -40,7 +42,7 @@ extern "C" int cv3_embedding(const void* table, int kind, const uint16_t* scales
   if (n == 0) return CV3_OK;
   CV3_REQUIRE(n <= 0x7FFFFFFF, CV3_ERR_VALUE, "embedding: too many ids");
   const int threads = dim >= 512 ? 256 : 128;
-  embed_kernel<<<(unsigned)n, threads, 0, cv3::as_stream(stream)>>>(table, kind, scales, rows, dim, kp, ids, n, out,
-                                                                    ldo, bad);
-  return cv3::check_launch("embedding");
+  return cv3::check_launch("embedding", cv3::launch_dep(embed_kernel, dim3((unsigned)n), dim3(threads), 0,
+                                                        cv3::as_stream(stream), table, kind, scales, rows, dim, kp,
+                                                        ids, n, out, ldo, bad));
 }

@@ -107,6 +107,10 @@ q8_gemv_mma_kernel(MmaArgs a) {
     s1[i] = in ? h2f(a.sc[(int64_t)r1 * ks + g0 + G]) : 0.f;
   }
 
+  // everything below reads what the previous kernels wrote
+  dep_wait();
+  dep_release();
+
   // -- stage x asynchronously (all pieces in flight at once), optional RMSNorm -----------
   const int k4 = kw >> 2;
   for (int i = tid; i < MAXB * k4; i += NWARP * 32) {
@@ -300,6 +304,5 @@ extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int6
     int rc = cv3::allow_smem((const void*)fn, smem);
     if (rc) return rc;
   }
-  fn<<<grid, NWARP * 32, smem, st>>>(a);
-  return cv3::check_launch("q8_decode_gemv_mma");
+  return cv3::check_launch("q8_decode_gemv_mma", cv3::launch_dep(fn, grid, dim3(NWARP * 32), (size_t)smem, st, a));
 }

@@ -18,6 +18,8 @@ __global__ void rope_qkv_append_kernel(const float* __restrict__ qkv, int64_t ld
                                        const int* __restrict__ pos, int heads, int kv_heads, int d,
                                        float* __restrict__ qout, float* __restrict__ kc, float* __restrict__ vc,
                                        int64_t cap) {
+  dep_wait();
+  dep_release();
   const int r = blockIdx.x;
   const int slot = blockIdx.y;  // [0, H) q heads, [H, H+Hk) k heads, [H+Hk, H+2Hk) v heads
   const int e = threadIdx.x;
@@ -62,6 +64,8 @@ decode_attention_kernel(const float* __restrict__ q, const float* __restrict__ k
   __shared__ float4 qs[HPG][DM / 4];
   __shared__ float4 part[PG][HPG][DM / 4];
   __shared__ float stat[HPG][2];
+  dep_wait();
+  dep_release();
   const int g = blockIdx.x, b = blockIdx.y;
   const int hpg = heads / kv_heads;
   const int m = (int)min((int64_t)lens[b], cap);
@@ -158,6 +162,8 @@ head_select_kernel(const float* __restrict__ logits, int64_t vocab, int64_t sele
   __shared__ float red[32];
   __shared__ float bv[32];
   __shared__ int bi[32];
+  dep_wait();
+  dep_release();
   const int b = blockIdx.x;
   const float* x = logits + (int64_t)b * vocab;
   float m = -INFINITY;
@@ -197,6 +203,8 @@ head_select_kernel(const float* __restrict__ logits, int64_t vocab, int64_t sele
 }
 
 __global__ void step_increment_kernel(int* step) {
+  dep_wait();
+  dep_release();
   if (threadIdx.x == 0 && blockIdx.x == 0) *step += 1;
 }
 
@@ -212,9 +220,10 @@ extern "C" int cv3_rope_qkv_append(const float* qkv, int64_t rows, int64_t ldq, 
   if (rows == 0) return CV3_OK;
   dim3 grid((unsigned)rows, (unsigned)(heads + 2 * kv_heads));
   const int threads = ((int)head_dim + 31) / 32 * 32;
-  rope_qkv_append_kernel<<<grid, threads, 0, cv3::as_stream(stream)>>>(
-      qkv, ldq, cos_table, sin_table, seq, pos, (int)heads, (int)kv_heads, (int)head_dim, q_out, k_cache, v_cache, cap);
-  return cv3::check_launch("rope_qkv_append");
+  return cv3::check_launch(
+      "rope_qkv_append", cv3::launch_dep(rope_qkv_append_kernel, grid, dim3(threads), 0, cv3::as_stream(stream), qkv,
+                                         ldq, cos_table, sin_table, seq, pos, (int)heads, (int)kv_heads,
+                                         (int)head_dim, q_out, k_cache, v_cache, cap));
 }
 
 extern "C" int cv3_decode_attention(const float* q, const float* k_cache, const float* v_cache, const int* lens,
@@ -233,9 +242,9 @@ extern "C" int cv3_decode_attention(const float* q, const float* k_cache, const 
   int rc = cv3::allow_smem((const void*)decode_attention_kernel, (int)smem);
   if (rc) return rc;
   dim3 grid((unsigned)kv_heads, (unsigned)batch);
-  decode_attention_kernel<<<grid, AT, (size_t)smem, cv3::as_stream(stream)>>>(q, k_cache, v_cache, lens, (int)heads,
-                                                                               (int)kv_heads, cap, scale, out);
-  return cv3::check_launch("decode_attention");
+  return cv3::check_launch("decode_attention",
+                           cv3::launch_dep(decode_attention_kernel, grid, dim3(AT), (size_t)smem, cv3::as_stream(stream),
+                                           q, k_cache, v_cache, lens, (int)heads, (int)kv_heads, cap, scale, out));
 }
 
 extern "C" int cv3_swiglu(const float* gate_up, int64_t rows, int64_t inter, float* y, void* stream) {
@@ -253,10 +262,9 @@ extern "C" int cv3_head_select(const float* logits, int64_t batch, int64_t vocab
   CV3_REQUIRE(batch >= 0 && vocab > 0 && select > 0 && select <= vocab, CV3_ERR_VALUE, "head_select: bad shape");
   if (batch == 0) return CV3_OK;
   cudaStream_t st = cv3::as_stream(stream);
-  head_select_kernel<<<(unsigned)batch, 1024, 0, st>>>(logits, vocab, select, logp_out, next_ids, pos, lens, history,
-                                                       hist_stride, step);
-  int rc = cv3::check_launch("head_select");
+  int rc = cv3::check_launch("head_select", cv3::launch_dep(head_select_kernel, dim3((unsigned)batch), dim3(1024), 0,
+                                                            st, logits, vocab, select, logp_out, next_ids, pos, lens,
+                                                            history, hist_stride, step));
   if (rc || !step) return rc;
-  step_increment_kernel<<<1, 32, 0, st>>>(step);
-  return cv3::check_launch("step_increment");
+  return cv3::check_launch("step_increment", cv3::launch_dep(step_increment_kernel, dim3(1), dim3(32), 0, st, step));
 }

@@ -421,6 +421,14 @@ int cv3_conv1d_tc(const float* x, int64_t xsb, int64_t xsc, int64_t xst, int64_t
 /* Error word of the tensor-core conv kernel (see cv3_tc_gemm_status). */
 int cv3_tc_conv_status(int* code);
 
+/* Programmatic dependent launch of the LM decode step's kernels (q8 decode
+ * GEMVs, RoPE + cache append, decode attention, head select, embedding): 1
+ * (default) lets each start while the previous kernel on the stream runs --
+ * it streams its weights, then waits for the previous kernel's results and
+ * only then releases its own successor; 0 launches them normally.  Results
+ * are identical; graphs captured afterwards keep the setting. */
+int cv3_set_dependent_launch(int enable);
+
 /* Input path of cv3_conv1d_tc: 1 (default) stages each channel block's input
  * window in shared memory by TMA when the strides allow it (16-byte multiples)
  * and the window fits 256 frames, else gathers from global memory; 0 always
