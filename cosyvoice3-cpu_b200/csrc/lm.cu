@@ -25,20 +25,22 @@ __global__ void rope_qkv_append_kernel(const float* __restrict__ qkv, int64_t ld
   const int e = threadIdx.x;
   if (e >= d) return;
   const int p = pos[r], s = seq[r];
+  const bool in_cache = p >= 0 && p < cap;  // a position past the cache is not stored (the host checks first)
   const float* row = qkv + (int64_t)r * ldq;
   if (slot < heads + kv_heads) {
     const float* x = row + (int64_t)slot * d;
     const int half = d / 2;
     const float rot = e < half ? -x[e + half] : x[e - half];
-    const float c = cosT[(int64_t)p * d + e], sn = sinT[(int64_t)p * d + e];
+    const int pt = in_cache ? p : 0;  // (tables cover the cache's positions)
+    const float c = cosT[(int64_t)pt * d + e], sn = sinT[(int64_t)pt * d + e];
     const float v = __fadd_rn(__fmul_rn(x[e], c), __fmul_rn(rot, sn));  // x*cos + rotate_half(x)*sin
     if (slot < heads) {
       qout[((int64_t)r * heads + slot) * d + e] = v;
-    } else {
+    } else if (in_cache) {
       const int hk = slot - heads;
       kc[(((int64_t)s * kv_heads + hk) * cap + p) * d + e] = v;
     }
-  } else {
+  } else if (in_cache) {
     const int hk = slot - heads - kv_heads;
     vc[(((int64_t)s * kv_heads + hk) * cap + p) * d + e] = row[(int64_t)slot * d + e];
   }
@@ -52,8 +54,8 @@ constexpr int PG = 16;     // key groups of the V pass (16 groups x 16 lanes x f
 // One CTA per (sequence, kv head): every query head of the group reads each
 // cached key/value row once.  Scores: one key per thread (its 256-byte row as
 // 16 independent float4 loads) against all heads of the group.  Softmax: one
-// warp per head.  V pass: 16 key groups x 16 lanes of float4 dims, per-group
-// partial sums reduced in a fixed order.  Same arithmetic as ops.sdpa with no
+// warp per head.  V pass: 16 key groups x 16 lanes of float4 dims, eight keys'
+// value loads in flight per group, per-group partial sums reduced in a fixed order.  Same arithmetic as ops.sdpa with no
 // mask (cv3cpu/ops.py:284-300): scores of the scaled query, exp(s - max), sum,
 // then P.V / sum.
 __global__ void __launch_bounds__(AT)
@@ -117,16 +119,26 @@ decode_attention_kernel(const float* __restrict__ q, const float* __restrict__ k
   float4 acc[HPG];
 #pragma unroll
   for (int h = 0; h < HPG; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = grp; j < m; j += PG) {
-    const float4 v = reinterpret_cast<const float4*>(vb + (int64_t)j * DM)[l];
+  constexpr int VU = 8;  // value rows in flight per key group: one L2 round trip per VU keys
+  for (int j = grp; j < m; j += VU * PG) {
+    float4 v[VU];
 #pragma unroll
-    for (int h = 0; h < HPG; ++h) {
-      if (h < hpg) {
-        const float p = sc[h * cap + j];
-        acc[h].x = fmaf(p, v.x, acc[h].x);
-        acc[h].y = fmaf(p, v.y, acc[h].y);
-        acc[h].z = fmaf(p, v.z, acc[h].z);
-        acc[h].w = fmaf(p, v.w, acc[h].w);
+    for (int u = 0; u < VU; ++u)
+      v[u] = j + u * PG < m ? reinterpret_cast<const float4*>(vb + (int64_t)(j + u * PG) * DM)[l]
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < VU; ++u) {
+      if (j + u * PG < m) {
+#pragma unroll
+        for (int h = 0; h < HPG; ++h) {
+          if (h < hpg) {
+            const float p = sc[h * cap + j + u * PG];
+            acc[h].x = fmaf(p, v[u].x, acc[h].x);
+            acc[h].y = fmaf(p, v[u].y, acc[h].y);
+            acc[h].z = fmaf(p, v[u].z, acc[h].z);
+            acc[h].w = fmaf(p, v[u].w, acc[h].w);
+          }
+        }
       }
     }
   }
@@ -196,7 +208,8 @@ head_select_kernel(const float* __restrict__ logits, int64_t vocab, int64_t sele
     for (int w = 1; w < nw; ++w)
       if (bv[w] > B || (bv[w] == B && bi[w] < I)) { B = bv[w]; I = bi[w]; }
     next_ids[b] = I;
-    if (history) history[(int64_t)b * hist_stride + (step ? *step : 0)] = I;
+    const int sn = step ? *step : 0;
+    if (history && sn >= 0 && sn < hist_stride) history[(int64_t)b * hist_stride + sn] = I;  // full history: not kept
     pos[b] += 1;
     lens[b] += 1;
   }
