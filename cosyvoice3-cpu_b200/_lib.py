@@ -50,6 +50,7 @@ SIGNATURES = {
     "cv3_torch_randn": [U64, I64, I64, P, P, P],
     "cv3_rope_qkv_append": [P, I64, I64, P, P, P, P, I64, I64, I64, P, P, P, I64, P],
     "cv3_decode_attention": [P, P, P, P, I64, I64, I64, I64, I64, F, P, P],
+    "cv3_decode_rope_attention": [P, I64, P, P, P, P, P, P, I64, I64, I64, I64, I64, F, P, P],
     "cv3_swiglu": [P, I64, I64, P, P],
     "cv3_head_select": [P, I64, I64, I64, P, P, P, P, P, I64, P, P],
     "cv3_dit_input_cat": [P, P, P, P, I64, I64, I64, I64, P, P],

@@ -58,8 +58,15 @@ constexpr int PG = 16;     // key groups of the V pass (16 groups x 16 lanes x f
 // value loads in flight per group, per-group partial sums reduced in a fixed order.  Same arithmetic as ops.sdpa with no
 // mask (cv3cpu/ops.py:284-300): scores of the scaled query, exp(s - max), sum,
 // then P.V / sum.
+// ROPE: q is the raw qkv projection (rows ldq apart); the CTA first rotates its
+// group's query heads and its kv head's key (half-split RoPE at pos[b], rounded as
+// cv3_rope_qkv_append does) and appends that key and the value at pos[b], so RoPE,
+// the cache append and attention are one launch.  (The caches are then written and
+// read by the same CTA: plain loads, no read-only path.)
+template <bool ROPE>
 __global__ void __launch_bounds__(AT)
-decode_attention_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ cosT,
+                        const float* __restrict__ sinT, const int* __restrict__ pos, float* kc, float* vc,
                         const int* __restrict__ lens, int heads, int kv_heads, int64_t cap, float scale,
                         float* __restrict__ out) {
   extern __shared__ float sc[];  // [hpg][cap] scores, then probabilities
@@ -72,11 +79,30 @@ decode_attention_kernel(const float* __restrict__ q, const float* __restrict__ k
   const int hpg = heads / kv_heads;
   const int m = (int)min((int64_t)lens[b], cap);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < hpg * (DM / 4); i += AT) {
-    const int h = i / (DM / 4), c = i - h * (DM / 4);
-    float4 v = reinterpret_cast<const float4*>(q + ((int64_t)b * heads + g * hpg + h) * DM)[c];
-    v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
-    qs[h][c] = v;
+  if (ROPE) {
+    const int p = pos[b];
+    const bool in_cache = p >= 0 && p < cap;  // a position past the cache is not stored
+    const int pt = in_cache ? p : 0;
+    const float* row = q + (int64_t)b * ldq;
+    for (int i = tid; i < (hpg + 2) * DM; i += AT) {
+      const int hh = i / DM, e = i - hh * DM;  // hh < hpg: query head; hpg: key; hpg + 1: value
+      const int slot = hh < hpg ? g * hpg + hh : (hh == hpg ? heads + g : heads + kv_heads + g);
+      const float* x = row + (int64_t)slot * DM;
+      float v = x[e];
+      if (hh <= hpg) {
+        const float rot = e < DM / 2 ? -x[e + DM / 2] : x[e - DM / 2];
+        v = __fadd_rn(__fmul_rn(v, cosT[(int64_t)pt * DM + e]), __fmul_rn(rot, sinT[(int64_t)pt * DM + e]));
+      }
+      if (hh < hpg) reinterpret_cast<float*>(&qs[hh][0])[e] = v * scale;
+      else if (in_cache) (hh == hpg ? kc : vc)[(((int64_t)b * kv_heads + g) * cap + p) * DM + e] = v;
+    }
+  } else {
+    for (int i = tid; i < hpg * (DM / 4); i += AT) {
+      const int h = i / (DM / 4), c = i - h * (DM / 4);
+      float4 v = reinterpret_cast<const float4*>(q + ((int64_t)b * heads + g * hpg + h) * DM)[c];
+      v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
+      qs[h][c] = v;
+    }
   }
   __syncthreads();
   const float* kb = kc + ((int64_t)b * kv_heads + g) * cap * DM;
@@ -239,9 +265,12 @@ extern "C" int cv3_rope_qkv_append(const float* qkv, int64_t rows, int64_t ldq, 
                                          (int)head_dim, q_out, k_cache, v_cache, cap));
 }
 
-extern "C" int cv3_decode_attention(const float* q, const float* k_cache, const float* v_cache, const int* lens,
-                                    int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap,
-                                    float scale, float* out, void* stream) {
+namespace {
+
+int launch_decode_attention(bool rope, const float* q, int64_t ldq, const float* cos_table, const float* sin_table,
+                            const int* pos, float* k_cache, float* v_cache, const int* lens, int64_t batch,
+                            int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap, float scale, float* out,
+                            void* stream) {
   CV3_REQUIRE(batch >= 0 && heads > 0 && kv_heads > 0 && heads % kv_heads == 0, CV3_ERR_VALUE,
               "%lld query heads is not a multiple of %lld kv heads", (long long)heads, (long long)kv_heads);
   CV3_REQUIRE(head_dim == DM, CV3_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (built for %d)",
@@ -252,12 +281,34 @@ extern "C" int cv3_decode_attention(const float* q, const float* k_cache, const 
   CV3_REQUIRE(((uintptr_t)q & 15) == 0 && ((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0,
               CV3_ERR_VALUE, "decode_attention: 16-byte aligned tensors required");
   if (batch == 0) return CV3_OK;
-  int rc = cv3::allow_smem((const void*)decode_attention_kernel, (int)smem);
+  auto fn = rope ? decode_attention_kernel<true> : decode_attention_kernel<false>;
+  int rc = cv3::allow_smem((const void*)fn, (int)smem);
   if (rc) return rc;
   dim3 grid((unsigned)kv_heads, (unsigned)batch);
   return cv3::check_launch("decode_attention",
-                           cv3::launch_dep(decode_attention_kernel, grid, dim3(AT), (size_t)smem, cv3::as_stream(stream),
-                                           q, k_cache, v_cache, lens, (int)heads, (int)kv_heads, cap, scale, out));
+                           cv3::launch_dep(fn, grid, dim3(AT), (size_t)smem, cv3::as_stream(stream), q, ldq,
+                                           cos_table, sin_table, pos, k_cache, v_cache, lens, (int)heads,
+                                           (int)kv_heads, cap, scale, out));
+}
+
+}  // namespace
+
+extern "C" int cv3_decode_attention(const float* q, const float* k_cache, const float* v_cache, const int* lens,
+                                    int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap,
+                                    float scale, float* out, void* stream) {
+  return launch_decode_attention(false, q, 0, nullptr, nullptr, nullptr, const_cast<float*>(k_cache),
+                                 const_cast<float*>(v_cache), lens, batch, heads, kv_heads, head_dim, cap, scale, out,
+                                 stream);
+}
+
+extern "C" int cv3_decode_rope_attention(const float* qkv, int64_t ldq, const float* cos_table,
+                                         const float* sin_table, const int* pos, float* k_cache, float* v_cache,
+                                         const int* lens, int64_t batch, int64_t heads, int64_t kv_heads,
+                                         int64_t head_dim, int64_t cap, float scale, float* out, void* stream) {
+  CV3_REQUIRE(ldq >= (heads + 2 * kv_heads) * head_dim && ldq % 4 == 0 && cos_table && sin_table && pos,
+              CV3_ERR_VALUE, "decode_rope_attention: qkv rows of (heads + 2 kv_heads) * head_dim, tables, positions");
+  return launch_decode_attention(true, qkv, ldq, cos_table, sin_table, pos, k_cache, v_cache, lens, batch, heads,
+                                 kv_heads, head_dim, cap, scale, out, stream);
 }
 
 extern "C" int cv3_swiglu(const float* gate_up, int64_t rows, int64_t inter, float* y, void* stream) {

@@ -135,7 +135,7 @@ class DecodeGemv:
     """
 
     def __init__(self, w: QTensor, bias=None, norm_w=None, eps: float = 1e-6, swiglu: bool = False,
-                 target_ctas: int = 296):
+                 target_ctas: int = 296, mma_splits: int = 1):
         self._keep = [w, bias, norm_w]
         self.n, self.k, self.kp = int(w.shape[0]), int(w.shape[1]), w.padded_k
         self.q, self.scales = w.q.data_ptr(), w.scales.data_ptr()
@@ -143,12 +143,17 @@ class DecodeGemv:
         self.norm = norm_w.data_ptr() if norm_w is not None else None
         self.eps = float(eps)
         self.swiglu = 1 if swiglu else 0
-        # the tensor-core kernel takes every unpadded K up to 5120 (all of Qwen2's linears),
-        # unsplit (a K split measured slower for the LM's down projection: 15 vs 12 us)
+        # the tensor-core kernel takes every unpadded K up to 5120 (all of Qwen2's linears);
+        # mma_splits > 1 splits K over CTAs (not with a fused RMSNorm, which needs whole rows).
+        # Measured in the batch-8 decode graph: the down projection (896 rows, K 4864) gains
+        # from 2 splits (112 CTAs instead of 56), 4 splits and the out projection lose.
         self.mma = self.kp == self.k and self.k % 64 == 0 and self.k <= 5120
         if self.mma:
             tiles = -(-self.n // (32 if self.n >= 4096 else 16))
-            self.splits = eff = 1
+            groups = self.k // 64
+            self.splits = max(1, min(int(mma_splits), groups)) if norm_w is None else 1
+            gs = -(-groups // self.splits)
+            eff = -(-groups // gs)
         else:
             tiles = -(-self.n // 32)
             self.splits = max(1, min(64, -(-target_ctas // tiles), self.kp // 64))

@@ -306,7 +306,7 @@ class DecodeEngine:
                 self.fast.append((DecodeGemv(ws[0], L.qkv._keep[1], L.ln1, c.rms_norm_eps),
                                   DecodeGemv(ws[1]),
                                   DecodeGemv(gu, norm_w=L.ln2, eps=c.rms_norm_eps, swiglu=True),
-                                  DecodeGemv(ws[4])))
+                                  DecodeGemv(ws[4], mma_splits=2)))
             else:
                 self.fast.append(None)
         self.fast_head = DecodeGemv(head_w, norm_w=model.norm_w(), eps=c.rms_norm_eps) \
@@ -381,10 +381,9 @@ class DecodeEngine:
             F = self.fast[i]
             if F is not None:
                 F[0](self.h.data_ptr(), B, self.qkv.data_ptr(), stream=st)
-                call("cv3_rope_qkv_append", self.qkv.data_ptr(), B, self.qkv.shape[1], self.cos.data_ptr(),
-                     self.sin.data_ptr(), self.seqs.data_ptr(), self.pos.data_ptr(), H, Hk, hd, self.q.data_ptr(),
-                     kc, vc, self.cap, st)
-                call("cv3_decode_attention", self.q.data_ptr(), kc, vc, self.lens.data_ptr(), B, H, Hk, hd,
+                # RoPE, cache append and attention in one launch (rows are the sequences in order)
+                call("cv3_decode_rope_attention", self.qkv.data_ptr(), self.qkv.shape[1], self.cos.data_ptr(),
+                     self.sin.data_ptr(), self.pos.data_ptr(), kc, vc, self.lens.data_ptr(), B, H, Hk, hd,
                      self.cap, self.scale, self.a.data_ptr(), st)
                 F[1](self.a.data_ptr(), B, self.h.data_ptr(), residual=self.h.data_ptr(), stream=st)
                 F[2](self.h.data_ptr(), B, self.act.data_ptr(), stream=st)

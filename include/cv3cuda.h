@@ -272,6 +272,18 @@ int cv3_decode_attention(const float* q, const float* k_cache, const float* v_ca
                          int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap,
                          float scale, float* out, void* stream);
 
+/* One decode step's RoPE, KV-cache append and attention in one launch: qkv rows b
+ * (sequence b, ldq floats apart) hold the q/k/v projection ((heads + 2 kv_heads)
+ * heads of 64); each (sequence, kv head) rotates its query heads and its key at
+ * pos[b] (half-split RoPE with the [position][64] cos / sin tables, rounded as
+ * cv3_rope_qkv_append), appends key and value at pos[b] (not stored outside
+ * [0, cap)), then attends like cv3_decode_attention over lens[b] cached rows.
+ * Same results as cv3_rope_qkv_append followed by cv3_decode_attention. */
+int cv3_decode_rope_attention(const float* qkv, int64_t ldq, const float* cos_table, const float* sin_table,
+                              const int* pos, float* k_cache, float* v_cache, const int* lens, int64_t batch,
+                              int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap, float scale, float* out,
+                              void* stream);
+
 /* y[r][i] = silu(gu[r][i]) * gu[r][inter + i]; qwen2.py:175-177. */
 int cv3_swiglu(const float* gate_up, int64_t rows, int64_t inter, float* y, void* stream);
 

@@ -114,3 +114,46 @@ def test_tensor_core_and_cuda_core_gemvs_agree(n, k, m):
     torch.cuda.synchronize()
     assert rel_err(y1.cpu().numpy(), ref) < 1e-5
     assert rel_err(y1.cpu().numpy(), y2.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_decode_rope_attention_matches_separate_kernels(m):
+    """cv3_decode_rope_attention (RoPE + cache append + attention in one launch) against
+    cv3_rope_qkv_append followed by cv3_decode_attention on the same qkv rows and caches:
+    bit-identical outputs and caches, including a sequence whose position lies past the
+    cache (its key and value are not stored by either)."""
+    import torch
+    L = pkg("_lib")
+    H, Hk, hd, cap = 14, 2, 64, 96
+    n = (H + 2 * Hk) * hd
+    rng = np.random.default_rng(70 + m)
+    c, s = pkg("models.qwen2").rope_tables(cap, hd, 1e6)
+    cosd, sind = torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
+    qkv = torch.from_numpy(rng.normal(size=(m, n)).astype(np.float32)).cuda()
+    pos_h = rng.integers(10, cap, size=m).astype(np.int32)
+    if m > 2:
+        pos_h[1] = cap + 5
+    lens_h = np.minimum(pos_h + 1, cap).astype(np.int32)
+    pos, lens = torch.from_numpy(pos_h).cuda(), torch.from_numpy(lens_h).cuda()
+    seqs = torch.arange(m, dtype=torch.int32, device="cuda")
+    kc0 = torch.from_numpy(rng.normal(size=(m, Hk, cap, hd)).astype(np.float32)).cuda()
+    vc0 = torch.from_numpy(rng.normal(size=(m, Hk, cap, hd)).astype(np.float32)).cuda()
+    st = torch.cuda.current_stream().cuda_stream
+    scale = float(np.float32(1.0 / np.sqrt(hd)))
+    outs = []
+    for fused in (True, False):
+        kc, vc = kc0.clone(), vc0.clone()
+        a = torch.zeros(m, H * hd, device="cuda")
+        if fused:
+            L.call("cv3_decode_rope_attention", qkv.data_ptr(), n, cosd.data_ptr(), sind.data_ptr(), pos.data_ptr(),
+                   kc.data_ptr(), vc.data_ptr(), lens.data_ptr(), m, H, Hk, hd, cap, scale, a.data_ptr(), st)
+        else:
+            q = torch.empty(m, H * hd, device="cuda")
+            L.call("cv3_rope_qkv_append", qkv.data_ptr(), m, n, cosd.data_ptr(), sind.data_ptr(), seqs.data_ptr(),
+                   pos.data_ptr(), H, Hk, hd, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), cap, st)
+            L.call("cv3_decode_attention", q.data_ptr(), kc.data_ptr(), vc.data_ptr(), lens.data_ptr(), m, H, Hk, hd,
+                   cap, scale, a.data_ptr(), st)
+        torch.cuda.synchronize()
+        outs.append((a.cpu().numpy(), kc.cpu().numpy(), vc.cpu().numpy()))
+    for x, y in zip(*outs):
+        assert np.array_equal(x, y)
