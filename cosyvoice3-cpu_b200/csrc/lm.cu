@@ -48,58 +48,84 @@ __global__ void rope_qkv_append_kernel(const float* __restrict__ qkv, int64_t ld
 
 constexpr int AT = 256;
 constexpr int DM = 64;
-constexpr int HPG = 8;     // most query heads sharing one kv head (Qwen2-0.5B: 7)
-constexpr int PG = 16;     // key groups of the V pass (16 groups x 16 lanes x float4)
+constexpr int HPG = 8;       // most query heads sharing one kv head (Qwen2-0.5B: 7)
+constexpr int HC = 2;        // query heads per CTA
+constexpr int PG = AT / 16;  // key groups of the V pass (16 lanes x float4 per group)
 
-// One CTA per (sequence, kv head): every query head of the group reads each
-// cached key/value row once.  Scores: one key per thread (its 256-byte row as
-// 16 independent float4 loads) against all heads of the group.  Softmax: one
-// warp per head.  V pass: 16 key groups x 16 lanes of float4 dims, eight keys'
-// value loads in flight per group, per-group partial sums reduced in a fixed order.  Same arithmetic as ops.sdpa with no
-// mask (cv3cpu/ops.py:284-300): scores of the scaled query, exp(s - max), sum,
-// then P.V / sum.
-// ROPE: q is the raw qkv projection (rows ldq apart); the CTA first rotates its
-// group's query heads and its kv head's key (half-split RoPE at pos[b], rounded as
-// cv3_rope_qkv_append does) and appends that key and the value at pos[b], so RoPE,
-// the cache append and attention are one launch.  (The caches are then written and
-// read by the same CTA: plain loads, no read-only path.)
+// One CTA per (sequence, kv head, pair of that kv head's query heads): the
+// query heads of a group are spread over ceil(hpg / 2) CTAs, each reading the
+// group's cached key/value rows (the repeats hit L2).  Scores: one key per
+// thread (its 256-byte row as 16 independent float4 loads) against the CTA's
+// heads.  Softmax: one warp per head.  V pass: 16 key groups x 16 lanes of
+// float4 dims, eight keys' value loads in flight per group, per-group partial
+// sums reduced in a fixed order.  Same arithmetic as ops.sdpa with no mask
+// (cv3cpu/ops.py:284-300): scores of the scaled query, exp(s - max), sum, then
+// P.V / sum.
+// ROPE: q is the raw qkv projection (rows ldq apart); every CTA rotates its
+// query heads and its kv head's key (half-split RoPE at pos[b], rounded as
+// cv3_rope_qkv_append does) and takes that key and the value for position pos[b]
+// from shared memory; the first CTA of the group also appends them to the cache.
+// So RoPE, the cache append and attention are one launch, and no CTA reads a
+// cache row another CTA of the launch writes.
 template <bool ROPE>
 __global__ void __launch_bounds__(AT)
 decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ cosT,
                         const float* __restrict__ sinT, const int* __restrict__ pos, float* kc, float* vc,
                         const int* __restrict__ lens, int heads, int kv_heads, int64_t cap, float scale,
                         float* __restrict__ out) {
-  extern __shared__ float sc[];  // [hpg][cap] scores, then probabilities
-  __shared__ float4 qs[HPG][DM / 4];
-  __shared__ float4 part[PG][HPG][DM / 4];
-  __shared__ float stat[HPG][2];
+  extern __shared__ float sc[];  // [HC][cap] scores, then probabilities
+  __shared__ float4 qs[HC][DM / 4];
+  __shared__ float4 knew[DM / 4], vnew[DM / 4];
+  __shared__ float4 part[PG][HC][DM / 4];
+  __shared__ float stat[HC];
+  const int g = blockIdx.x, b = blockIdx.y;
+  if (threadIdx.x == 0) {
+    // Warm L2 with this (sequence, kv head)'s cached keys and values while the previous
+    // kernel still runs.  Only a hint: L2 is coherent, so even a stale length (read
+    // before the wait) cannot change what the loads below see; the range stays inside
+    // the cache rows of this (sequence, kv head).
+    const int64_t rows = min((int64_t)max(*(const volatile int*)(lens + b), 0), cap);
+    const uint32_t bytes = (uint32_t)(rows * DM * 4);
+    if (bytes >= 16) {
+      const int64_t base = ((int64_t)b * kv_heads + g) * cap * DM;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kc + base), "r"(bytes) : "memory");
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vc + base), "r"(bytes) : "memory");
+    }
+  }
   dep_wait();
   dep_release();
-  const int g = blockIdx.x, b = blockIdx.y;
   const int hpg = heads / kv_heads;
+  const int h0 = blockIdx.z * HC;            // this CTA's first query head within the group
+  const int nh = min(HC, hpg - h0);          // >= 1: the grid covers ceil(hpg / HC) pairs
   const int m = (int)min((int64_t)lens[b], cap);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int pnew = -1;  // position whose key and value come from shared memory
   if (ROPE) {
     const int p = pos[b];
     const bool in_cache = p >= 0 && p < cap;  // a position past the cache is not stored
     const int pt = in_cache ? p : 0;
     const float* row = q + (int64_t)b * ldq;
-    for (int i = tid; i < (hpg + 2) * DM; i += AT) {
-      const int hh = i / DM, e = i - hh * DM;  // hh < hpg: query head; hpg: key; hpg + 1: value
-      const int slot = hh < hpg ? g * hpg + hh : (hh == hpg ? heads + g : heads + kv_heads + g);
+    for (int i = tid; i < (nh + 2) * DM; i += AT) {
+      const int hh = i / DM, e = i - hh * DM;  // hh < nh: query head; nh: key; nh + 1: value
+      const int slot = hh < nh ? g * hpg + h0 + hh : (hh == nh ? heads + g : heads + kv_heads + g);
       const float* x = row + (int64_t)slot * DM;
       float v = x[e];
-      if (hh <= hpg) {
+      if (hh <= nh) {
         const float rot = e < DM / 2 ? -x[e + DM / 2] : x[e - DM / 2];
         v = __fadd_rn(__fmul_rn(v, cosT[(int64_t)pt * DM + e]), __fmul_rn(rot, sinT[(int64_t)pt * DM + e]));
       }
-      if (hh < hpg) reinterpret_cast<float*>(&qs[hh][0])[e] = v * scale;
-      else if (in_cache) (hh == hpg ? kc : vc)[(((int64_t)b * kv_heads + g) * cap + p) * DM + e] = v;
+      if (hh < nh) {
+        reinterpret_cast<float*>(&qs[hh][0])[e] = v * scale;
+      } else {
+        reinterpret_cast<float*>(hh == nh ? knew : vnew)[e] = v;
+        if (in_cache && blockIdx.z == 0) (hh == nh ? kc : vc)[(((int64_t)b * kv_heads + g) * cap + p) * DM + e] = v;
+      }
     }
+    pnew = in_cache ? p : -1;
   } else {
-    for (int i = tid; i < hpg * (DM / 4); i += AT) {
+    for (int i = tid; i < nh * (DM / 4); i += AT) {
       const int h = i / (DM / 4), c = i - h * (DM / 4);
-      float4 v = reinterpret_cast<const float4*>(q + ((int64_t)b * heads + g * hpg + h) * DM)[c];
+      float4 v = reinterpret_cast<const float4*>(q + ((int64_t)b * heads + g * hpg + h0 + h) * DM)[c];
       v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
       qs[h][c] = v;
     }
@@ -109,24 +135,32 @@ decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* _
   const float* vb = vc + ((int64_t)b * kv_heads + g) * cap * DM;
   for (int j = tid; j < m; j += AT) {
     float4 kr[DM / 4];
-    const float4* src = reinterpret_cast<const float4*>(kb + (int64_t)j * DM);
+    if (j == pnew) {
 #pragma unroll
-    for (int c = 0; c < DM / 4; ++c) kr[c] = src[c];
-    for (int h = 0; h < hpg; ++h) {
-      float s = 0.f;
+      for (int c = 0; c < DM / 4; ++c) kr[c] = knew[c];
+    } else {
+      const float4* src = reinterpret_cast<const float4*>(kb + (int64_t)j * DM);
 #pragma unroll
-      for (int c = 0; c < DM / 4; ++c) {
-        const float4 qq = qs[h][c];
-        s = fmaf(qq.x, kr[c].x, s);
-        s = fmaf(qq.y, kr[c].y, s);
-        s = fmaf(qq.z, kr[c].z, s);
-        s = fmaf(qq.w, kr[c].w, s);
+      for (int c = 0; c < DM / 4; ++c) kr[c] = src[c];
+    }
+#pragma unroll
+    for (int h = 0; h < HC; ++h) {
+      if (h < nh) {
+        float s = 0.f;
+#pragma unroll
+        for (int c = 0; c < DM / 4; ++c) {
+          const float4 qq = qs[h][c];
+          s = fmaf(qq.x, kr[c].x, s);
+          s = fmaf(qq.y, kr[c].y, s);
+          s = fmaf(qq.z, kr[c].z, s);
+          s = fmaf(qq.w, kr[c].w, s);
+        }
+        sc[h * cap + j] = s;
       }
-      sc[h * cap + j] = s;
     }
   }
   __syncthreads();
-  if (warp < hpg) {
+  if (warp < nh) {
     float* row = sc + warp * cap;
     float mx = -INFINITY;
     for (int j = lane; j < m; j += 32) mx = fmaxf(mx, row[j]);
@@ -138,26 +172,28 @@ decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* _
       sum += p;
     }
     sum = warp_sum(sum);
-    if (lane == 0) stat[warp][0] = sum;
+    if (lane == 0) stat[warp] = sum;
   }
   __syncthreads();
   const int grp = tid / (DM / 4), l = tid % (DM / 4);
-  float4 acc[HPG];
+  float4 acc[HC];
 #pragma unroll
-  for (int h = 0; h < HPG; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int h = 0; h < HC; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
   constexpr int VU = 8;  // value rows in flight per key group: one L2 round trip per VU keys
   for (int j = grp; j < m; j += VU * PG) {
     float4 v[VU];
 #pragma unroll
-    for (int u = 0; u < VU; ++u)
-      v[u] = j + u * PG < m ? reinterpret_cast<const float4*>(vb + (int64_t)(j + u * PG) * DM)[l]
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = 0; u < VU; ++u) {
+      const int jj = j + u * PG;
+      v[u] = jj >= m ? make_float4(0.f, 0.f, 0.f, 0.f)
+                     : (jj == pnew ? vnew[l] : reinterpret_cast<const float4*>(vb + (int64_t)jj * DM)[l]);
+    }
 #pragma unroll
     for (int u = 0; u < VU; ++u) {
       if (j + u * PG < m) {
 #pragma unroll
-        for (int h = 0; h < HPG; ++h) {
-          if (h < hpg) {
+        for (int h = 0; h < HC; ++h) {
+          if (h < nh) {
             const float p = sc[h * cap + j + u * PG];
             acc[h].x = fmaf(p, v[u].x, acc[h].x);
             acc[h].y = fmaf(p, v[u].y, acc[h].y);
@@ -169,14 +205,14 @@ decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* _
     }
   }
 #pragma unroll
-  for (int h = 0; h < HPG; ++h)
-    if (h < hpg) part[grp][h][l] = acc[h];
+  for (int h = 0; h < HC; ++h)
+    if (h < nh) part[grp][h][l] = acc[h];
   __syncthreads();
-  for (int i = tid; i < hpg * DM; i += AT) {
+  for (int i = tid; i < nh * DM; i += AT) {
     const int h = i / DM, e = i - h * DM;
     float o = 0.f;
     for (int p = 0; p < PG; ++p) o += reinterpret_cast<const float*>(&part[p][h][0])[e];
-    out[(int64_t)b * heads * DM + (int64_t)(g * hpg + h) * DM + e] = o / stat[h][0];
+    out[(int64_t)b * heads * DM + (int64_t)(g * hpg + h0 + h) * DM + e] = o / stat[h];
   }
 }
 
@@ -276,7 +312,7 @@ int launch_decode_attention(bool rope, const float* q, int64_t ldq, const float*
   CV3_REQUIRE(head_dim == DM, CV3_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (built for %d)",
               (long long)head_dim, DM);
   CV3_REQUIRE(heads / kv_heads <= HPG, CV3_ERR_UNSUPPORTED, "decode_attention: more than %d heads per kv head", HPG);
-  const int64_t smem = (heads / kv_heads) * cap * 4;
+  const int64_t smem = HC * cap * 4;
   CV3_REQUIRE(cap > 0 && smem <= 150 * 1024, CV3_ERR_UNSUPPORTED, "decode_attention: cap too large");
   CV3_REQUIRE(((uintptr_t)q & 15) == 0 && ((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0,
               CV3_ERR_VALUE, "decode_attention: 16-byte aligned tensors required");
@@ -284,7 +320,8 @@ int launch_decode_attention(bool rope, const float* q, int64_t ldq, const float*
   auto fn = rope ? decode_attention_kernel<true> : decode_attention_kernel<false>;
   int rc = cv3::allow_smem((const void*)fn, (int)smem);
   if (rc) return rc;
-  dim3 grid((unsigned)kv_heads, (unsigned)batch);
+  const int64_t hpg = heads / kv_heads;
+  dim3 grid((unsigned)kv_heads, (unsigned)batch, (unsigned)((hpg + HC - 1) / HC));
   return cv3::check_launch("decode_attention",
                            cv3::launch_dep(fn, grid, dim3(AT), (size_t)smem, cv3::as_stream(stream), q, ldq,
                                            cos_table, sin_table, pos, k_cache, v_cache, lens, (int)heads,
