@@ -17,10 +17,12 @@
 //
 // CTA = 16 x RT weight rows x all of K, 8 warps (warp w takes row tile w % RT
 // and every (8 / RT)-th scale group); all of a warp's weight loads are issued
-// first, then the activations are copied to shared memory asynchronously
-// (cp.async: every 16-byte piece in flight at once, no registers), RMSNorm
-// is applied there, and the warps' partial sums are added in a fixed order in
-// shared memory (deterministic).  Epilogues: bias, residual add
+// first, with the epilogue's bias and the RMSNorm weight (constants); after
+// the dependency wait the residual is read at once and the activations are
+// copied to shared memory asynchronously (cp.async: every 16-byte piece in
+// flight at once, no registers); RMSNorm is applied there by one warp per
+// sequence, and the warps' partial sums are added in a fixed order in shared
+// memory (deterministic).  Epilogues: bias, residual add
 // (y may alias it), SwiGLU of interleaved gate/up rows (cv3cpu/models/qwen2.py:
 // 155-177, llm.py:74-78).
 #include "common.cuh"
@@ -46,6 +48,7 @@ struct MmaArgs {
   int gsplit;        // scale groups per K split (all of them when not split)
   float* partial;    // [splits][n][MAXB] when split
   int* counter;      // [row tiles], zero on entry and left zero
+  int cluster;       // 1: the K splits of a row tile form one thread-block cluster
 };
 
 __device__ __forceinline__ void widen16(const int4 w, float f[16]) {
@@ -77,12 +80,11 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
 // RT: 16-row tiles per CTA; GMAX: most scale groups one warp takes
 // (K <= 64 * (NWARP / RT) * GMAX)
 template <int RT, int GMAX>
-__global__ void __launch_bounds__(NWARP * 32)
+__global__ void __launch_bounds__(NWARP * 32, GMAX <= 4 ? 3 : 1)  // short K: 3 CTAs per SM (9728 rows in one wave)
 q8_gemv_mma_kernel(MmaArgs a) {
   constexpr int ROWS = 16 * RT, GSTEP = NWARP / RT;
   extern __shared__ float xs[];  // [MAXB][k] staged (and normalised) activations, rows >= m zero
   __shared__ float red[NWARP][16][MAXB];
-  __shared__ float rn[MAXB];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   const int tile = warp % RT, gw = warp / RT;
@@ -107,12 +109,29 @@ q8_gemv_mma_kernel(MmaArgs a) {
     s1[i] = in ? h2f(a.sc[(int64_t)r1 * ks + g0 + G]) : 0.f;
   }
 
+  // constants of the epilogue and the RMSNorm weight (staged behind x) do not depend on
+  // the previous kernels either
+  const int k4 = kw >> 2;
+  float* nws = xs + MAXB * kw;  // [kw] RMSNorm weight (only with norm_w; then kw == k)
+  if (a.norm_w)
+    for (int i = tid; i < k4; i += NWARP * 32)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(nws + 4 * i)),
+                   "l"(a.norm_w + 4 * i)
+                   : "memory");
+  const int rt = tid / MAXB, bb = tid - rt * MAXB;  // epilogue: row inside the CTA, sequence
+  const int row = blockIdx.x * ROWS + rt;
+  const bool epi = tid < ROWS * MAXB && row < a.n && bb < a.m;
+  const float bias_v = (epi && a.bias) ? a.bias[row] : 0.f;
+  const float bias_u = (epi && a.bias && a.swiglu && row + 1 < a.n) ? a.bias[row + 1] : 0.f;
+
   // everything below reads what the previous kernels wrote
   dep_wait();
   dep_release();
+  // the residual row is read now, so that its latency hides behind the staging and math
+  // (y may alias it: each element is read and written by this same thread only)
+  const float res_v = (epi && !a.swiglu && a.residual) ? a.residual[(int64_t)bb * a.ldy + row] : 0.f;
 
   // -- stage x asynchronously (all pieces in flight at once), optional RMSNorm -----------
-  const int k4 = kw >> 2;
   for (int i = tid; i < MAXB * k4; i += NWARP * 32) {
     const int mr = i / k4;
     float4* dst = reinterpret_cast<float4*>(xs) + i;
@@ -128,26 +147,30 @@ q8_gemv_mma_kernel(MmaArgs a) {
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   if (a.norm_w) {
+    // RMSNorm, one warp per sequence: the statistic, then (x * r) * w in place, rounded
+    // as ops.rms_norm (not split: kw == k)
     if (warp < a.m) {
-      float s = 0.f;
-      for (int cc = lane; cc < kw; cc += 32) {  // not split when normalised: kw == k
-        const float v = xs[warp * kw + cc];
-        s += v * v;
+      float4* xr = reinterpret_cast<float4*>(xs + warp * kw);
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int cc = lane; cc < k4; cc += 32) {
+        const float4 v = xr[cc];
+        s4[0] += v.x * v.x;
+        s4[1] += v.y * v.y;
+        s4[2] += v.z * v.z;
+        s4[3] += v.w * v.w;
       }
-      s = warp_sum(s);
-      if (lane == 0) rn[warp] = 1.0f / sqrtf(s / (float)a.k + a.eps);
-    }
-    __syncthreads();
-    for (int i = tid; i < a.m * k4; i += NWARP * 32) {
-      const int mr = i / k4, c4 = i - mr * k4;
-      const float r = rn[mr];
-      const float4 w4 = reinterpret_cast<const float4*>(a.norm_w)[c4];
-      float4 v = reinterpret_cast<float4*>(xs)[i];
-      v.x = (v.x * r) * w4.x;
-      v.y = (v.y * r) * w4.y;
-      v.z = (v.z * r) * w4.z;
-      v.w = (v.w * r) * w4.w;
-      reinterpret_cast<float4*>(xs)[i] = v;
+      const float ssum = warp_sum((s4[0] + s4[1]) + (s4[2] + s4[3]));
+      const float r = 1.0f / sqrtf(ssum / (float)a.k + a.eps);
+      const float4* wr = reinterpret_cast<const float4*>(nws);
+      for (int cc = lane; cc < k4; cc += 32) {
+        const float4 w4 = wr[cc];
+        float4 v = xr[cc];
+        v.x = (v.x * r) * w4.x;
+        v.y = (v.y * r) * w4.y;
+        v.z = (v.z * r) * w4.z;
+        v.w = (v.w * r) * w4.w;
+        xr[cc] = v;
+      }
     }
     __syncthreads();
   }
@@ -213,8 +236,6 @@ q8_gemv_mma_kernel(MmaArgs a) {
   // -- reduce the warps of each tile in a fixed order, then the K splits ---------------------
   __shared__ float tot[16 * RT][MAXB];
   __shared__ int last_cta;
-  const int rt = tid / MAXB, bb = tid - rt * MAXB;  // rt: row inside the CTA
-  const int row = blockIdx.x * ROWS + rt;
   if (tid < ROWS * MAXB) {
     const int tl = rt / 16, rr = rt % 16;
     float v = 0.f;
@@ -222,7 +243,27 @@ q8_gemv_mma_kernel(MmaArgs a) {
     for (int w = 0; w < GSTEP; ++w) v += red[tl + RT * w][rr][bb];
     tot[rt][bb] = v;
   }
-  if (gridDim.y > 1) {
+  if (gridDim.y > 1 && a.cluster) {
+    // the K splits of this row tile are one cluster: split 0 adds the others' sums from
+    // their shared memory in split order (deterministic), the rest wait until it has read
+    // them and leave; no global round trip
+    float v = 0.f;
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (blockIdx.y == 0 && tid < ROWS * MAXB) {
+      v = tot[rt][bb];
+      const uint32_t local = (uint32_t)__cvta_generic_to_shared(&tot[rt][bb]);
+      for (int sp = 1; sp < (int)gridDim.y; ++sp) {
+        uint32_t remote;
+        float pv;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(sp));
+        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(remote) : "memory");
+        v += pv;
+      }
+    }
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (blockIdx.y != 0) return;
+    if (tid < ROWS * MAXB) tot[rt][bb] = v;
+  } else if (gridDim.y > 1) {
     // deterministic split reduction: every split parks its sums, the last CTA of
     // the row tile to arrive adds them in split order and runs the epilogue
     if (tid < ROWS * MAXB && row < a.n)
@@ -244,18 +285,17 @@ q8_gemv_mma_kernel(MmaArgs a) {
   if (tid < ROWS * MAXB) {
     const int rr = rt % 16;
     float v = tot[rt][bb];
-    if (row < a.n && bb < a.m) {
-      if (a.bias) v += a.bias[row];
+    if (epi) {
+      if (a.bias) v += bias_v;
       if (a.swiglu) {
         if ((rr & 1) == 0) {  // rows 2i (gate) and 2i+1 (up)
           float up = tot[rt + 1][bb];
-          if (a.bias) up += a.bias[row + 1];
+          if (a.bias) up += bias_u;
           a.y[(int64_t)bb * a.ldy + row / 2] = (v / (1.0f + expf(-v))) * up;
         }
       } else {
-        float* yp = a.y + (int64_t)bb * a.ldy + row;
-        if (a.residual) v = v + a.residual[(int64_t)bb * a.ldy + row];
-        *yp = v;
+        if (a.residual) v = v + res_v;
+        a.y[(int64_t)bb * a.ldy + row] = v;
       }
     }
   }
@@ -292,9 +332,10 @@ extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int6
                 "q8_decode_gemv_mma: K splits need a workspace of splits*n*8 floats and zeroed counters "
                 "(one per %d-row tile)", rows);
   }
+  const bool cluster = nsplit > 1 && nsplit <= 8;  // portable cluster size
   MmaArgs a{x, ldx, (int)m, (int)k, q, scales, (int)n, bias, residual, y, ldy, norm_w, eps, swiglu,
-            gsplit, workspace, counters};
-  const int smem = MAXB * 64 * gsplit * 4;
+            gsplit, workspace, counters, cluster ? 1 : 0};
+  const int smem = (MAXB + (norm_w ? 1 : 0)) * 64 * gsplit * 4;
   dim3 grid((unsigned)tiles, (unsigned)nsplit);
   cudaStream_t st = cv3::as_stream(stream);
   void (*fn)(MmaArgs);
@@ -304,5 +345,21 @@ extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int6
     int rc = cv3::allow_smem((const void*)fn, smem);
     if (rc) return rc;
   }
-  return cv3::check_launch("q8_decode_gemv_mma", cv3::launch_dep(fn, grid, dim3(NWARP * 32), (size_t)smem, st, a));
+  if (!cluster)
+    return cv3::check_launch("q8_decode_gemv_mma", cv3::launch_dep(fn, grid, dim3(NWARP * 32), (size_t)smem, st, a));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(NWARP * 32);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = cv3::dependent_launch_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = (unsigned)nsplit;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cv3::check_launch("q8_decode_gemv_mma", cudaLaunchKernelEx(&cfg, fn, a));
 }

@@ -49,12 +49,12 @@ __global__ void rope_qkv_append_kernel(const float* __restrict__ qkv, int64_t ld
 constexpr int AT = 256;
 constexpr int DM = 64;
 constexpr int HPG = 8;       // most query heads sharing one kv head (Qwen2-0.5B: 7)
-constexpr int HC = 2;        // query heads per CTA
+constexpr int HC = 1;        // query heads per CTA (measured: 1 beats 2 and 7)
 constexpr int PG = AT / 16;  // key groups of the V pass (16 lanes x float4 per group)
 
-// One CTA per (sequence, kv head, pair of that kv head's query heads): the
-// query heads of a group are spread over ceil(hpg / 2) CTAs, each reading the
-// group's cached key/value rows (the repeats hit L2).  Scores: one key per
+// One CTA per (sequence, kv head, query head of that group): the query heads
+// of a group are spread over hpg / HC CTAs, each reading the group's cached
+// key/value rows (the repeats hit L2).  Scores: one key per
 // thread (its 256-byte row as 16 independent float4 loads) against the CTA's
 // heads.  Softmax: one warp per head.  V pass: 16 key groups x 16 lanes of
 // float4 dims, eight keys' value loads in flight per group, per-group partial
