@@ -412,8 +412,38 @@ def run_kernel(args) -> None:
     print("kernel %s: 5 launches done" % args.kernel, flush=True)
 
 
+def run_lm_step(args) -> None:
+    """Time the LM's graph-replayed decode step alone (full-size balanced LM, ``--lm-step B``
+    sequences with 130-165-row prompts, caches of 512 positions; 20 warm-up steps, then 200
+    steps between CUDA events on the replay stream); prints microseconds per step."""
+    import numpy as np
+    import torch
+    B = args.lm_step
+    W = pkg("synth").synthetic_weights("balanced", stages=("llm",))
+    lm = pkg("models.llm").CosyVoice3LM(pkg("weights").DeviceWeights(W))
+    rng = np.random.default_rng(3)
+    prompts = [(rng.normal(size=(130 + 5 * i, 896)) * 0.1).astype(np.float32) for i in range(B)]
+    eng = lm.engine(B, 512, 260)
+    eng.run(prompts, 2, use_graph=True)
+    for _ in range(20):
+        eng.step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 200
+    e0.record()
+    for _ in range(n):
+        eng.step()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / n * 1e3
+    print(json.dumps({"lm_decode_step_us": round(us, 1), "batch": B, "weight_bytes_per_step": 375255804,
+                      "weight_stream_gbs": round(375255804 / (us * 1e-6) / 1e9, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--lm-step", type=int, default=0, metavar="B",
+                    help="time the LM decode step alone at batch B (1..8)")
     ap.add_argument("--slice", action="store_true", help="profiling slice (see run_slice)")
     ap.add_argument("--kernel", choices=["ff1", "attention", "conv", "gemv"],
                     help="run one hot kernel alone at its bench shape (for ncu captures)")
@@ -431,7 +461,9 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     try:
-        if args.kernel:
+        if args.lm_step:
+            run_lm_step(args)
+        elif args.kernel:
             run_kernel(args)
         elif args.slice:
             run_slice(args)
