@@ -53,6 +53,7 @@ SIGNATURES = {
     "cv3_decode_rope_attention": [P, I64, P, P, P, P, P, P, I64, I64, I64, I64, I64, F, P, P],
     "cv3_swiglu": [P, I64, I64, P, P],
     "cv3_head_select": [P, I64, I64, I64, P, P, P, P, P, I64, P, P],
+    "cv3_sample_select": [P, I64, I64, I64, P, P, I32, D, I64, I64, D, P, P, P, P, P, I64, P, P, P, P],
     "cv3_dit_input_cat": [P, P, P, P, I64, I64, I64, I64, P, P],
     "cv3_ln_modulate": [P, I64, I64, F, P, P, I64, I64, P, P],
     "cv3_gate_residual": [P, P, P, I64, I64, I64, I64, P],

@@ -23,6 +23,7 @@ from .qwen2 import DecodeEngine, Qwen2Config, Qwen2Model
 torch = D.torch
 
 SPEECH_TOKEN_SIZE = 6561
+SAMPLER_MAX_TOP_K = 32  # cv3_sample_select's largest top_k (larger ones use the host sampler)
 ENDOFPROMPT_ID = 151646
 
 
@@ -71,6 +72,7 @@ class CosyVoice3LM:
         self.stop_token_ids = set(range(self.speech_token_size, self.speech_token_size + 200))
         self.endofprompt_id = int(weights.meta.get("endofprompt_id", ENDOFPROMPT_ID))
         self._engines = {}
+        self._sampling_engines = {}
 
     # -- pieces (llm.py:68-78) -------------------------------------------------
     def _speech_emb(self, ids):
@@ -101,7 +103,14 @@ class CosyVoice3LM:
     # -- sampling generation (llm.py:80-123) --------------------------------------
     def generate(self, text_tokens: Sequence[int], prompt_text_tokens: Sequence[int] = (),
                  prompt_speech_tokens: Sequence[int] = (), sampling: Optional[SamplingConfig] = None,
-                 strict_min_len: Optional[bool] = None, progress=None) -> Iterator[int]:
+                 strict_min_len: Optional[bool] = None, progress=None,
+                 device_sampler: bool = True) -> Iterator[int]:
+        """Speech tokens for ``text_tokens`` with the reference's sampling (llm.py:80-123).
+
+        ``device_sampler`` (top_k <= 32): the decode steps replay a CUDA graph and the token
+        choice runs on the device (cv3_sample_select); the tokens are produced before the
+        first is yielded.  Otherwise each step is a device forward followed by the host
+        sampler.  Both draw the same random stream from ``sampling.rng``."""
         sampling = sampling or SamplingConfig()
         if strict_min_len is None:
             strict_min_len = sampling.strict_min_len
@@ -109,6 +118,17 @@ class CosyVoice3LM:
         n_new = len(text_tokens)
         min_len = int(n_new * sampling.min_token_text_ratio)
         max_len = int(n_new * sampling.max_token_text_ratio)
+        if max_len <= 0:
+            return
+        if device_sampler and 1 <= int(sampling.top_k) <= SAMPLER_MAX_TOP_K and sampling.top_p > 0:
+            # graph-replayed decode steps with the device sampler: the same tokens and the
+            # same random stream as the host sampler (the state is handed back to sampling.rng)
+            toks = self.generate_sampled([x], sampling, [min_len], [max_len], strict_min_len)[0]
+            for i, t in enumerate(toks):
+                yield t
+                if progress is not None:
+                    progress(i, t)
+            return
         cache = self.body.new_cache(1, int(x.shape[0]) + max_len + 1)
         out: List[int] = []
         for i in range(max_len):
@@ -142,6 +162,44 @@ class CosyVoice3LM:
             p /= p.sum()
             top = int(cfg.rng.choice(p.shape[0], p=p))
         return top
+
+    def sampling_engine(self, batch: int, cap: int, max_steps: int, cfg: SamplingConfig,
+                        strict: bool) -> DecodeEngine:
+        key = (batch, cap, max_steps, float(cfg.top_p), int(cfg.top_k), int(cfg.win_size), float(cfg.tau_r),
+               bool(strict))
+        if key not in self._sampling_engines:
+            eng = DecodeEngine(self.body, self.w.weight(self.prefix + "llm_decoder.weight"),
+                               self.w.weight(self.prefix + "speech_embedding"), self.speech_token_size, batch, cap,
+                               max_steps)
+            eng.enable_sampling(cfg.top_p, cfg.top_k, cfg.win_size, cfg.tau_r, strict)
+            self._sampling_engines[key] = eng
+        return self._sampling_engines[key]
+
+    def generate_sampled(self, prompts, sampling: SamplingConfig, min_lens, max_lens, strict_min_len: bool):
+        """Sampled decode of every prompt embedding ``(T_b, H)`` with the device sampler.
+
+        Sequence b draws from its own copy of ``sampling.rng``'s stream in turn: b = 0 starts
+        from the generator's state, b + 1 from where b ended, as consecutive host calls of
+        ``generate`` would; the generator is left where the last one ended.  Returns the
+        token lists (stop ids excluded)."""
+        st = sampling.rng.bit_generator.state
+        if st.get("bit_generator") != "PCG64":
+            raise ValueError("the device sampler replays numpy's PCG64 stream")
+        B = len(prompts)
+        need = max(int(np.shape(p)[0]) for p in prompts) + max(max_lens) + 1
+        cap = max(256, -(-need // 256) * 256)
+        steps = max(256, -(-max(max_lens) // 256) * 256)
+        out = []
+        state = (st["state"]["state"], st["state"]["inc"])
+        for b in range(B):   # sequential draws share one stream: one sequence per run
+            eng = self.sampling_engine(1, cap, steps, sampling, strict_min_len)
+            toks, states = eng.run_sampled([prompts[b]], [state], [min_lens[b]], [max_lens[b]])
+            out.append(toks[0])
+            state = states[0]
+        sampling.rng.bit_generator.state = {"bit_generator": "PCG64",
+                                             "state": {"state": state[0], "inc": state[1]},
+                                             "has_uint32": st["has_uint32"], "uinteger": st["uinteger"]}
+        return out
 
     # -- batched greedy decode ------------------------------------------------
     def engine(self, batch: int, cap: int, max_steps: int) -> DecodeEngine:

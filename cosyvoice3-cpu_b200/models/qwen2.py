@@ -295,6 +295,7 @@ class DecodeEngine:
         self.scale = float(np.float32(1.0 / np.sqrt(hd)))
         self.graph = None
         self.keep_logp = False
+        self.sampling = None  # (top_p, top_k, win_size, tau_r, strict): device sampler instead of greedy
         # fused q8 decode GEMVs (RMSNorm in, residual / SwiGLU out) where the layer is q8
         self.fast = []
         for i, L in enumerate(model.layers()):
@@ -409,12 +410,38 @@ class DecodeEngine:
              self.n.data_ptr(), st)
         self.select_and_feed(st)
 
+    def enable_sampling(self, top_p: float, top_k: int, win_size: int, tau_r: float, strict: bool):
+        """Choose tokens with the device sampler (cv3_sample_select) instead of the greedy
+        head: per-sequence numpy PCG64 states, token counts, min/max lengths and done flags
+        live on the device, so a sampled step is graph-capturable like a greedy one."""
+        B = self.B
+        self.sampling = (float(top_p), int(top_k), int(win_size), float(tau_r), 1 if strict else 0)
+        self.rng_state = torch.zeros((B, 4), dtype=torch.int64, device="cuda")
+        self.min_len = torch.zeros(B, dtype=torch.int32, device="cuda")
+        self.max_len = torch.zeros(B, dtype=torch.int32, device="cuda")
+        self.count = torch.zeros(B, dtype=torch.int32, device="cuda")
+        self.done = torch.zeros(B, dtype=torch.int32, device="cuda")
+        self.graph = None
+
     def select_and_feed(self, st, logits_ready: bool = False):
         if not logits_ready:
             self.head(self.n.data_ptr(), self.B, self.logits.data_ptr(), stream=st)
+        if self.sampling is not None:
+            top_p, top_k, win, tau_r, strict = self.sampling
+            call("cv3_sample_select", self.logits.data_ptr(), self.B, self.vocab, self.select,
+                 self.min_len.data_ptr(), self.max_len.data_ptr(), strict, top_p, top_k, win, tau_r,
+                 self.rng_state.data_ptr(), self.next_ids.data_ptr(), self.pos.data_ptr(), self.lens.data_ptr(),
+                 self.history.data_ptr(), self.max_steps, self.count.data_ptr(), self.done.data_ptr(),
+                 self.logp.data_ptr() if self.keep_logp else None, st)
+            self._feed(st)
+            return
         call("cv3_head_select", self.logits.data_ptr(), self.B, self.vocab, self.select,
              self.logp.data_ptr() if self.keep_logp else None, self.next_ids.data_ptr(), self.pos.data_ptr(),
              self.lens.data_ptr(), self.history.data_ptr(), self.max_steps, self.step_no.data_ptr(), st)
+        self._feed(st)
+
+    def _feed(self, st):
+        """The chosen tokens' speech embeddings become the next step's input rows."""
         e = self.emb
         if isinstance(e, QTensor):
             call("cv3_embedding", e.q.data_ptr(), 2, e.scales.data_ptr(), int(e.shape[0]), int(e.shape[1]),
@@ -446,6 +473,49 @@ class DecodeEngine:
             self.launches(D.stream())
         else:
             self.graph.replay()
+
+    def run_sampled(self, prompts, rng_states, min_lens, max_lens, poll: int = 8):
+        """Sampled decode (enable_sampling first) until every sequence has drawn a stop id or
+        reached its max length.  ``rng_states``: per sequence numpy PCG64 ``(state, inc)``.
+        Steps run as graph replays; the done flags are read every ``poll`` steps (a finished
+        sequence's steps change nothing).  Returns the token lists and the final states."""
+        if self.sampling is None:
+            raise RuntimeError("run_sampled needs enable_sampling()")
+        B = self.B
+        if not (len(prompts) == len(rng_states) == len(min_lens) == len(max_lens) == B):
+            raise ValueError("one prompt, random state, min and max length per sequence")
+        if max(max_lens) > self.max_steps:
+            raise ValueError("max length exceeds the engine's max_steps")
+        if max(int(np.shape(x)[0]) for x in prompts) + max(max_lens) > self.cap:
+            raise ValueError("prompt + max length exceed the KV cache capacity")
+        m64 = (1 << 64) - 1
+        words = []
+        for st_, inc in rng_states:
+            for v in ((st_ >> 64) & m64, st_ & m64, (inc >> 64) & m64, inc & m64):
+                words.append(v - (1 << 64) if v >= (1 << 63) else v)  # as int64 bit patterns
+        self.rng_state.copy_(torch.tensor(words, dtype=torch.int64).view(B, 4))
+        self.min_len.copy_(torch.tensor(list(min_lens), dtype=torch.int32))
+        self.max_len.copy_(torch.tensor(list(max_lens), dtype=torch.int32))
+        self.count.zero_()
+        self.done.copy_(torch.tensor([1 if m <= 0 else 0 for m in max_lens], dtype=torch.int32))
+        self.prefill(prompts)
+        if self.graph is None:
+            state = (self.h, self.pos, self.lens, self.step_no, self.next_ids, self.history, self.rng_state,
+                     self.count, self.done)
+            saved = [t.clone() for t in state]
+            self.capture()
+            for t, v in zip(state, saved):
+                t.copy_(v)
+        steps = 1
+        while steps < max(max_lens) and not bool(self.done.all()):
+            for _ in range(min(poll, max(max_lens) - steps)):
+                self.step()
+                steps += 1
+        counts = self.count.cpu().tolist()
+        hist = self.history.cpu().numpy()
+        rs = self.rng_state.cpu().numpy().astype(np.uint64).tolist()
+        out_states = [((int(r[0]) << 64) | int(r[1]), (int(r[2]) << 64) | int(r[3])) for r in rs]
+        return [hist[b, :counts[b]].tolist() for b in range(B)], out_states
 
     def run(self, prompts, n_tokens: int, use_graph: bool = True, persistent: bool = False):
         """Greedy-decode ``n_tokens`` tokens for every prompt; returns ``[B][n_tokens]`` ids (device).

@@ -284,6 +284,26 @@ int cv3_decode_rope_attention(const float* qkv, int64_t ldq, const float* cos_ta
                               int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap, float scale, float* out,
                               void* stream);
 
+/* One sampled decode step per sequence, replacing the host sampler of
+ * cv3cpu/models/llm.py:107-123 (generate), :125-149 (_sample) and :37-49
+ * (nucleus_sampling): logits [batch][vocab] -> log_softmax -> stop ids
+ * [speech_token_size, +200) masked while count[b] < min_len[b] (only the first
+ * unless strict_min_len) -> softmax -> the top_k (<= 32) most probable in stable
+ * order, kept while their float64 running sum is below top_p -> a draw from them
+ * -> if that token occurs >= win_size * tau_r times in the last win_size tokens
+ * of history, a redraw from the full distribution without it.  rng_state
+ * [batch][4] holds numpy PCG64 states (state hi, lo, increment hi, lo) and is
+ * advanced exactly as numpy's Generator.choice advances it.  A stop id sets
+ * done[b] (nothing recorded); otherwise the token goes to history[b][count[b]],
+ * next_ids[b], count/pos/lens advance, and done[b] is set once count reaches
+ * max_len[b].  Sequences with done[b] set are left untouched.  logp_out
+ * (optional) receives the log-probabilities. */
+int cv3_sample_select(const float* logits, int64_t batch, int64_t vocab, int64_t speech_token_size,
+                      const int* min_len, const int* max_len, int strict_min_len, double top_p, int64_t top_k,
+                      int64_t win_size, double tau_r, uint64_t* rng_state, int64_t* next_ids, int* pos, int* lens,
+                      int64_t* history, int64_t hist_stride, int* count, int* done, float* logp_out,
+                      void* stream);
+
 /* y[r][i] = silu(gu[r][i]) * gu[r][inter + i]; qwen2.py:175-177. */
 int cv3_swiglu(const float* gate_up, int64_t rows, int64_t inter, float* y, void* stream);
 

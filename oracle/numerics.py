@@ -508,3 +508,41 @@ def rand(shape, seed: int = 0, gen: Optional[MT19937] = None) -> np.ndarray:
     n = int(np.prod(shape)) if shape else 1
     g = gen if gen is not None else MT19937(seed)
     return g.random_float32(n).reshape(shape)
+
+
+# ---------------------------------------------------------------------------
+# speech-token sampling                       cv3cpu/models/llm.py:37-49, :125-149
+# ---------------------------------------------------------------------------
+
+def nucleus_sampling(probs_sorted, idx_sorted, rng, top_p: float, top_k: int) -> int:   # llm.py:37-49
+    cum, n = 0.0, 0
+    for i in range(min(top_k, idx_sorted.shape[0])):
+        if cum >= top_p:
+            break
+        cum += float(probs_sorted[i])
+        n += 1
+    p = probs_sorted[:n].astype(np.float64)
+    p = p / p.sum()
+    return int(idx_sorted[rng.choice(n, p=p)])
+
+
+def sample_token(logp, decoded, rng, speech_token_size: int, ignore_eos: bool, strict_min_len: bool,
+                 top_p: float = 0.8, top_k: int = 25, win_size: int = 10, tau_r: float = 0.1) -> int:
+    """One step of CosyVoice3LM._sample (llm.py:125-149): stop ids masked below min_len,
+    nucleus draw from softmax(scores), repetition-aware resample from the full distribution."""
+    scores = np.array(logp, dtype=np.float32, copy=True)
+    if ignore_eos:
+        if strict_min_len:
+            scores[speech_token_size:speech_token_size + 200] = -np.inf
+        else:
+            scores[speech_token_size] = -np.inf
+    probs = softmax(scores)
+    order = np.argsort(-probs, kind="stable")
+    top = nucleus_sampling(probs[order], order, rng, top_p, top_k)
+    window = list(decoded)[-win_size:]
+    if sum(1 for t in window if t == top) >= win_size * tau_r:
+        scores[top] = -np.inf
+        p = softmax(scores).astype(np.float64)
+        p /= p.sum()
+        top = int(rng.choice(p.shape[0], p=p))
+    return top

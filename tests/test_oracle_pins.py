@@ -166,3 +166,29 @@ def test_oracle_matches_frozen_upstream_outputs(tmp_path):
         if i < len(forced):
             x = lm.speech_emb([int(forced[i])])
     W.close()
+
+
+@pytest.mark.skipif(not have_reference(), reason="reference checkout not present")
+@pytest.mark.parametrize("strict", [False, True])
+def test_oracle_sampler_matches_reference(strict):
+    """The oracle's sampler against CosyVoice3LM._sample (llm.py:125-149) itself: same
+    tokens and the same random stream over 300 steps with stops, masking and repeats."""
+    sys.path.insert(0, REFERENCE)
+    from cv3cpu.models import llm as rl
+    sts = 6561
+    ref = rl.CosyVoice3LM.__new__(rl.CosyVoice3LM)
+    ref.speech_token_size = sts
+    ref.stop_token_ids = set(range(sts, sts + 200))
+    cfg = rl.SamplingConfig(seed=11)
+    rng = np.random.default_rng(11)
+    data = np.random.default_rng(5)
+    decoded = []
+    for i in range(300):
+        logits = (data.normal(size=6761) * 3.0).astype(np.float32)
+        logp = nx.log_softmax(logits)
+        ign = i % 7 < 3
+        a = ref._sample(logp, decoded, cfg, ign, strict)
+        b = nx.sample_token(logp, decoded, rng, sts, ign, strict)
+        assert a == b, i
+        decoded.append(a)
+    assert cfg.rng.bit_generator.state == rng.bit_generator.state
