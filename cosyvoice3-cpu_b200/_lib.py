@@ -32,6 +32,8 @@ SIGNATURES = {
     "cv3_q8_linear": [P, I64, I64, I64, P, P, I64, I64, P, P, P, I64, P],
     "cv3_f32_linear": [P, I64, I64, I64, P, I64, I64, P, P, P, I64, P],
     "cv3_q8_dequant": [P, P, I64, I64, I64, P, P],
+    "cv3_q4_linear": [P, I64, I64, I64, P, P, I64, I64, P, P, P, I64, P],
+    "cv3_q4_dequant": [P, P, I64, I64, I64, P, P],
     "cv3_unary": [I32, F, P, I64, P, P],
     "cv3_rms_norm": [P, P, I64, I64, F, P, P],
     "cv3_layer_norm": [P, P, P, I64, I64, F, P, P],

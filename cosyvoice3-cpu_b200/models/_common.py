@@ -25,16 +25,17 @@ TC_MIN_ROWS = 16   # below this many rows the fp32 GEMV/SIMT path is used
 class Lin:
     """A linear layer's device operands: q8 (payload, scales) or fp32 matrix, and bias."""
 
-    __slots__ = ("q8", "w", "scales", "n", "k", "kp", "bias", "_keep", "_lo")
+    __slots__ = ("q8", "q4", "w", "scales", "n", "k", "kp", "bias", "_keep", "_lo")
 
     def __init__(self, w, bias=None):
         self._keep = [w, bias]
         if isinstance(w, QTensor):
-            self.q8 = True
+            self.q8 = True            # quantised (q8, or q4 when self.q4)
+            self.q4 = w.kind == "q4"
             self.w, self.scales = w.q.data_ptr(), w.scales.data_ptr()
             self.n, self.k, self.kp = int(w.shape[0]), int(w.shape[1]), w.padded_k
         else:
-            self.q8 = False
+            self.q8 = self.q4 = False
             self.w, self.scales = w.data_ptr(), None
             self.n, self.k = int(w.shape[0]), int(w.shape[1])
             self.kp = self.k
@@ -62,8 +63,8 @@ class Lin:
         ldx = self.k if ldx is None else ldx
         ldy = self.n if ldy is None else ldy
         if self.q8:
-            call("cv3_q8_linear", x, m, self.k, ldx, self.w, self.scales, self.n, self.kp, self.bias,
-                 residual, y, ldy, s)
+            call("cv3_q4_linear" if self.q4 else "cv3_q8_linear", x, m, self.k, ldx, self.w, self.scales, self.n,
+                 self.kp, self.bias, residual, y, ldy, s)
         elif m >= TC_MIN_ROWS and self.k % 4 == 0 and ldx % 4 == 0:
             if residual is not None and residual != y:
                 raise ValueError("tensor-core linear adds the residual in place (residual must alias y)")
@@ -191,21 +192,22 @@ def interleave_rows(a: QTensor, b: QTensor) -> QTensor:
 
 def cat_rows(parts):
     """Stack weights along the output dimension (q8 payload + scales, or fp32)."""
-    if all(isinstance(p, QTensor) for p in parts):
+    if all(isinstance(p, QTensor) for p in parts) and len({p.kind for p in parts}) == 1:
         k = parts[0].shape[1]
         q = torch.cat([p.q for p in parts], 0).contiguous()
         s = torch.cat([p.scales for p in parts], 0).contiguous()
-        return QTensor("q8", q, s, (int(q.shape[0]), k), parts[0].block, None)
+        return QTensor(parts[0].kind, q, s, (int(q.shape[0]), k), parts[0].block, None)
     # mixed storage (small q8 and fp32 parts): stack fp32, dequantised exactly on the GPU
     return torch.cat([f32_of(p) for p in parts], 0).contiguous()
 
 
 def f32_of(w):
-    """fp32 device matrix of a device weight (q8 dequantised on the GPU, exactly)."""
+    """fp32 device matrix of a device weight (q8 / q4 dequantised on the GPU, exactly)."""
     if isinstance(w, QTensor):
         n, k = int(w.shape[0]), int(w.shape[1])
         out = D.empty((n, k))
-        call("cv3_q8_dequant", w.q.data_ptr(), w.scales.data_ptr(), n, w.padded_k, k, out.data_ptr(), D.stream())
+        call("cv3_q4_dequant" if w.kind == "q4" else "cv3_q8_dequant", w.q.data_ptr(), w.scales.data_ptr(), n,
+             w.padded_k, k, out.data_ptr(), D.stream())
         return out
     return w
 

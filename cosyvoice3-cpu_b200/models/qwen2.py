@@ -302,7 +302,7 @@ class DecodeEngine:
             p = f"layers.{i}."
             ws = [L.qkv._keep[0], L.o._keep[0], model._t(p + "mlp.gate_proj.weight"),
                   model._t(p + "mlp.up_proj.weight"), L.down._keep[0]]
-            if all(isinstance(w, QTensor) for w in ws):
+            if all(isinstance(w, QTensor) and w.kind == "q8" for w in ws):   # (q4 layers: generic path)
                 gu = model.w.cache((model.prefix + p + "gate_up_interleaved",), lambda ws=ws: interleave_rows(ws[2], ws[3]))
                 self.fast.append((DecodeGemv(ws[0], L.qkv._keep[1], L.ln1, c.rms_norm_eps),
                                   DecodeGemv(ws[1]),
@@ -311,7 +311,7 @@ class DecodeEngine:
             else:
                 self.fast.append(None)
         self.fast_head = DecodeGemv(head_w, norm_w=model.norm_w(), eps=c.rms_norm_eps) \
-            if isinstance(head_w, QTensor) else None
+            if isinstance(head_w, QTensor) and head_w.kind == "q8" else None
         self._mk = self._persistent_setup()
 
     # -- persistent decode (cv3_decode_steps): every step of a run in one launch ----------
@@ -325,7 +325,7 @@ class DecodeEngine:
         if (B > 8 or c.head_dim != 64 or hid != c.num_attention_heads * 64 or hid % 64 or c.intermediate_size % 64
                 or self.fast_head is None or any(F is None for F in self.fast)
                 or any(g.kp != g.k for F in self.fast for g in F) or self.fast_head.kp != hid
-                or (isinstance(e, QTensor) and e.padded_k != hid)):
+                or (isinstance(e, QTensor) and (e.kind != "q8" or e.padded_k != hid))):
             return None
         ptrs = []
         for i, F in enumerate(self.fast):
@@ -444,7 +444,8 @@ class DecodeEngine:
         """The chosen tokens' speech embeddings become the next step's input rows."""
         e = self.emb
         if isinstance(e, QTensor):
-            call("cv3_embedding", e.q.data_ptr(), 2, e.scales.data_ptr(), int(e.shape[0]), int(e.shape[1]),
+            call("cv3_embedding", e.q.data_ptr(), 3 if e.kind == "q4" else 2, e.scales.data_ptr(), int(e.shape[0]),
+                 int(e.shape[1]),
                  e.padded_k, self.next_ids.data_ptr(), self.B, self.h.data_ptr(), int(e.shape[1]), None, st)
         else:
             call("cv3_embedding", e.data_ptr(), 0, None, int(e.shape[0]), int(e.shape[1]), int(e.shape[1]),

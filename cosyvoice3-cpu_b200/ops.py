@@ -131,7 +131,7 @@ def layer_norm(x, weight=None, bias=None, eps: float = 1e-5):   # cv3cpu/ops.py:
 def _weight_dev(weight):
     """(kind, tensors...) for a linear weight: q8 device QTensor or fp32 matrix."""
     if isinstance(weight, QTensor):
-        if weight.kind != "q8":
+        if weight.kind not in ("q8", "q4"):
             raise ValueError(f"quant kind {weight.kind!r} is not supported by the device build")
         return weight.to_device()
     return D.dev(weight)
@@ -156,8 +156,8 @@ def linear(x, weight: Weight, bias=None, residual=None, out=None):
     bd = D.dev(bias).reshape(-1) if bias is not None else None
     rd = D.dev(residual) if residual is not None else None
     if isinstance(w, QTensor):
-        call("cv3_q8_linear", D.ptr(x2), m, k, k, D.ptr(w.q), D.ptr(w.scales), n, w.padded_k,
-             D.ptr(bd), D.ptr(rd), D.ptr(y), n, D.stream())
+        call("cv3_q4_linear" if w.kind == "q4" else "cv3_q8_linear", D.ptr(x2), m, k, k, D.ptr(w.q),
+             D.ptr(w.scales), n, w.padded_k, D.ptr(bd), D.ptr(rd), D.ptr(y), n, D.stream())
     elif m >= 16 and k % 4 == 0:
         # fp32 weights, enough rows: tensor cores (3xTF32, fp32-level accuracy)
         if rd is not None:
@@ -172,7 +172,7 @@ def linear(x, weight: Weight, bias=None, residual=None, out=None):
 
 def _table_kind(table):
     if isinstance(table, QTensor):
-        return 2
+        return 3 if table.kind == "q4" else 2
     t = table if isinstance(table, torch.Tensor) else np.asarray(table)
     return 1 if t.dtype in (np.float16, torch.float16) else 0
 
@@ -187,7 +187,7 @@ def embedding(table: Weight, ids):
             raise IndexError(f"token id {int(ids.max())} is outside the {rows}-row embedding table")
     idd = D.dev(ids, torch.int64).reshape(-1)
     kind = _table_kind(table)
-    if kind == 2:
+    if kind >= 2:
         t = table.to_device()
         dim, kp = int(t.shape[1]), t.padded_k
         tab, sc = t.q, t.scales
@@ -213,6 +213,8 @@ def conv1d(x, weight: Weight, bias=None, stride: int = 1, dilation: int = 1, gro
     """
     host = D.is_host(x)
     if isinstance(weight, QTensor):
+        if weight.kind != "q8":
+            raise ValueError(f"quantised conv weights of kind {weight.kind!r} are not supported")
         k = kernel_size or weight.kernel_size
         if k is None:
             raise ValueError("kernel_size is required for a quantised conv weight "

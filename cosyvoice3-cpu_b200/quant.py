@@ -18,6 +18,7 @@ from typing import Optional
 import numpy as np
 
 Q8_BLOCK = 64
+Q4_BLOCK = 32
 
 
 @dataclass
@@ -59,11 +60,15 @@ class QTensor:
 
     def dequant_rows(self, r0: int, r1: int) -> np.ndarray:
         """Host fp32 rows (format inspection only; the GPU path never calls this)."""
-        q = np.asarray(self.q)[r0:r1].astype(np.float32)
         s = np.asarray(self.scales)[r0:r1]
         if s.dtype != np.float16:
             s = s.view(np.float16)
         nb = s.shape[1]
+        if self.kind == "q4":   # byte j of a block: code j (low nibble), code j + 16 (high)
+            b = np.asarray(self.q)[r0:r1].reshape(r1 - r0, nb, self.block // 2)
+            q = np.concatenate([(b & 0x0F).astype(np.float32) - 8.0, (b >> 4).astype(np.float32) - 8.0], axis=2)
+        else:
+            q = np.asarray(self.q)[r0:r1].astype(np.float32)
         w = (q.reshape(r1 - r0, nb, self.block) * s.astype(np.float32)[:, :, None])
         return w.reshape(r1 - r0, nb * self.block)[:, : self.shape[1]]
 
@@ -86,9 +91,31 @@ def quantize_q8(w: np.ndarray, block: int = Q8_BLOCK):
     return q.reshape(n, kp), scale.astype(np.float16), kp
 
 
-def make_qtensor(w: np.ndarray, orig_shape=None) -> QTensor:
-    q, s, _ = quantize_q8(w.reshape(w.shape[0], -1))
-    return QTensor("q8", q, s, (w.shape[0], int(np.prod(w.shape[1:]))), Q8_BLOCK,
+def quantize_q4(w: np.ndarray, block: int = Q4_BLOCK):
+    """``(uint8 [N, Kp/2], float16 [N, Kp/block], Kp)``: the "tiny" profile's 4-bit
+    format (``cv3cpu/quant.py:70-86``): per block the largest-magnitude element (first
+    on ties) sets ``scale = ext / -8`` so it maps to code 0; codes ``rint(w / scale +
+    8)`` clipped to [0, 15]; byte j packs code j (low nibble) and j + 16 (high)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, k = w.shape
+    kp = -(-k // block) * block
+    if kp != k:
+        w = np.pad(w, ((0, 0), (0, kp - k)))
+    b = w.reshape(n, kp // block, block)
+    ext = np.take_along_axis(b, np.abs(b).argmax(axis=2)[:, :, None], axis=2)[:, :, 0]
+    scale = (ext / -8.0).astype(np.float32)
+    scale[scale == 0] = 1.0
+    code = np.clip(np.rint(b / scale[:, :, None] + 8.0), 0, 15).astype(np.uint8)
+    half = block // 2
+    packed = (code[:, :, :half] | (code[:, :, half:] << 4)).astype(np.uint8)
+    return packed.reshape(n, kp // 2), scale.astype(np.float16), kp
+
+
+def make_qtensor(w: np.ndarray, orig_shape=None, kind: str = "q8") -> QTensor:
+    if kind not in ("q8", "q4"):
+        raise ValueError(f"unknown quant kind {kind!r}")
+    q, s, _ = (quantize_q4 if kind == "q4" else quantize_q8)(w.reshape(w.shape[0], -1))
+    return QTensor(kind, q, s, (w.shape[0], int(np.prod(w.shape[1:]))), Q4_BLOCK if kind == "q4" else Q8_BLOCK,
                    tuple(orig_shape) if orig_shape is not None else tuple(w.shape))
 
 

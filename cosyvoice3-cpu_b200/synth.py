@@ -45,14 +45,14 @@ HIFT = {"upsample_rates": [8, 5, 3], "upsample_kernel_sizes": [16, 11, 7],
         "nsf_voiced_threshold": 10.0, "conv_pre_look_right": 4}
 
 # storage kind per profile: (default kind, LM body kind, min elements to quantise)
-PROFILES = {"balanced": ("q8", "q8", 1 << 16), "f32": ("f32", "f32", 1 << 62)}
+PROFILES = {"balanced": ("q8", "q8", 1 << 16), "tiny": ("q8", "q4", 1 << 16), "f32": ("f32", "f32", 1 << 62)}
 _KEEP_F32 = re.compile(r"(\.bias$)|(layernorm)|(\.norm$)|(alpha)|(f0_predictor)|(l_linear)|"
                        r"(spk_embed_affine)|(conv_pos_embed)")
 _KEEP_F16 = re.compile(r"^hift\.|(flow\.input_embedding$)|(proj_out)|(time_embed)|(pre_lookahead)")
 
 
 def storage_kind(name: str, shape, profile: str) -> str:
-    """q8 / f16 / f32 for one tensor; the rules of convert.py:255-265 and :300-302."""
+    """q8 / q4 / f16 / f32 for one tensor; the rules of convert.py:255-265 and :300-302."""
     default, lm_kind, min_numel = PROFILES[profile]
     if len(shape) == 1 or _KEEP_F32.search(name) or int(np.prod(shape)) < min_numel:
         return "f32"
@@ -68,8 +68,8 @@ def _tensor(name: str, shape, profile: str, ones: bool = False):
     arr = (np.ones(shape, np.float32) if ones else
            np.random.default_rng(zlib.crc32(name.encode())).standard_normal(shape, dtype=np.float32) * 0.02)
     kind = storage_kind(name, shape, profile)
-    if kind == "q8":
-        return make_qtensor(arr.reshape(arr.shape[0], -1), orig_shape=arr.shape)
+    if kind in ("q8", "q4"):
+        return make_qtensor(arr.reshape(arr.shape[0], -1), orig_shape=arr.shape, kind=kind)
     if kind == "f16":
         return arr.astype(np.float16)
     return arr

@@ -126,9 +126,9 @@ class WeightFile:
         if q is None:
             out = self._raw(name)
         else:
-            if q["kind"] != "q8":
+            if q["kind"] not in ("q8", "q4"):
                 raise ValueError(f"{name}: quant kind {q['kind']!r} is not supported by the device build")
-            out = QTensor("q8", self._raw(name), self._raw(name + SCALES_SUFFIX),
+            out = QTensor(q["kind"], self._raw(name), self._raw(name + SCALES_SUFFIX),
                           tuple(q["mshape"]), int(q["block"]), tuple(q["shape"]))
         self._cache[name] = out
         return out

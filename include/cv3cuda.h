@@ -111,6 +111,19 @@ int cv3_f32_linear(const float* x, int64_t m, int64_t k, int64_t ldx,
 int cv3_q8_dequant(const int8_t* q, const uint16_t* scales, int64_t n, int64_t kp,
                    int64_t k, float* out, void* stream);
 
+/* The q4 "tiny"-profile linear, cv3cpu/quant.py:156-204 with a QTensor of kind
+ * "q4" (format quant.py:70-86, expansion :124-131): y[m][n] = x[m][k] . W[n][k]
+ * (+ bias[n]) (+ residual[m][n]), W = (code - 8) * fp16 scale per 32-wide block;
+ * payload uint8 [n][kp/2] (byte j of a block: code j low nibble, code j + 16 high
+ * nibble), scales [n][kp/32], kp = k rounded up to 32.  Any m (8 rows per pass). */
+int cv3_q4_linear(const float* x, int64_t m, int64_t k, int64_t ldx, const uint8_t* q, const uint16_t* scales,
+                  int64_t n, int64_t kp, const float* bias, const float* residual, float* y, int64_t ldy,
+                  void* stream);
+
+/* q4 weight -> fp32 [n][k] (exact); cv3cpu/quant.py:110-133 (QTensor.dequant_rows, q4 branch). */
+int cv3_q4_dequant(const uint8_t* q, const uint16_t* scales, int64_t n, int64_t kp, int64_t k, float* out,
+                   void* stream);
+
 /* ------------------------------------------------------------------ */
 /* elementwise and normalisation                                        */
 /* ------------------------------------------------------------------ */
@@ -152,10 +165,11 @@ int cv3_snake(const float* x, const float* alpha, int64_t batch, int64_t channel
 #define CV3_TABLE_F32 0
 #define CV3_TABLE_F16 1
 #define CV3_TABLE_Q8 2
+#define CV3_TABLE_Q4 3
 
-/* out[i][:] = table[ids[i]][:] widened to fp32 (q8: dequantised row).
+/* out[i][:] = table[ids[i]][:] widened to fp32 (q8 / q4: dequantised row).
  * Replaces cv3cpu/ops.py:126-144 (embedding).  ids: device int64[n];
- * table: f32/f16 [rows][dim] or q8 [rows][kp] with scales.  Rows outside
+ * table: f32/f16 [rows][dim], q8 [rows][kp] or q4 [rows][kp/2] with scales.  Rows outside
  * the table produce zeros and increment *bad (device int, may be NULL);
  * the host raises IndexError before launching for host-side ids. */
 int cv3_embedding(const void* table, int kind, const uint16_t* scales, int64_t rows, int64_t dim,

@@ -68,15 +68,48 @@ def quantize_q8(w: np.ndarray, block: int = Q8_BLOCK):
     return q.reshape(rows, kp), scale.astype(np.float16), kp
 
 
-def dequant_rows(w, r0: int, r1: int) -> np.ndarray:
-    """fp32 rows ``[r0, r1)`` of a q8 weight, padding sliced off; quant.py:110-133.
+Q4_BLOCK = 32  # quant.py:32
 
-    ``float32(q) * float32(scale)`` is exact (8 x 11 significant bits).
+
+def quantize_q4(w: np.ndarray, block: int = Q4_BLOCK):
+    """llama.cpp-style Q4_0 per (row, 32-wide K block); quant.py:70-86.
+
+    The block's largest-magnitude element (first on ties) fixes the scale
+    ``s = ext / -8``, so it lands exactly on code 0; codes ``rint(w / s + 8)``
+    clipped to [0, 15]; byte j of a block packs code j (low nibble) and code
+    j + 16 (high nibble).  Returns ``(uint8 payload [N, Kp/2], float16 scales
+    [N, Kp/block], Kp)``; an all-zero block gets scale 1.
+    """
+    w = np.ascontiguousarray(w, dtype=F32)
+    rows, k = w.shape
+    kp = -(-k // block) * block
+    if kp != k:
+        w = np.concatenate([w, np.zeros((rows, kp - k), F32)], axis=1)
+    blk = w.reshape(rows, kp // block, block)
+    pick = np.abs(blk).argmax(axis=2)
+    ext = np.take_along_axis(blk, pick[:, :, None], axis=2)[:, :, 0]
+    scale = (ext / -8.0).astype(F32)
+    scale[scale == 0] = 1.0
+    code = np.clip(np.rint(blk / scale[:, :, None] + 8.0), 0, 15).astype(np.uint8)
+    half = block // 2
+    packed = (code[:, :, :half] | (code[:, :, half:] << 4)).astype(np.uint8)
+    return packed.reshape(rows, kp // 2), scale.astype(np.float16), kp
+
+
+def dequant_rows(w, r0: int, r1: int) -> np.ndarray:
+    """fp32 rows ``[r0, r1)`` of a q8 or q4 weight, padding sliced off; quant.py:110-133.
+
+    q8: ``float32(q) * float32(scale)``; q4: ``(float32(code) - 8) * float32(scale)``,
+    low nibbles first within each block.  Both are exact in fp32.
     """
     nb = w.scales.shape[1]
     blk = w.block
     rows = r1 - r0
-    wide = w.q[r0:r1].reshape(rows, nb, blk).astype(F32)
+    if getattr(w, "kind", "q8") == "q4":
+        b = np.asarray(w.q[r0:r1]).reshape(rows, nb, blk // 2)
+        wide = np.concatenate([(b & 0x0F).astype(F32) - F32(8.0), (b >> 4).astype(F32) - F32(8.0)], axis=2)
+    else:
+        wide = w.q[r0:r1].reshape(rows, nb, blk).astype(F32)
     wide *= w.scales[r0:r1].astype(F32)[:, :, None]
     return wide.reshape(rows, nb * blk)[:, : w.shape[1]]
 

@@ -192,3 +192,23 @@ def test_oracle_sampler_matches_reference(strict):
         assert a == b, i
         decoded.append(a)
     assert cfg.rng.bit_generator.state == rng.bit_generator.state
+
+
+@pytest.mark.skipif(not have_reference(), reason="reference checkout not present")
+def test_oracle_q4_matches_reference():
+    """q4 ('tiny' profile) writer and expansion: byte-identical payload and scales to
+    cv3cpu.quant.quantize_q4 (quant.py:70-86), identical rows to QTensor.dequant_rows."""
+    sys.path.insert(0, REFERENCE)
+    from cv3cpu import quant as rq
+    rng = np.random.default_rng(8)
+    for n, k in [(37, 96), (64, 100), (5, 31)]:
+        w = (rng.normal(size=(n, k)) * 0.05).astype(np.float32)
+        w[0, :5] = 0.0
+        w[1, :32] = 0.0                       # an all-zero block
+        w[2, 3] = -w[2, :32].__abs__().max()  # negative extreme
+        q, s, kp = nx.quantize_q4(w)
+        rq_q, rq_s, rq_kp = rq.quantize_q4(w)
+        assert kp == rq_kp and np.array_equal(q, rq_q) and np.array_equal(s, rq_s)
+        ref = rq.QTensor("q4", rq_q, rq_s, (n, k), rq.Q4_BLOCK).dequant()
+        got = nx.dequant(nx.QTensor("q4", q, s, (n, k), nx.Q4_BLOCK))
+        assert np.array_equal(ref, got)
