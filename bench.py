@@ -67,6 +67,28 @@ def make_requests(seeds, meta):
 
 
 # ---------------------------------------------------------------------------
+# multi-GPU plumbing: one process per GPU, utterances sharded, no data-path collective
+# ---------------------------------------------------------------------------
+
+def rank_seeds(rank: int, per_rank: int = None) -> range:
+    """The utterance seeds rank ``rank`` synthesises: a disjoint block per rank (weak
+    scaling: every GPU gets the same amount of work)."""
+    per_rank = UTTS if per_rank is None else per_rank
+    return range(rank * per_rank, (rank + 1) * per_rank)
+
+
+def max_over_ranks(ms: float, world: int, device="cuda") -> float:
+    """The job's time for a step: the slowest rank's (one all-reduce MAX; timing only)."""
+    if world <= 1:
+        return float(ms)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(ms)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 
@@ -264,7 +286,7 @@ def run_cuda(args, rank: int, world: int) -> None:
     synth, pipeline, L = pkg("synth"), pkg("pipeline"), pkg("_lib")
     W = synth.synthetic_weights("balanced")
     tts = pipeline.CosyVoice3CUDA(W)
-    seeds = range(rank * UTTS, rank * UTTS + UTTS)
+    seeds = rank_seeds(rank)
     reqs = make_requests(seeds, W.meta)
     prepared = tts.prepare(reqs)
     for _ in range(max(args.warmup, 1)):
@@ -288,11 +310,7 @@ def run_cuda(args, rank: int, world: int) -> None:
         torch.cuda.synchronize()
     barrier()
     launches = L.executed_launches() - l0
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
 
     # -- e2e: host inputs in, host waveforms out, through the public API --------------------
     barrier()
@@ -306,11 +324,7 @@ def run_cuda(args, rank: int, world: int) -> None:
     f1.record()
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = f0.elapsed_time(f1) / args.steps
-    t = torch.tensor([e2e_ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
     d2h = int(wav_h.nbytes)
 
     peaks = json.load(open(PEAKS)) if os.path.exists(PEAKS) else {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
