@@ -434,11 +434,24 @@ def run_lm_step(args) -> None:
     import torch
     B = args.lm_step
     W = pkg("synth").synthetic_weights("balanced", stages=("llm",))
-    lm = pkg("models.llm").CosyVoice3LM(pkg("weights").DeviceWeights(W))
+    llm = pkg("models.llm")
+    lm = llm.CosyVoice3LM(pkg("weights").DeviceWeights(W))
     rng = np.random.default_rng(3)
     prompts = [(rng.normal(size=(130 + 5 * i, 896)) * 0.1).astype(np.float32) for i in range(B)]
-    eng = lm.engine(B, 512, 260)
-    eng.run(prompts, 2, use_graph=True)
+    if args.sampled:
+        # the sampled step (device sampler as the last kernel), every sequence kept running
+        # (all stop ids masked: strict min length over the whole timed run)
+        cfg = llm.SamplingConfig(seed=0)
+        eng = lm.sampling_engine(B, 512, 260, cfg, True)
+        st = cfg.rng.bit_generator.state["state"]
+        eng.run_sampled(prompts, [(st["state"], st["inc"])] * B, [2] * B, [2] * B)
+        eng.min_len.fill_(250)
+        eng.max_len.fill_(250)
+        eng.done.zero_()
+        eng.count.zero_()
+    else:
+        eng = lm.engine(B, 512, 260)
+        eng.run(prompts, 2, use_graph=True)
     for _ in range(20):
         eng.step()
     torch.cuda.synchronize()
@@ -450,6 +463,17 @@ def run_lm_step(args) -> None:
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) / n * 1e3
+    if args.sampled:
+        # the host-sampler path of generate(): a device forward, the log-probs to the host and
+        # numpy's sampler, per token (batch 1)
+        text = [int(W.meta.get("endofprompt_id", 151646))] + list(range(100, 130))
+        cfg = llm.SamplingConfig(seed=0, min_token_text_ratio=0.0, max_token_text_ratio=2.0)
+        t0 = time.perf_counter()
+        ntok = len(list(lm.generate(text, (), [1, 2, 3], sampling=cfg, device_sampler=False)))
+        host_ms = (time.perf_counter() - t0) * 1e3 / max(ntok, 1)
+        print(json.dumps({"lm_sampled_step_us": round(us, 1), "batch": B,
+                          "host_sampler_ms_per_token": round(host_ms, 3), "host_tokens": ntok}), flush=True)
+        return
     print(json.dumps({"lm_decode_step_us": round(us, 1), "batch": B, "weight_bytes_per_step": 375255804,
                       "weight_stream_gbs": round(375255804 / (us * 1e-6) / 1e9, 1)}), flush=True)
 
@@ -458,6 +482,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--lm-step", type=int, default=0, metavar="B",
                     help="time the LM decode step alone at batch B (1..8)")
+    ap.add_argument("--sampled", action="store_true",
+                    help="with --lm-step: the sampled step (device sampler) and the host-sampler path")
     ap.add_argument("--slice", action="store_true", help="profiling slice (see run_slice)")
     ap.add_argument("--kernel", choices=["ff1", "attention", "conv", "gemv"],
                     help="run one hot kernel alone at its bench shape (for ncu captures)")

@@ -127,6 +127,81 @@ __device__ T np_pairwise(const T* a, int n) {
   }
 }
 
+constexpr int MAX_LEAVES = 256;  // n <= 10240 (the launcher's limit): leaves of > 64 terms, <= 160
+
+// numpy's pairwise sum of a[0..n) by the whole block, bit-identical to np_pairwise:
+// thread 0 lists the tree's leaves (blocks of <= 128 terms) left to right, the block
+// sums them in parallel with the eight-accumulator rule, and thread 0 adds the leaf
+// sums up the same tree.  Returns the sum to every thread.
+template <typename T>
+__device__ T np_pairwise_block(const T* a, int n, T* leafsum, int* leafoff, int* leaflen, int* nleaves, T* out) {
+  constexpr int DEPTH = 16;  // n <= 10240: at most 9 levels
+  if (threadIdx.x == 0) {
+    int off[DEPTH], len[DEPTH], sp = 0, nl = 0;
+    off[0] = 0;
+    len[0] = n;
+    while (sp >= 0) {  // pre-order with the right half pushed first: leaves in order
+      const int o = off[sp], m = len[sp];
+      --sp;
+      if (m <= 128) {
+        leafoff[nl] = o;
+        leaflen[nl] = m;
+        ++nl;
+      } else {
+        const int m2 = np_half(m);
+        off[++sp] = o + m2;
+        len[sp] = m - m2;
+        off[++sp] = o;
+        len[sp] = m2;
+      }
+    }
+    *nleaves = nl;
+  }
+  __syncthreads();
+  const int nl = *nleaves;
+  for (int l = threadIdx.x; l < nl; l += blockDim.x) leafsum[l] = np_pairwise_leaf(a + leafoff[l], leaflen[l]);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // post-order walk of the same tree, a leaf's sum taken from leafsum in order
+    int len[DEPTH], stage[DEPTH];
+    T left[DEPTH];
+    int sp = 0, leaf = 0;
+    len[0] = n;
+    stage[0] = 0;
+    bool done = false;
+    while (!done) {
+      const int m = len[sp];
+      if (m <= 128) {
+        T v = leafsum[leaf++];
+        while (true) {  // hand the value up until a left half completes
+          if (sp == 0) {
+            *out = v;
+            done = true;
+            break;
+          }
+          --sp;
+          if (stage[sp] == 0) {
+            left[sp] = v;
+            stage[sp] = 1;
+            len[sp + 1] = len[sp] - np_half(len[sp]);
+            stage[sp + 1] = 0;
+            ++sp;
+            break;
+          }
+          v = left[sp] + v;
+        }
+      } else {
+        stage[sp] = 0;
+        len[sp + 1] = np_half(m);
+        stage[sp + 1] = 0;
+        ++sp;
+      }
+    }
+  }
+  __syncthreads();
+  return *out;
+}
+
 // first index whose cumulative share exceeds u: searchsorted(cdf / cdf[-1], u, 'right')
 __device__ int search_right(const double* cdf, int n, double u) {
   const double last = cdf[n - 1];
@@ -141,16 +216,23 @@ __device__ int search_right(const double* cdf, int n, double u) {
 
 __device__ __forceinline__ bool before(float v, int i, float w, int j) { return v > w || (v == w && i < j); }
 
-// softmax of src into dst (max, exp(x - max), numpy-order float32 sum by thread 0, divide)
-__device__ void softmax_block(const float* src, float* dst, int V, float* red, float* bcast) {
+struct SumScratch {  // shared memory of np_pairwise_block
+  float leaf_f[MAX_LEAVES];
+  double leaf_d[MAX_LEAVES];
+  int off[MAX_LEAVES], len[MAX_LEAVES];
+  int nleaves;
+  float out_f;
+  double out_d;
+};
+
+// softmax of src into dst (max, exp(x - max), numpy-order float32 sum, divide)
+__device__ void softmax_block(const float* src, float* dst, int V, float* red, SumScratch& ss) {
   float m = -INFINITY;
   for (int i = threadIdx.x; i < V; i += ST) m = fmaxf(m, src[i]);
   m = block_max(m, red);
   for (int i = threadIdx.x; i < V; i += ST) dst[i] = expf(src[i] - m);
   __syncthreads();
-  if (threadIdx.x == 0) *bcast = np_pairwise(dst, V);
-  __syncthreads();
-  const float s = *bcast;
+  const float s = np_pairwise_block(dst, V, ss.leaf_f, ss.off, ss.len, &ss.nleaves, &ss.out_f);
   for (int i = threadIdx.x; i < V; i += ST) dst[i] = dst[i] / s;
   __syncthreads();
 }
@@ -163,7 +245,7 @@ __global__ void __launch_bounds__(ST) sample_select_kernel(SampleArgs a) {
   float* pr = lp + V;                                // [V] probabilities
   float* work = reinterpret_cast<float*>(cdf);
   __shared__ float red[32];
-  __shared__ float fb;
+  __shared__ SumScratch ss;
   __shared__ float candv[SW][KMAX];
   __shared__ int candi[SW][KMAX];
   __shared__ float topv[KMAX];
@@ -190,9 +272,7 @@ __global__ void __launch_bounds__(ST) sample_select_kernel(SampleArgs a) {
     pr[i] = expf(z);
   }
   __syncthreads();
-  if (tid == 0) fb = logf(np_pairwise(pr, V));
-  __syncthreads();
-  const float lse = fb;
+  const float lse = logf(np_pairwise_block(pr, V, ss.leaf_f, ss.off, ss.len, &ss.nleaves, &ss.out_f));
   for (int i = tid; i < V; i += ST) {
     const float v = lp[i] - lse;
     lp[i] = v;
@@ -208,7 +288,7 @@ __global__ void __launch_bounds__(ST) sample_select_kernel(SampleArgs a) {
     }
   }
   __syncthreads();
-  softmax_block(lp, pr, V, red, &fb);
+  softmax_block(lp, pr, V, red, ss);
   // -- top-k by (probability desc, index asc): each warp its chunk, then a 32-way merge -------
   const int K = min(a.top_k, V);
   for (int i = tid; i < V; i += ST) work[i] = pr[i];
@@ -311,20 +391,24 @@ __global__ void __launch_bounds__(ST) sample_select_kernel(SampleArgs a) {
     // resample from the whole distribution with the pick removed
     if (tid == 0) lp[s_top] = -INFINITY;
     __syncthreads();
-    softmax_block(lp, pr, V, red, &fb);
+    softmax_block(lp, pr, V, red, ss);
     for (int i = tid; i < V; i += ST) cdf[i] = (double)pr[i];
     __syncthreads();
-    __shared__ double db;
-    if (tid == 0) db = np_pairwise(cdf, V);
-    __syncthreads();
-    const double s = db;
+    const double s = np_pairwise_block(cdf, V, ss.leaf_d, ss.off, ss.len, &ss.nleaves, &ss.out_d);
     for (int i = tid; i < V; i += ST) cdf[i] = cdf[i] / s;
     __syncthreads();
     if (tid == 0) {
-      double acc = 0.0;
-      for (int i = 0; i < V; ++i) {
-        acc += cdf[i];
-        cdf[i] = acc;
+      double acc = 0.0;  // cumsum: sequential by definition; loads run ahead of the chain
+      for (int i = 0; i < V; i += 8) {
+        double v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = i + j < V ? cdf[i + j] : 0.0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (i + j < V) {
+            acc += v[j];
+            cdf[i + j] = acc;
+          }
       }
       uint64_t* rs = a.rng + 4 * (int64_t)b;
       unsigned __int128 state = ((unsigned __int128)rs[0] << 64) | rs[1];
