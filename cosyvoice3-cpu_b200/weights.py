@@ -3,7 +3,8 @@
 Format (``cv3cpu/io/weights.py:1-14``, ``:60-86``; container
 ``cv3cpu/io/safetensors_io.py``): a standard safetensors file -- little-endian
 u64 header length, JSON header, packed tensor data.  A q8 weight stores its
-int8 payload under its own name (``I8``) and its float16 scales under
+int8 payload under its own name (``I8``; a q4 weight its packed nibbles, ``U8``)
+and its float16 scales under
 ``<name>.__scales__`` (``F16``); the JSON string ``__metadata__["cv3cpu"]``
 holds ``{"version", "meta", "quant": {name: {kind, block, shape, mshape}}}``.
 
@@ -52,7 +53,8 @@ def write_weights(path: str, tensors: Dict[str, Any], meta: Dict[str, Any]) -> N
     for name in tensors:
         t = tensors[name]
         if isinstance(t, QTensor):
-            add(name, np.asarray(t.q, dtype=np.int8))
+            # q8 payloads are int8 (I8); q4 payloads packed nibbles, uint8 (U8) as quant.py:70-86 makes them
+            add(name, np.asarray(t.q).view(np.uint8 if t.kind == "q4" else np.int8))
             sc = np.asarray(t.scales)
             add(name + SCALES_SUFFIX, sc if sc.dtype == np.float16 else sc.view(np.float16))
             quant[name] = {"kind": t.kind, "block": t.block,

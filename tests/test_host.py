@@ -20,6 +20,23 @@ def test_quantize_q8_matches_the_oracle():
         assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]) and a[2] == b[2]
 
 
+def test_quantize_q4_matches_the_oracle():
+    """The 'tiny' profile's 4-bit writer: payload, scales and padded K equal the oracle's
+    (itself pinned byte-for-byte to cv3cpu.quant.quantize_q4), negative extremes land on
+    code 0, zero blocks get scale 1, and the host expansion equals the oracle's."""
+    rng = np.random.default_rng(7)
+    for shape in [(9, 100), (64, 64), (33, 31), (4, 32)]:
+        w = rng.normal(size=shape).astype(np.float32)
+        w[0, :32] = 0.0
+        a = pkg("quant").quantize_q4(w)
+        b = nx.quantize_q4(w)
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]) and a[2] == b[2]
+        assert np.all(a[1][0, 0] == 1.0)
+        t = pkg("quant").make_qtensor(w, kind="q4")
+        assert t.kind == "q4" and t.padded_k == b[2] and t.q.shape == (shape[0], b[2] // 2)
+        assert np.array_equal(t.dequant(), nx.dequant(nx.QTensor("q4", b[0], b[1], shape, nx.Q4_BLOCK)))
+
+
 def test_zero_blocks_get_unit_scale():
     q, s, _ = pkg("quant").quantize_q8(np.zeros((4, 64), np.float32))
     assert np.all(s == 1.0) and np.all(q == 0)
@@ -63,6 +80,30 @@ def test_reference_reads_our_files(tmp_path):
     r.close()
 
 
+def test_q4_weight_file_round_trip_and_reference_reader(tmp_path):
+    """A 'tiny' file: the q4 token table is written with its kind and block, read back
+    bit-equal by this package's reader and, when the reference checkout is present, by
+    cv3cpu's own reader with the same expansion."""
+    W = pkg("weights")
+    syn = pkg("synth").synthetic_weights("tiny", small=True, stages=("llm",))
+    name = "llm.model.embed_tokens"                      # q4 in the small tiny model
+    assert syn[name].kind == "q4"
+    path = str(tmp_path / "t.safetensors")
+    W.write_weights(path, dict(syn), syn.meta)
+    f = W.WeightFile(path)
+    qt = f.get(name)
+    assert qt.kind == "q4" and qt.block == 32 and f.entry(name)["kind"] == "q4"
+    assert np.array_equal(qt.q, syn[name].q) and np.array_equal(qt.scales, syn[name].scales)
+    assert np.array_equal(qt.dequant(), syn[name].dequant())
+    f.close()
+    if have_reference():
+        sys.path.insert(0, REFERENCE)
+        from cv3cpu.io.weights import WeightFile as RefWF
+        r = RefWF(path)
+        assert np.array_equal(r.get_f32(name), syn[name].dequant())
+        r.close()
+
+
 def test_synthetic_storage_kinds_follow_the_balanced_profile():
     k = pkg("synth").storage_kind
     assert k("llm.model.layers.0.mlp.up_proj.weight", (4864, 896), "balanced") == "q8"
@@ -74,6 +115,18 @@ def test_synthetic_storage_kinds_follow_the_balanced_profile():
     assert k("hift.f0_predictor.condnet.0.weight", (512, 80, 4), "balanced") == "f32"
     assert k("llm.model.layers.0.input_layernorm", (896,), "balanced") == "f32"
     assert k("llm.model.layers.0.mlp.up_proj.weight", (4864, 896), "f32") == "f32"
+
+
+def test_synthetic_storage_kinds_follow_the_tiny_profile():
+    """'tiny' (convert.py PROFILES): the LM body and its token table 4-bit, the rest as balanced."""
+    k = pkg("synth").storage_kind
+    assert k("llm.model.layers.0.mlp.up_proj.weight", (4864, 896), "tiny") == "q4"
+    assert k("llm.model.embed_tokens", (151936, 896), "tiny") == "q4"
+    assert k("llm.llm_decoder.weight", (6761, 896), "tiny") == "q8"
+    assert k("llm.speech_embedding", (6761, 896), "tiny") == "q8"
+    assert k("flow.decoder.estimator.transformer_blocks.0.attn.to_q.weight", (1024, 1024), "tiny") == "q8"
+    assert k("hift.ups.0.weight", (256, 512, 16), "tiny") == "f16"
+    assert k("llm.model.layers.0.input_layernorm", (896,), "tiny") == "f32"
 
 
 def test_synthetic_small_model_geometry():
