@@ -129,7 +129,7 @@ def layer_norm(x, weight=None, bias=None, eps: float = 1e-5):   # cv3cpu/ops.py:
 
 
 def _weight_dev(weight):
-    """(kind, tensors...) for a linear weight: q8 device QTensor or fp32 matrix."""
+    """(kind, tensors...) for a linear weight: q8 / q4 device QTensor or fp32 matrix."""
     if isinstance(weight, QTensor):
         if weight.kind not in ("q8", "q4"):
             raise ValueError(f"quant kind {weight.kind!r} is not supported by the device build")
@@ -140,7 +140,7 @@ def _weight_dev(weight):
 def linear(x, weight: Weight, bias=None, residual=None, out=None):
     """``x @ weight.T + bias`` with ``weight`` ``(out, in)``; cv3cpu/ops.py:121-123.
 
-    ``weight`` may be a q8 :class:`QTensor` (``cv3cpu/quant.py:156``) or a plain
+    ``weight`` may be a q8 or q4 :class:`QTensor` (``cv3cpu/quant.py:156``) or a plain
     fp32/fp16 matrix.  ``residual`` (device extension) is added after the bias.
     """
     host = D.is_host(x)

@@ -1,12 +1,15 @@
-"""q8 block-quantised weights and the quantised linear, on the GPU.
+"""Block-quantised weights (q8 and q4) and the quantised linear, on the GPU.
 
-Layout (the reference's "balanced" format, ``cv3cpu/quant.py:9-19``): a weight
-of logical shape ``(N, K)`` is stored as an ``int8[N, Kp]`` payload, K padded
-with zeros up to a multiple of 64, plus ``float16[N, Kp/64]`` scales, one per
-(row, 64-wide K block).  ``W[n, k] = float32(q[n, k]) * float32(s[n, k // 64])``.
+q8 (the reference's "balanced" format, ``cv3cpu/quant.py:9-19``): a weight of
+logical shape ``(N, K)`` is stored as an ``int8[N, Kp]`` payload, K padded with
+zeros up to a multiple of 64, plus ``float16[N, Kp/64]`` scales, one per (row,
+64-wide K block).  ``W[n, k] = float32(q[n, k]) * float32(s[n, k // 64])``.
+q4 (the "tiny" profile's LM body, ``cv3cpu/quant.py:70-86``): 32-wide blocks,
+``uint8[N, Kp/2]`` with byte j of a block holding code j (low nibble) and code
+j + 16 (high nibble), ``W = (code - 8) * scale``.
 
-``quantize_q8`` is the format's writer (offline, host side, identical in
-result to ``cv3cpu/quant.py:56-67``).  ``qmatmul`` -- the operation the models
+``quantize_q8`` / ``quantize_q4`` are the format's writers (offline, host side,
+identical in result to ``cv3cpu/quant.py:56-86``).  ``qmatmul`` -- the operation the models
 run -- executes on the GPU through ``libcv3cuda.so`` and has no CPU path.
 """
 
