@@ -174,6 +174,26 @@ class SpeechLM:
             x = self.speech_emb([nxt])
         return toks, np.stack(logps) if logps else np.zeros((0, 0), F32)
 
+    def generate_sampled(self, x0, n_new_text: int, rng, min_ratio: float = 2.0, max_ratio: float = 20.0,
+                         strict_min_len: bool = False, top_p: float = 0.8, top_k: int = 25,
+                         win_size: int = 10, tau_r: float = 0.1):
+        """The reference's sampling loop (llm.py:107-123) from prompt embeddings ``x0``:
+        min / max lengths from the new text's length, one forward per step, the sampler of
+        llm.py:125-149 (``nx.sample_token``) drawing from ``rng``; a stop id ends it."""
+        min_len, max_len = int(n_new_text * min_ratio), int(n_new_text * max_ratio)
+        cache = self.body.new_cache()
+        out, x = [], x0
+        sts = self.speech_token_size
+        for i in range(max_len):
+            h = self.body.forward(x, cache)
+            logp = nx.log_softmax(self.head(h[-1:]).astype(F32), axis=-1)[0]
+            top = nx.sample_token(logp, out, rng, sts, i < min_len, strict_min_len, top_p, top_k, win_size, tau_r)
+            if sts <= top < sts + 200:
+                break
+            out.append(top)
+            x = self.speech_emb([top])
+        return out
+
 
 # ---------------------------------------------------------------------------
 # DiT estimator                                          cv3cpu/models/dit.py

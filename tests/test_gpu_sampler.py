@@ -94,3 +94,30 @@ def test_generate_device_sampler_matches_host_sampler(small_weights, profile):
         host = list(lm.generate(text, (), sp, sampling=b, device_sampler=False))
         assert dev == host, trial
         assert a.rng.bit_generator.state == b.rng.bit_generator.state
+
+
+@pytest.mark.parametrize("profile", ["balanced", "f32"])
+def test_generate_matches_oracle_sampled_generation(small_weights, profile):
+    """CosyVoice3LM.generate (graph-replayed steps, device sampler) against the oracle's
+    restatement of the reference's sampling loop (pinned to CosyVoice3LM.generate itself):
+    the same tokens, stops and min/max lengths, and the generator left in the same state."""
+    import oracle.stages as st
+    W = small_weights[profile]
+    llm = pkg("models.llm")
+    lm = llm.CosyVoice3LM(pkg("weights").DeviceWeights(W))
+    olm = st.SpeechLM(W, W.meta)
+    eop = W.meta["endofprompt_id"]
+    data = np.random.default_rng(2)
+    total = 0
+    for trial, (lo, strict) in enumerate([(2.0, True), (3.0, True), (1.0, False), (2.5, True)]):
+        text = data.integers(0, 2000, size=6 + 3 * trial).tolist()
+        speech = data.integers(0, 256, size=4).tolist()
+        cfg = llm.SamplingConfig(seed=30 + trial, max_token_text_ratio=4.0, min_token_text_ratio=lo,
+                                 strict_min_len=strict)
+        got = list(lm.generate(text, [eop], speech, sampling=cfg))
+        rng = np.random.default_rng(30 + trial)
+        want = olm.generate_sampled(olm.prompt_embedding(text, [eop], speech), len(text), rng, lo, 4.0, strict)
+        assert got == want, trial
+        assert cfg.rng.bit_generator.state == rng.bit_generator.state
+        total += len(want)
+    assert total >= 40

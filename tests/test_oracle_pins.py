@@ -15,7 +15,7 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import REFERENCE, have_reference, rel_err
+from conftest import REFERENCE, have_reference, pkg, rel_err
 
 import oracle.numerics as nx
 import oracle.stages as st
@@ -212,3 +212,37 @@ def test_oracle_q4_matches_reference():
         ref = rq.QTensor("q4", rq_q, rq_s, (n, k), rq.Q4_BLOCK).dequant()
         got = nx.dequant(nx.QTensor("q4", q, s, (n, k), nx.Q4_BLOCK))
         assert np.array_equal(ref, got)
+
+
+@pytest.mark.skipif(not have_reference(), reason="reference checkout not present")
+@pytest.mark.parametrize("profile", ["balanced", "f32"])
+def test_oracle_sampled_generation_matches_reference(tmp_path, profile):
+    """The oracle's sampling loop against CosyVoice3LM.generate (llm.py:80-123) on the small
+    synthetic model read through the reference's own weight reader: identical tokens
+    (stops, min/max lengths, repetition redraws) and the generator left in the same state."""
+    sys.path.insert(0, REFERENCE)
+    from cv3cpu.io.weights import WeightFile as RefWF
+    from cv3cpu.models import llm as rl
+    W = pkg("weights")
+    syn = pkg("synth").synthetic_weights(profile, small=True, stages=("llm",))
+    path = str(tmp_path / "lm.safetensors")
+    W.write_weights(path, dict(syn), syn.meta)
+    ref = rl.CosyVoice3LM(RefWF(path))
+    olm = st.SpeechLM(syn, syn.meta)
+    eop = syn.meta["endofprompt_id"]
+    data = np.random.default_rng(2)
+    total = 0
+    # (min ratio, strict): the small model's 200 stop ids are a large share of its speech
+    # vocabulary, so most trials mask all of them up to min_len to get long samples
+    for trial, (lo, strict) in enumerate([(2.0, True), (3.0, True), (1.0, False), (2.5, True), (1.5, True)]):
+        text = data.integers(0, 2000, size=6 + 3 * trial).tolist()
+        prompt_text = [eop]
+        speech = data.integers(0, 256, size=4).tolist()
+        cfg = rl.SamplingConfig(seed=30 + trial, max_token_text_ratio=4.0, min_token_text_ratio=lo)
+        want = list(ref.generate(text, prompt_text, speech, sampling=cfg, strict_min_len=strict))
+        rng = np.random.default_rng(30 + trial)
+        got = olm.generate_sampled(olm.prompt_embedding(text, prompt_text, speech), len(text), rng, lo, 4.0, strict)
+        assert got == want, trial
+        assert rng.bit_generator.state == cfg.rng.bit_generator.state
+        total += len(want)
+    assert total >= 60
