@@ -13,10 +13,17 @@ Run in a checkout that has the reference project importable (its root on
   ``balanced`` (q8) and ``f32`` profiles.  Inputs are seeded and stored beside
   the outputs.
 
+* ``sampling_small.npz`` -- the reference's q4 writer on a seeded matrix
+  (``quant.quantize_q4``), 200 steps of its sampler (``CosyVoice3LM._sample``
+  on log-probabilities of seeded logits, with stops, min-length masking in both
+  modes and repetition redraws) with the final generator state, and its sampled
+  ``generate`` on the small ``balanced`` model.  The seeds that regenerate the
+  inputs are stored beside the outputs.
+
 It also asserts that the synthetic generator reproduces the reference's own
 random-model generator tensor for tensor.
 
-    python tests/golden/make_golden.py --reference /path/to/cosyvoice3-cpu
+    python tests/golden/make_golden.py --reference /path/to/cosyvoice3-cpu [--only sampling]
 """
 
 from __future__ import annotations
@@ -57,12 +64,70 @@ def hift_mel(seed: int, frames: int):
     return np.clip(rng.normal(-5.0, 2.0, size=(80, frames)), -11.5, 2.0).astype(np.float32)
 
 
+def sampler_logits(data, vocab: int = 6761):
+    """Seeded, peaked logits of one sampler step (shared with the tests)."""
+    x = (data.normal(size=vocab) * 3.0).astype(np.float32)
+    x[data.integers(0, 40, size=4)] += 6.0
+    return x
+
+
+SAMPLED_TRIALS = [(2.0, True), (3.0, True), (1.0, False), (2.5, True), (1.5, True)]
+
+
+def make_sampling(reference: str) -> None:
+    from cv3cpu import ops, quant
+    from cv3cpu.io.weights import WeightFile
+    from cv3cpu.models import llm as rl
+    out = {}
+    # q4 writer
+    w = (np.random.default_rng(8).normal(size=(37, 96)) * 0.05).astype(np.float32)
+    w[1, :32] = 0.0
+    q, sc, kp = quant.quantize_q4(w)
+    out["q4_w"], out["q4_q"], out["q4_scales"], out["q4_kp"] = w, q, sc, np.int64(kp)
+    # 200 sampler steps per mode: logits from data seed 5, generator seed 11, ignore_eos when i % 7 < 3
+    sts = 6561
+    ref = rl.CosyVoice3LM.__new__(rl.CosyVoice3LM)
+    ref.speech_token_size = sts
+    ref.stop_token_ids = set(range(sts, sts + 200))
+    for strict in (False, True):
+        cfg = rl.SamplingConfig(seed=11)
+        data = np.random.default_rng(5)
+        decoded = []
+        for i in range(200):
+            logp = ops.log_softmax(sampler_logits(data))
+            decoded.append(ref._sample(logp, decoded, cfg, i % 7 < 3, strict))
+        st = cfg.rng.bit_generator.state["state"]
+        out[f"sampler_{int(strict)}_tokens"] = np.array(decoded, np.int64)
+        out[f"sampler_{int(strict)}_state"] = np.array([str(st["state"]), str(st["inc"])])
+    # sampled generation on the small balanced model (text / speech from data seed 2)
+    syn = _pkg("synth").synthetic_weights("balanced", small=True, stages=("llm",))
+    path = os.path.join(tempfile.mkdtemp(), "lm.safetensors")
+    _pkg("weights").write_weights(path, dict(syn), syn.meta)
+    lm = rl.CosyVoice3LM(WeightFile(path))
+    eop = syn.meta["endofprompt_id"]
+    data = np.random.default_rng(2)
+    for trial, (lo, strict) in enumerate(SAMPLED_TRIALS):
+        text = data.integers(0, 2000, size=6 + 3 * trial).tolist()
+        speech = data.integers(0, 256, size=4).tolist()
+        cfg = rl.SamplingConfig(seed=30 + trial, max_token_text_ratio=4.0, min_token_text_ratio=lo)
+        toks = list(lm.generate(text, [eop], speech, sampling=cfg, strict_min_len=strict))
+        out[f"generate_{trial}_text"] = np.array(text, np.int64)
+        out[f"generate_{trial}_speech"] = np.array(speech, np.int64)
+        out[f"generate_{trial}_tokens"] = np.array(toks, np.int64)
+    np.savez_compressed(os.path.join(HERE, "sampling_small.npz"), **out)
+    print("wrote sampling_small.npz", sorted(out))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference checkout")
+    ap.add_argument("--only", choices=["sampling"], help="regenerate only this fixture")
     a = ap.parse_args()
     sys.path.insert(0, a.reference)
     sys.path.insert(0, os.path.join(a.reference, "tools"))
+    if a.only == "sampling":
+        make_sampling(a.reference)
+        return
     from cv3cpu.io.weights import WeightFile
     from cv3cpu.models.flow import Flow
     from cv3cpu.models.hift import HiFTGenerator
@@ -130,6 +195,7 @@ def main() -> None:
         f.close()
     np.savez_compressed(os.path.join(HERE, "stages_small.npz"), **out)
     print("wrote", sorted(out))
+    make_sampling(a.reference)
 
 
 if __name__ == "__main__":

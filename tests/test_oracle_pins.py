@@ -246,3 +246,49 @@ def test_oracle_sampled_generation_matches_reference(tmp_path, profile):
         assert rng.bit_generator.state == cfg.rng.bit_generator.state
         total += len(want)
     assert total >= 60
+
+
+# ---- the same pins from committed fixtures (tests/golden/sampling_small.npz, written by
+# ---- make_golden.py from the reference): they run without the reference checkout
+
+def _sampling_golden():
+    from conftest import GOLDEN
+    sys.path.insert(0, GOLDEN)
+    import make_golden
+    with np.load(os.path.join(GOLDEN, "sampling_small.npz")) as z:
+        return {k: z[k] for k in z.files}, make_golden
+
+
+def test_oracle_q4_matches_reference_golden():
+    g, _ = _sampling_golden()
+    q, s, kp = nx.quantize_q4(g["q4_w"])
+    assert np.array_equal(q, g["q4_q"]) and np.array_equal(s, g["q4_scales"]) and kp == int(g["q4_kp"])
+
+
+@pytest.mark.parametrize("strict", [False, True])
+def test_oracle_sampler_matches_reference_golden(strict):
+    g, mg = _sampling_golden()
+    rng = np.random.default_rng(11)
+    data = np.random.default_rng(5)
+    decoded = []
+    for i in range(200):
+        logp = nx.log_softmax(mg.sampler_logits(data))
+        decoded.append(nx.sample_token(logp, decoded, rng, 6561, i % 7 < 3, strict))
+    assert decoded == g[f"sampler_{int(strict)}_tokens"].tolist()
+    st = rng.bit_generator.state["state"]
+    assert [str(st["state"]), str(st["inc"])] == g[f"sampler_{int(strict)}_state"].tolist()
+
+
+def test_oracle_sampled_generation_matches_reference_golden():
+    g, mg = _sampling_golden()
+    syn = pkg("synth").synthetic_weights("balanced", small=True, stages=("llm",))
+    olm = st.SpeechLM(syn, syn.meta)
+    eop = syn.meta["endofprompt_id"]
+    total = 0
+    for trial, (lo, strict) in enumerate(mg.SAMPLED_TRIALS):
+        text, speech = g[f"generate_{trial}_text"].tolist(), g[f"generate_{trial}_speech"].tolist()
+        got = olm.generate_sampled(olm.prompt_embedding(text, [eop], speech), len(text),
+                                   np.random.default_rng(30 + trial), lo, 4.0, strict)
+        assert got == g[f"generate_{trial}_tokens"].tolist(), trial
+        total += len(got)
+    assert total >= 60
