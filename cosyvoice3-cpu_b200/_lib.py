@@ -50,6 +50,8 @@ SIGNATURES = {
     "cv3_interpolate_linear": [P, I64, I64, P, P, P, I64, P, P],
     "cv3_torch_rand": [U64, I64, I64, P, P],
     "cv3_torch_randn": [U64, I64, I64, P, P, P],
+    "cv3_torch_u32": [U64, I64, I64, P, P],
+    "cv3_torch_rand64": [U64, I64, I64, P, P],
     "cv3_rope_qkv_append": [P, I64, I64, P, P, P, P, I64, I64, I64, P, P, P, I64, P],
     "cv3_decode_attention": [P, P, P, P, I64, I64, I64, I64, I64, F, P, P],
     "cv3_decode_rope_attention": [P, I64, P, P, P, P, P, P, I64, I64, I64, I64, I64, F, P, P],

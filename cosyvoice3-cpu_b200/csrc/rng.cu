@@ -159,6 +159,25 @@ extern "C" int cv3_torch_rand(uint64_t seed, int64_t skip, int64_t n, float* out
   return stream_words(seed, skip, n, 0, out, cv3::as_stream(stream));
 }
 
+extern "C" int cv3_torch_u32(uint64_t seed, int64_t skip, int64_t n, uint32_t* out, void* stream) {
+  CV3_REQUIRE(n >= 0 && skip >= 0, CV3_ERR_VALUE, "torch_u32: negative count");
+  if (n == 0) return CV3_OK;
+  return stream_words(seed, skip, n, 1, out, cv3::as_stream(stream));
+}
+
+extern "C" int cv3_torch_rand64(uint64_t seed, int64_t skip, int64_t n, double* out, void* stream) {
+  CV3_REQUIRE(n >= 0 && skip >= 0, CV3_ERR_VALUE, "torch_rand64: negative count");
+  CV3_REQUIRE(((uintptr_t)out & 7) == 0, CV3_ERR_VALUE, "torch_rand64: output must be 8-byte aligned");
+  if (n == 0) return CV3_OK;
+  cudaStream_t st = cv3::as_stream(stream);
+  int rc = stream_words(seed, skip, n, 2, out, st);  // 2n words, then each pair -> one double in place
+  if (rc) return rc;
+  int64_t grid = (n + 255) / 256;
+  if (grid > 1024) grid = 1024;
+  pairs_to_f64_kernel<<<(unsigned)grid, 256, 0, st>>>(reinterpret_cast<uint32_t*>(out), n);
+  return cv3::check_launch("pairs_to_f64");
+}
+
 extern "C" int cv3_torch_randn(uint64_t seed, int64_t skip, int64_t n, float* out, void* scratch, void* stream) {
   CV3_REQUIRE(n >= 0 && skip >= 0, CV3_ERR_VALUE, "torch_randn: negative count");
   if (n == 0) return CV3_OK;

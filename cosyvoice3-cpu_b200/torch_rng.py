@@ -55,6 +55,22 @@ class TorchMT19937:
         self.seed = seed & 0xFFFFFFFF
         self.pos = 0
 
+    def next_u32(self, n: int, device: bool = False):
+        """The next ``n`` tempered 32-bit words (cv3cpu/torch_rng.py:71-86)."""
+        out = torch.empty(n, dtype=torch.int32, device="cuda")
+        if n:
+            call("cv3_torch_u32", self.seed, self.pos, n, D.ptr(out), D.stream())
+        self.pos += n
+        return out if device else out.cpu().numpy().view(np.uint32)
+
+    def random_float64(self, n: int, device: bool = False):
+        """``n`` double uniforms from word pairs, first word high (cv3cpu/torch_rng.py:93-102)."""
+        out = torch.empty(n, dtype=torch.float64, device="cuda")
+        if n:
+            call("cv3_torch_rand64", self.seed, self.pos, n, D.ptr(out), D.stream())
+        self.pos += 2 * n
+        return out if device else out.cpu().numpy()
+
     def random_float32(self, n: int, device: bool = False):
         out = D.empty((n,))
         if n:

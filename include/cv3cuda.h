@@ -256,6 +256,14 @@ int cv3_interpolate_linear(const float* x, int64_t rows, int64_t t, const int64_
  * stream (MT19937, low 24 bits); torch_rng.py:88-91 and :145-150. */
 int cv3_torch_rand(uint64_t seed, int64_t skip, int64_t n, float* out, void* stream);
 
+/* Raw tempered MT19937 words of torch's CPU generator seeded with `seed`, starting `skip`
+ * words into the stream: TorchMT19937.next_u32 (cv3cpu/torch_rng.py:71-86). */
+int cv3_torch_u32(uint64_t seed, int64_t skip, int64_t n, uint32_t* out, void* stream);
+
+/* n double uniforms from consecutive word pairs (first word high, 53 bits), starting `skip`
+ * words in: TorchMT19937.random_float64 (cv3cpu/torch_rng.py:93-102); consumes 2n words. */
+int cv3_torch_rand64(uint64_t seed, int64_t skip, int64_t n, double* out, void* stream);
+
 /* out[0..n) = torch.randn(n) drawn from torch.manual_seed(seed)'s generator
  * after `skip` 32-bit words were consumed (skip = 0: a fresh seed), bit-exact
  * with cv3cpu/torch_rng.py:117-142.  Consumes n (+16 when n % 16 != 0) words,

@@ -223,6 +223,20 @@ def test_rand_and_shared_generator_bit_exact():
     assert np.array_equal(g.random_float32(37), h.random_float32(37))
 
 
+@pytest.mark.parametrize("seed", [0, 1986])
+def test_generator_words_and_doubles_bit_exact(seed):
+    """TorchMT19937.next_u32 / random_float64 (cv3cpu/torch_rng.py:71-102), interleaved with
+    the other draws across a state regeneration: the same words, doubles and stream position."""
+    R = pkg("torch_rng")
+    g, h = R.TorchMT19937(seed), nx.MT19937(seed)
+    assert np.array_equal(g.next_u32(5), h.next_u32(5))
+    assert np.array_equal(g.random_float64(3), h.random_float64(3))
+    assert np.array_equal(g.rand((7,)), h.random_float32(7))
+    assert np.array_equal(g.next_u32(1300), h.next_u32(1300))        # crosses 624-word regenerations
+    assert np.array_equal(g.random_float64(700), h.random_float64(700))
+    assert np.array_equal(g.randn((20,)), nx.randn((20,), gen=h))
+
+
 @pytest.mark.parametrize("rows,dim,rpg", [(10400, 1024, 650), (37, 1024, 0), (300, 512, 100), (50, 80, 25)])
 def test_ln_modulate(rng, rows, dim, rpg):
     """cv3_ln_modulate (the DiT's AdaLN: layer_norm(h) * (1 + scale[g]) + shift[g], g = row //
