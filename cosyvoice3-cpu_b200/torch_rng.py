@@ -1,8 +1,8 @@
 """PyTorch's CPU random stream, generated on the GPU; the surface of
 ``cv3cpu/torch_rng.py`` (``randn``, ``rand``, ``TorchMT19937``).
 
-The arithmetic runs in ``libcv3cuda.so`` (``cv3_torch_rand`` /
-``cv3_torch_randn``) and equals the reference bit for bit.  Results come back
+The arithmetic runs in ``libcv3cuda.so`` (``cv3_torch_rand``, ``cv3_torch_randn``,
+``cv3_torch_u32``, ``cv3_torch_rand64``) and equals the reference bit for bit.  Results come back
 as NumPy arrays unless ``device=True`` is passed.
 """
 
