@@ -292,3 +292,43 @@ def test_oracle_sampled_generation_matches_reference_golden():
         assert got == g[f"generate_{trial}_tokens"].tolist(), trial
         total += len(got)
     assert total >= 60
+
+
+@pytest.mark.skipif(not have_reference(), reason="reference checkout not present")
+def test_oracle_q4_lm_matches_reference(tmp_path):
+    """The small LM with every body linear and the token table in q4 (the 'tiny' storage),
+    written with this package's writer and run by the reference (cv3cpu.quant q4 path,
+    quant.py:110-133 + 156-204) and by the oracle: log-probabilities within 1e-5 and the
+    same greedy tokens over 8 steps."""
+    sys.path.insert(0, REFERENCE)
+    from cv3cpu import ops as rops
+    from cv3cpu.io.weights import WeightFile as RefWF
+    from cv3cpu.models import llm as rl
+    Q, W = pkg("quant"), pkg("weights")
+    syn = pkg("synth").synthetic_weights("f32", small=True, stages=("llm",))
+    tensors = dict(syn)
+    for name, t in syn.items():
+        if name.startswith("llm.model.layers.") and name.endswith("proj.weight") or name == "llm.model.embed_tokens":
+            tensors[name] = Q.make_qtensor(t, kind="q4")
+    path = str(tmp_path / "tiny.safetensors")
+    W.write_weights(path, tensors, syn.meta)
+    ref = rl.CosyVoice3LM(RefWF(path))
+    Wt = W.TensorDict(tensors, syn.meta)
+    olm = st.SpeechLM(Wt, Wt.meta)
+    eop = syn.meta["endofprompt_id"]
+    text, speech = [eop] + list(range(30, 39)), [4, 5, 6]
+    x = np.concatenate([ref._speech_emb([ref.sos]), ref._text_emb(text), ref._speech_emb([ref.task_id]),
+                        ref._speech_emb(speech)], axis=0).astype(np.float32)
+    assert rel_err(olm.prompt_embedding(text, (), speech), x) < 1e-6
+    cache = ref.body.new_cache()
+    toks, logps = [], []
+    for _ in range(8):
+        h = ref.body.forward(x, cache)
+        logp = rops.log_softmax(ref._head(h[-1:]).astype(np.float32), axis=-1)[0]
+        top = int(np.argmax(logp[: ref.speech_token_size]))
+        toks.append(top)
+        logps.append(logp)
+        x = ref._speech_emb([top])
+    otoks, ologps = olm.generate_greedy(olm.prompt_embedding(text, (), speech), 8)
+    assert otoks == toks
+    assert rel_err(ologps, np.stack(logps)) < 1e-5
