@@ -270,8 +270,8 @@ def dominant_kernel_roofline(tts, peaks):
     return {"kernel": "DiT ff1 GEMM (M=%d, N=%d, K=%d, fp32 via 3xTF32)" % (M, blk.n, blk.k), "bound": "tensor",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
             "peak_source": "measured bf16 dense (MEASURED_PEAKS.json, burst)",
-            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this shape (ncu --set
-            # full of `bench.py --kernel ff1`, profiles/hot_kernels_ncu_full.md); algorithmic 144.6 MB
+            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this shape (the
+            # committed ncu --set full summary of `bench.py --kernel ff1`); algorithmic 144.6 MB
             "traffic": 59.5e6 + 43.0e6, "traffic_unit": "bytes per launch",
             "avg_launch_ms": ms,
             "tensor_pipe": {"tf32_tflops_issued": 3.0 * achieved, "tf32_peak_measured": tf32.value,

@@ -86,7 +86,6 @@ SIGNATURES = {
     "cv3_tc_tf32_peak": [P, P],
     "cv3_q8_decode_gemv": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
     "cv3_q8_decode_gemv_mma": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
-    "cv3_tc_gemm_cfg": [P, I64, P, I64, P, I64, I64, I64, I64, I32, P, P, I64, I64, I32, I32, P],
 }
 _RESTYPE = {"cv3_last_error": ctypes.c_char_p, "cv3_launch_count": ctypes.c_ulonglong}
 

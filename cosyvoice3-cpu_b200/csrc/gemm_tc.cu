@@ -610,7 +610,10 @@ __global__ void tf32_lo_kernel(const float* __restrict__ x, int64_t n, float* __
 
 }  // namespace
 
-extern "C" int cv3_tc_gemm_cfg(const float* a, int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc,
+// cv3_tc_gemm with an explicit accumulator layout: k_chunks (1, 2, 4) TMEM
+// accumulators each sum a contiguous K range; split_cross = 1 keeps the hi*lo +
+// lo*hi terms in their own accumulators (at most 4 in all).
+static int tc_gemm_layout(const float* a, int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc,
                                int64_t m, int64_t n, int64_t k, int mode, const float* bias, const float* gate,
                                int64_t rows_per_group, int64_t gate_stride, int k_chunks, int split_cross,
                                void* stream) {
@@ -648,8 +651,8 @@ extern "C" int cv3_tc_gemm(const float* a, int64_t lda, const float* b, int64_t 
   // error of K = 1024 / 2048 reductions at 1.7e-6 / 3.1e-6, where a single
   // accumulator gives 1.0e-5 / 1.7e-5 -- small addends lose bits when the
   // tensor core adds them into a large accumulator.  Same speed.
-  return cv3_tc_gemm_cfg(a, lda, b, ldb, c, ldc, m, n, k, mode, bias, gate, rows_per_group, gate_stride, 2, 1,
-                         stream);
+  return tc_gemm_layout(a, lda, b, ldb, c, ldc, m, n, k, mode, bias, gate, rows_per_group, gate_stride, 2, 1,
+                        stream);
 }
 
 extern "C" int cv3_tc_gemm_status(int* code) {

@@ -67,7 +67,9 @@ __global__ void istft_frames_kernel(const float* __restrict__ spec, int mode, in
     for (int kf = 0; kf < nbin; ++kf) {
       const float a = sb[(int64_t)kf * frames + f], c = sb[(int64_t)(nbin + kf) * frames + f];
       if (mode == 1) {
-        const float mag = fminf(expf(fminf(a, 80.0f)), 100.0f);
+        // np.minimum / np.clip propagate NaN (hift.py:206); fminf would drop it
+        const float e = expf(a > 80.0f ? 80.0f : a);
+        const float mag = e > 100.0f ? 100.0f : e;
         const float ph = sinf(c);
         re[kf] = mag * cosf(ph);
         im[kf] = mag * sinf(ph);
@@ -106,7 +108,7 @@ __global__ void istft_ola_kernel(const float* __restrict__ fr, int64_t frames, i
       env += win[j] * win[j];
     }
     float v = fabsf(env) > 1e-11f ? acc / env : acc;
-    v = fminf(fmaxf(v, -limit), limit);
+    v = v < -limit ? -limit : (v > limit ? limit : v);  // np.clip: NaN stays NaN
     yb[t] = v;
   }
 }
@@ -234,8 +236,9 @@ constexpr int kMaxDevices = 64;
 // per device with that device current (a host-side symbol is not a device
 // address, so it must never be passed to a kernel directly).  The lookup
 // happens inside the first cv3_istft_noalloc call on each device; make that
-// first call before any stream capture.
-int istft_scratch_address(float** out) {
+// first call before any stream capture (a first call on a capturing stream is
+// refused: the lookup may load the module, which a capture does not allow).
+int istft_scratch_address(cudaStream_t stream, float** out) {
   static std::mutex mu;
   static float* addr[kMaxDevices] = {};
   int dev = 0;
@@ -243,6 +246,11 @@ int istft_scratch_address(float** out) {
   CV3_REQUIRE(dev >= 0 && dev < kMaxDevices, CV3_ERR_UNSUPPORTED, "istft_noalloc: device index %d", dev);
   std::lock_guard<std::mutex> lk(mu);
   if (!addr[dev]) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    CV3_CUDA(cudaStreamIsCapturing(stream, &cap));
+    CV3_REQUIRE(cap == cudaStreamCaptureStatusNone, CV3_ERR_VALUE,
+                "istft_noalloc: the first call on device %d must come before any stream capture "
+                "(it looks up the frame buffer's device address)", dev);
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_istft_scratch);
     CV3_REQUIRE(e == cudaSuccess && p != nullptr, CV3_ERR_CUDA, "istft_noalloc: cudaGetSymbolAddress failed: %s",
@@ -264,7 +272,7 @@ extern "C" int cv3_istft_noalloc(const float* spec, int mode, int64_t batch, int
               "use cv3_istft with a caller-provided buffer",
               (long long)batch, (long long)frames, (long long)n_fft, (long long)kIstftScratchFloats);
   float* scratch = nullptr;
-  const int rc = istft_scratch_address(&scratch);
+  const int rc = istft_scratch_address(cv3::as_stream(stream), &scratch);
   if (rc) return rc;
   return cv3_istft(spec, mode, batch, frames, n_fft, hop, win, limit, offset, scratch, y, out_len, stream);
 }

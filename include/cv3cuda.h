@@ -236,7 +236,8 @@ int cv3_istft(const float* spec, int mode, int64_t batch, int64_t frames, int64_
  * every device that loads the library until exit and shared by all calls:
  * calls whose kernels may overlap on the GPU race and must be ordered by the
  * caller.  The first call on each device looks up the array's device address;
- * make that call before any stream capture. */
+ * make that call before any stream capture (a first call on a capturing stream
+ * returns CV3_ERR_VALUE and does nothing). */
 int cv3_istft_noalloc(const float* spec, int mode, int64_t batch, int64_t frames, int64_t n_fft, int64_t hop,
                       const float* win, float limit, int64_t offset, float* y, int64_t out_len, void* stream);
 
@@ -428,14 +429,6 @@ int cv3_reflect_left1(const float* x, int64_t rows, int64_t t, float* y, void* s
 int cv3_tc_gemm(const float* a, int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc, int64_t m,
                 int64_t n, int64_t k, int mode, const float* bias, const float* gate, int64_t rows_per_group,
                 int64_t gate_stride, void* stream);
-
-/* cv3_tc_gemm with an explicit accumulator layout: k_chunks (1, 2, 4)
- * TMEM accumulators each sum a contiguous K range, split_cross = 1 keeps the
- * hi*lo + lo*hi terms in their own accumulators; all are summed in fp32 in the
- * epilogue (at most 4 accumulators).  cv3_tc_gemm uses 2 and 1. */
-int cv3_tc_gemm_cfg(const float* a, int64_t lda, const float* b, int64_t ldb, float* c, int64_t ldc,
-                    int64_t m, int64_t n, int64_t k, int mode, const float* bias, const float* gate,
-                    int64_t rows_per_group, int64_t gate_stride, int k_chunks, int split_cross, void* stream);
 
 /* lo[i] = x[i] - tf32(x[i]) (x with its low 13 mantissa bits cleared): the
  * exact remainder the 3xTF32 products need.  Made once per weight matrix. */

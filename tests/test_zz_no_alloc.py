@@ -60,3 +60,39 @@ def test_noalloc_istft_rejects_sizes_beyond_its_buffer():
     rc = lib.cv3_istft_noalloc(None, 0, 2, 40000, 16, 4, None, ctypes.c_float(1.0), 8, y.data_ptr(), 1, None)
     assert rc == L.CV3_ERR_VALUE
     assert b"built-in" in lib.cv3_last_error()
+
+
+_CAPTURE_CHILD = r"""
+import sys
+sys.path.insert(0, sys.argv[1])
+import torch
+from conftest import pkg
+L = pkg("_lib")
+lib = L.load()
+y = torch.empty(64, device="cuda")
+s = torch.cuda.Stream()
+g = torch.cuda.CUDAGraph()
+with torch.cuda.stream(s):
+    g.capture_begin()
+    rc = lib.cv3_istft_noalloc(None, 0, 1, 4, 16, 4, None, 1.0, 8, y.data_ptr(), 12, s.cuda_stream)
+    msg = lib.cv3_last_error()
+    g.capture_end()
+print("RC", rc, msg.decode())
+"""
+
+
+def test_noalloc_first_call_inside_a_capture_is_refused(tmp_path):
+    """In a fresh process (nothing looked up yet) the first call, made on a capturing
+    stream, returns CV3_ERR_VALUE with a message instead of breaking the capture."""
+    import os
+    import subprocess
+    import sys
+    tests = os.path.dirname(os.path.abspath(__file__))
+    script = tmp_path / "capture_child.py"
+    script.write_text(_CAPTURE_CHILD)
+    env = dict(os.environ, PYTHONPATH=tests + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    out = subprocess.run([sys.executable, str(script), tests], capture_output=True, text=True, timeout=300, env=env)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = [ln for ln in out.stdout.splitlines() if ln.startswith("RC ")][-1]
+    assert line.split()[1] == str(pkg("_lib").CV3_ERR_VALUE), line
+    assert "before any stream capture" in line
