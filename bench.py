@@ -45,25 +45,10 @@ def pkg(name=""):
 
 
 def make_requests(seeds, meta):
-    """Config-4 inputs per seed s: text ids U[40, 80] with <|endofprompt|> in the
-    prompt text, a 192-d N(0,1) speaker vector, a 150-frame N(0,1) prompt mel and
-    75 prompt speech tokens."""
-    voice_cls = pkg("voice").VoicePack
-    req_cls = pkg("pipeline").Request
-    eop = int(meta.get("endofprompt_id", 151646))
-    vocab = int(meta["qwen2"]["vocab_size"])
-    sts = int(meta.get("speech_token_size", 6561))
-    out = []
-    for s in seeds:
-        rng = np.random.default_rng(s)
-        n = int(rng.integers(40, 81))
-        text = rng.integers(0, vocab, size=n).tolist()
-        prompt_text = rng.integers(0, vocab, size=8).tolist() + [eop]
-        voice = voice_cls(speech_token=rng.integers(0, sts, size=PROMPT_TOKENS),
-                          mel=rng.normal(size=(2 * PROMPT_TOKENS, 80)).astype(np.float32),
-                          embedding=rng.normal(size=192).astype(np.float32), name=f"seed{s}")
-        out.append(req_cls(text, prompt_text, voice))
-    return out
+    """Config-4 inputs per seed (``workloads.requests``): 40..80 text ids, a prompt text
+    ending in <|endofprompt|>, 75 prompt speech tokens, 150 prompt mel frames, a 192-d
+    speaker vector."""
+    return pkg("workloads").requests(seeds, meta)
 
 
 # ---------------------------------------------------------------------------
@@ -186,39 +171,74 @@ def cpu_sample(W, req, decode_steps: int = 4):
                               "hift_s": t_hift}
 
 
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def blas_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
         n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else (os.cpu_count() or 1)
+        return max(n) if n else host_threads()
     except Exception:
-        return os.cpu_count() or 1
+        return host_threads()
 
 
-CPU_SAMPLE_DESC = ("one config-4 utterance: LM prefill + 4 greedy steps (x250/4 extrapolated), one DiT "
-                   "forward at CFG batch 2 x 650 frames (x10 steps), full 500-frame vocoder (chunk 250)")
+def use_all_host_threads():
+    """BLAS on every host core, whatever OMP_NUM_THREADS the launcher set (torchrun sets 1)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        return threadpool_limits(limits=host_threads(), user_api="blas")
+    except Exception:
+        return None
+
+
+CPU_SAMPLE_DESC = ("one config-4 utterance, modelled from a timed sample: LM prefill + 4 greedy steps (the "
+                   "per-step time x 249), one DiT forward at CFG batch 2 x 650 frames (x 10 steps), the full "
+                   "500-frame vocoder (chunk 250)")
+
+
+def cpu_baseline_line(W, req):
+    _limits = use_all_host_threads()
+    t0 = time.perf_counter()
+    per_utt, sampled, parts = cpu_sample(W, req)
+    wall = time.perf_counter() - t0
+    return {"value": 1.0 / per_utt, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+            "sample": CPU_SAMPLE_DESC, "sample_wall_s": wall, "modelled_s_per_utterance": per_utt,
+            "parts_s": parts}
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference arm: the CPU implementation of the path (the oracle port of cv3cpu's
+    kernel layer and stages) on all host cores.  Each step times one bounded sample of a
+    config-4 utterance (``cpu_sample``); ``ms_per_step`` is that sample's wall time and
+    ``value`` the utterance rate the sample implies (see CPU_SAMPLE_DESC)."""
     if rank != 0:
         return
+    _limits = use_all_host_threads()
     synth = pkg("synth")
     W = synth.synthetic_weights("balanced")
     reqs = make_requests(range(UTTS), W.meta)
-    times = []
+    per, walls = [], []
     for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
         per_utt, sampled, parts = cpu_sample(W, reqs[i % len(reqs)])
+        wall = time.perf_counter() - t0
         if i >= args.warmup:
-            times.append(per_utt)
-    per_utt = float(np.mean(times))
+            per.append(per_utt)
+            walls.append(wall)
+    per_utt = float(np.mean(per))
     value = 1.0 / per_utt
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_utt * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": float(np.mean(walls)) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(args),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port",
-                         "sample": CPU_SAMPLE_DESC},
+                         "sample": CPU_SAMPLE_DESC, "modelled_s_per_utterance": per_utt},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -235,6 +255,109 @@ def config_dict(args):
 # ---------------------------------------------------------------------------
 # the device arm
 # ---------------------------------------------------------------------------
+
+LM_WEIGHT_BYTES = 375_255_804      # int8 payload + fp16 scales of the 24 layers and the speech head
+KV_BYTES_PER_POS = 24_576          # k and v, 24 layers x 2 kv heads x 64 x 4 B, per cached position
+DIT_GEMM_PARAMS = 184_549_376      # per-token weights of the 22 blocks' q, k, v, out, ff1, ff2
+HIFT_GFLOP = 336.9                 # vocoder convolutions per 10 s (500 mel frames)
+
+
+def _timed(fn, reps: int):
+    """Mean milliseconds of ``fn()`` over ``reps`` runs, CUDA events on the current stream."""
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def measure_config1(tts, meta, peaks, reps: int = 3):
+    """Config 1: the balanced LM at batch 1, a 64-id prompt, 250 greedy tokens.  The decode
+    step's HBM roofline counts its algorithmic bytes: every int8 weight and scale once, plus the
+    KV cache read (24,576 B per cached position, mean length over the 249 steps) and one
+    position appended."""
+    import torch
+    wl = pkg("workloads")
+    lm = tts.llm
+    ids = wl.lm_prompt_ids(0, vocab=int(meta["qwen2"]["vocab_size"]))
+    x0 = pkg("_dev").dev(lm._text_emb(ids))
+    steps = wl.LM_STEPS
+    eng = lm.engine(1, 512, steps)
+    eng.run([x0], steps)                                   # builds and captures the step graph
+    t_prefill = _timed(lambda: eng.prefill([x0]), reps)
+    t_total = _timed(lambda: eng.run([x0], steps), reps)
+    step_ms = (t_total - t_prefill) / (steps - 1)
+    mean_len = wl.LM_PROMPT_IDS + steps / 2.0
+    bytes_step = LM_WEIGHT_BYTES + KV_BYTES_PER_POS * (mean_len + 1)
+    gbs = bytes_step / (step_ms * 1e-3) / 1e9
+    hbm = peaks.get("hbm_gbs")
+    return {"workload": "config1: batch-1 greedy decode, 64-id prompt + 250 tokens, balanced int8 LM",
+            "lm_tok_s": steps / (t_total * 1e-3), "ms_total": t_total, "prefill_ms": t_prefill,
+            "decode_step_us": step_ms * 1e3,
+            "roofline": {"kernel": "one graph-replayed decode step (24 layers + head)", "bound": "hbm",
+                         "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm if hbm else None,
+                         "algorithmic_bytes_per_step": bytes_step,
+                         "peak_source": "measured copy bandwidth (MEASURED_PEAKS.json)"}}
+
+
+def measure_config2(Wf, peaks, reps: int = 3):
+    """Config 2: the f32 DiT flow, 250 tokens -> 500 frames, 10 CFG Euler steps at batch 2.
+    Tensor work per solve = 10 x (GEMMs 2 * 184.5 M * B * N + attention 4 * N^2 * 1024 * B * 22)."""
+    import numpy as np
+    wl = pkg("workloads")
+    flow = pkg("models.flow").Flow(pkg("weights").DeviceWeights(Wf))
+    tokens, emb = wl.flow_inputs(0)
+    mu, spk, cond, _ = flow.conditioning(tokens, np.zeros(0, np.int64), np.zeros((0, 80), np.float32), emb)
+    run = lambda: flow.solve_batch([mu], [spk], [cond])  # noqa: E731
+    run()
+    ms = _timed(run, reps)
+    B, N, steps = 2, 2 * len(tokens), int(flow.n_timesteps)
+    flops = steps * (2.0 * DIT_GEMM_PARAMS * B * N + 4.0 * N * N * 1024 * B * 22)
+    tf = flops / (ms * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops")
+    return {"workload": "config2: f32 DiT flow, 250 tokens -> 500 frames, 10 CFG Euler steps (batch 2)",
+            "flow_s": ms * 1e-3, "dit_forward_ms": ms / steps,
+            "roofline": {"kernel": "the whole solve (GEMM + attention FLOPs, fp32 via 3xTF32)", "bound": "tensor",
+                         "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak if peak else None,
+                         "flops_per_solve": flops, "peak_source": "measured bf16 dense (MEASURED_PEAKS.json)"}}
+
+
+def measure_config3(Wf, peaks, reps: int = 3):
+    """Config 3: the f32 vocoder, 500 mel frames -> 240,000 samples (336.9 GFLOP of convolution)."""
+    wl = pkg("workloads")
+    hift = pkg("models.hift").HiFTGenerator(pkg("weights").DeviceWeights(Wf))
+    mel = pkg("_dev").dev(wl.vocoder_mel(1))[None]
+    run = lambda: hift.inference_batch(mel)  # noqa: E731
+    run()
+    ms = _timed(run, reps)
+    tf = HIFT_GFLOP * 1e9 / (ms * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops")
+    return {"workload": "config3: f32 vocoder, 500 frames -> 240000 samples", "vocoder_s": ms * 1e-3,
+            "roofline": {"kernel": "the whole vocoder (convolution FLOPs)", "bound": "tensor", "achieved": tf,
+                         "peak": peak, "unit": "TFLOP/s", "frac": tf / peak if peak else None,
+                         "peak_source": "measured bf16 dense (MEASURED_PEAKS.json)"}}
+
+
+def measure_strong(tts, meta, rank: int, world: int, reps: int, barrier):
+    """Config 4 as a fixed job: 8 utterances in all, split over the ``world`` GPUs
+    (1 per GPU at 8); the job's time is the slowest rank's."""
+    per = max(UTTS // world, 1)
+    mine = range(rank * per, min((rank + 1) * per, UTTS))
+    prepared = tts.prepare(make_requests(mine, meta)) if len(mine) else None
+    if prepared:
+        tts.run_prepared(prepared, TOKENS)
+    barrier()
+    ms = _timed(lambda: tts.run_prepared(prepared, TOKENS), reps) if prepared else 0.0
+    barrier()
+    ms = max_over_ranks(ms, world)
+    return {"workload": "config4 strong scaling: 8 utterances in all over %d GPU(s)" % world,
+            "utterances": UTTS, "ms": ms, "value": UTTS / (ms * 1e-3), "unit": UNIT}
+
+
 
 def dominant_kernel_roofline(tts, peaks):
     """Time the DiT FF GEMM at the bench shape in isolation (the largest kernel of
@@ -329,11 +452,21 @@ def run_cuda(args, rank: int, world: int) -> None:
 
     peaks = json.load(open(PEAKS)) if os.path.exists(PEAKS) else {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
     roof = dominant_kernel_roofline(tts, peaks) if rank == 0 else None
+
+    # -- the other configurations' numbers (every rank measures; rank 0 reports) -----------
+    stages = {}
+    if not args.no_stages:
+        stages["config1_lm"] = measure_config1(tts, W.meta, peaks)
+        Wf = synth.synthetic_weights("f32", stages=("flow", "hift"))
+        stages["config2_flow"] = measure_config2(Wf, peaks)
+        stages["config3_vocoder"] = measure_config3(Wf, peaks)
+        del Wf
+        stages["flow_hift_rtf"] = (stages["config2_flow"]["flow_s"] + stages["config3_vocoder"]["vocoder_s"]) / 10.0
+        if world > 1:
+            stages["config4_strong"] = measure_strong(tts, W.meta, rank, world, args.steps, barrier)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        per_utt, sampled, parts = cpu_sample(W, reqs[0])
-        cpu = {"value": 1.0 / per_utt, "unit": UNIT, "cores": blas_threads(), "kind": "port",
-               "sample": CPU_SAMPLE_DESC, "sampled_cpu_s": sampled, "parts_s": parts}
+        cpu = cpu_baseline_line(W, reqs[0])
     if rank == 0:
         total_utts = UTTS * world
         print(json.dumps({
@@ -347,7 +480,7 @@ def run_cuda(args, rank: int, world: int) -> None:
             "clocks": clk.summary(),
             "roofline": roof,
             "cpu_baseline": cpu,
-            "stage_note": "LM tok/s = %.0f per GPU (all stages in one step)" % (UTTS * TOKENS / (ms * 1e-3)),
+            "stages": stages,
         }), flush=True)
 
 
@@ -492,6 +625,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-stages", action="store_true", help="skip the config 1-3 stage numbers")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -174,7 +174,10 @@ class DeviceWeights:
 
     ``f32(name)`` returns a float32 CUDA tensor (f16 tables widened exactly),
     ``q8(name)`` the device :class:`QTensor`, ``raw(name)`` the tensor in its
-    stored dtype.  :meth:`evict` frees every cached tensor under a prefix.
+    stored dtype.  :meth:`evict` frees every cached tensor under a prefix and
+    hands the freed device memory back to the driver (the device counterpart of
+    the reference's ``WeightFile.evict``, cv3cpu/io/weights.py:182-205, which
+    returns a stage's mmap pages to the OS).
     """
 
     def __init__(self, host, device: str = "cuda"):
@@ -228,14 +231,33 @@ class DeviceWeights:
         """Cache an arbitrary derived device tensor (fused or pre-split weights)."""
         return self._put(("derived",) + tuple(key if isinstance(key, tuple) else (key,)), fn)
 
-    def evict(self, prefix: str = "") -> int:
+    def evict(self, prefix: str = "", release: bool = True) -> int:
+        """Drop every cached tensor whose name starts with ``prefix``; returns their bytes.
+
+        With ``release`` the caching allocator's now-unused blocks go back to the driver
+        (``cudaFree``), so another process or stage can use the HBM; callers must have
+        dropped their own references to the stage (models, engines, CUDA graphs) first,
+        as ``CosyVoice3CUDA._drop`` does."""
         freed = 0
         for k in list(self._cache):
             name = k[1] if len(k) > 1 and isinstance(k[1], str) else ""
             if name.startswith(prefix):
                 v = self._cache.pop(k)
                 freed += _nbytes(v)
+        if release:
+            release_device_memory()
         return freed
+
+
+def release_device_memory() -> None:
+    """Return the allocator's unused cached blocks to the driver (after collecting
+    reference cycles that may still hold device tensors or graph memory pools)."""
+    import gc
+    import torch
+    gc.collect()
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
 
 
 def _nbytes(v) -> int:

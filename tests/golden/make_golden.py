@@ -20,10 +20,19 @@ Run in a checkout that has the reference project importable (its root on
   ``generate`` on the small ``balanced`` model.  The seeds that regenerate the
   inputs are stored beside the outputs.
 
+* ``full_size.npz`` (``--only full``) -- the reference's model classes at the
+  benchmark geometry, on the seeded inputs of this package's ``workloads``
+  module: config 1 (balanced Qwen2-0.5B LM, 64-id prompt, 250 greedy steps:
+  ids, the top-two log-prob margin of every step and four log-prob rows),
+  config 2 (f32 DiT: one forward at batch 2 x 500 frames and the 10-step CFG
+  flow solve of 250 tokens), config 3 (f32 vocoder, 500 frames: F0 and the
+  waveform the default chunked inference returns) and one config-4 utterance
+  through all three balanced stages (ids, mel, waveform).
+
 It also asserts that the synthetic generator reproduces the reference's own
 random-model generator tensor for tensor.
 
-    python tests/golden/make_golden.py --reference /path/to/cosyvoice3-cpu [--only sampling]
+    python tests/golden/make_golden.py --reference /path/to/cosyvoice3-cpu [--only sampling|full]
 """
 
 from __future__ import annotations
@@ -118,15 +127,111 @@ def make_sampling(reference: str) -> None:
     print("wrote sampling_small.npz", sorted(out))
 
 
+LOGP_STEPS = (0, 1, 125, 249)
+
+
+def greedy_reference(lm, x, steps: int):
+    """The build's greedy decode written with the reference's pieces: body forward,
+    ``_head``, ``log_softmax`` (llm.py:112-114), first argmax over the speech tokens,
+    next input ``_speech_emb([top])``.  Returns ids, per-step top-two margins and the
+    log-prob rows of LOGP_STEPS."""
+    from cv3cpu import ops
+    cache = lm.body.new_cache()
+    ids, margins, rows = [], [], []
+    for i in range(steps):
+        h = lm.body.forward(x, cache)
+        logp = ops.log_softmax(lm._head(h[-1:]).astype(np.float32), axis=-1)[0]
+        sp = logp[: lm.speech_token_size]
+        top = int(np.argmax(sp))
+        two = np.partition(sp, -2)[-2:]
+        ids.append(top)
+        margins.append(float(two[1] - two[0]))
+        if i in LOGP_STEPS:
+            rows.append(logp.copy())
+        x = lm._speech_emb([top])
+        if i % 50 == 0:
+            print(f"  greedy step {i}", flush=True)
+    return np.array(ids, np.int64), np.array(margins, np.float32), np.stack(rows).astype(np.float32)
+
+
+def make_full(reference: str) -> None:
+    """Full-geometry fixtures (see the module docstring).  About 10 minutes of CPU."""
+    from cv3cpu.io.weights import WeightFile
+    from cv3cpu.models.dit import DiT
+    from cv3cpu.models.flow import Flow
+    from cv3cpu.models.hift import HiFTGenerator
+    from cv3cpu.models.llm import CosyVoice3LM
+    synth, weights, wl = _pkg("synth"), _pkg("weights"), _pkg("workloads")
+    tmp = tempfile.mkdtemp()
+    out = {}
+
+    def written(profile, stages):
+        W = synth.synthetic_weights(profile, stages=stages)
+        path = os.path.join(tmp, f"{profile}_{'_'.join(stages)}.safetensors")
+        weights.write_weights(path, dict(W), W.meta)
+        return WeightFile(path), W.meta
+
+    # ---- config 1: balanced LM, 64-id prompt, 250 greedy steps
+    f, meta = written("balanced", ("llm",))
+    lm = CosyVoice3LM(f, "llm.")
+    ids = wl.lm_prompt_ids(0, vocab=meta["qwen2"]["vocab_size"])
+    x0 = lm._text_emb(ids).astype(np.float32)
+    print("config 1: LM", flush=True)
+    toks, margins, rows = greedy_reference(lm, x0, wl.LM_STEPS)
+    out["c1_tokens"], out["c1_margin"], out["c1_logp"] = toks, margins, rows
+    out["c1_logp_steps"] = np.array(LOGP_STEPS, np.int64)
+    f.close()
+
+    # ---- config 2: f32 DiT forward at (2, 80, 500), and the 10-step flow solve
+    f, meta = written("f32", ("flow",))
+    print("config 2: DiT forward + flow solve", flush=True)
+    dit = DiT(f, "flow.decoder.estimator.")
+    out["c2_dit_out"] = dit.forward(*wl.dit_inputs(2)).astype(np.float32)
+    tokens, emb = wl.flow_inputs(0)
+    out["c2_mel"] = Flow(f, "flow.").inference(tokens, np.zeros(0, np.int64), np.zeros((0, 80), np.float32),
+                                               emb).astype(np.float32)
+    f.close()
+
+    # ---- config 3: f32 vocoder, 500 frames
+    f, meta = written("f32", ("hift",))
+    print("config 3: vocoder", flush=True)
+    hift = HiFTGenerator(f, "hift.")
+    mel = wl.vocoder_mel(1)
+    out["c3_f0"] = hift.f0_predict(mel)
+    out["c3_wav"] = hift.inference(mel).astype(np.float32)
+    f.close()
+
+    # ---- config 4: one utterance (seed 0) through the three balanced stages
+    f, meta = written("balanced", ("llm", "flow", "hift"))
+    print("config 4: chain", flush=True)
+    req = wl.requests([0], meta)[0]
+    v = req.voice
+    lm = CosyVoice3LM(f, "llm.")
+    text = list(req.prompt_ids) + list(req.text_ids)
+    x0 = np.concatenate([lm._speech_emb([lm.sos]), lm._text_emb(text), lm._speech_emb([lm.task_id]),
+                         lm._speech_emb(v.speech_token.tolist())], axis=0).astype(np.float32)
+    toks, margins, _ = greedy_reference(lm, x0, wl.LM_STEPS)
+    out["c4_tokens"], out["c4_margin"] = toks, margins
+    mel = Flow(f, "flow.").inference(toks, v.speech_token, v.mel, v.embedding).astype(np.float32)
+    out["c4_mel"] = mel
+    out["c4_wav"] = HiFTGenerator(f, "hift.").inference(mel).astype(np.float32)
+    f.close()
+    np.savez_compressed(os.path.join(HERE, "full_size.npz"), **out)
+    print("wrote full_size.npz", {k: v.shape for k, v in out.items()})
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference checkout")
-    ap.add_argument("--only", choices=["sampling"], help="regenerate only this fixture")
+    ap.add_argument("--only", choices=["sampling", "full"], help="regenerate only this fixture")
     a = ap.parse_args()
     sys.path.insert(0, a.reference)
     sys.path.insert(0, os.path.join(a.reference, "tools"))
     if a.only == "sampling":
         make_sampling(a.reference)
+        return
+    if a.only == "full":
+        make_full(a.reference)
         return
     from cv3cpu.io.weights import WeightFile
     from cv3cpu.models.flow import Flow

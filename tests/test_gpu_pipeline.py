@@ -54,3 +54,25 @@ def test_sampled_synthesis_runs_and_matches_reference_contract(small_weights):
     assert out.sample_rate == 24000 and out.audio.dtype == np.float32
     assert len(out.audio) == 2 * 480 * len(out.speech_tokens[0])
     assert np.isfinite(out.audio).all() and np.abs(out.audio).max() <= 0.99 + 1e-6
+
+
+def test_release_stages_gives_the_llm_hbm_back():
+    """With ``release_stages`` the LM stage's weights, engines and graphs are dropped after
+    the LM runs and the memory goes back to the driver (free HBM rises by at least the
+    int8 LM's 375 MB of layer weights) -- the device form of the reference's eviction
+    (cv3cpu/pipeline.py:81-86, io/weights.py:182-205)."""
+    import torch
+    W = pkg("synth").synthetic_weights("balanced", stages=("llm",))
+    tts = pkg("pipeline").CosyVoice3CUDA(W, release_stages=True)
+    lm = tts.llm
+    eop = W.meta["endofprompt_id"]
+    prompt = lm.prompt_embedding([eop, 11, 12, 13], (), [1, 2, 3])
+    toks = lm.generate_greedy([prompt], 4).cpu()
+    assert toks.shape == (1, 4)
+    del lm, prompt
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    tts._drop("llm")
+    free_after = torch.cuda.mem_get_info()[0]
+    assert tts._llm is None
+    assert free_after - free_before > 375e6, (free_before, free_after)

@@ -332,3 +332,45 @@ def test_oracle_q4_lm_matches_reference(tmp_path):
     otoks, ologps = olm.generate_greedy(olm.prompt_embedding(text, (), speech), 8)
     assert otoks == toks
     assert rel_err(ologps, np.stack(logps)) < 1e-5
+
+
+# ---------------------------------------------------------------------------
+# full benchmark geometry (tests/golden/full_size.npz, made by the reference)
+# ---------------------------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def full_golden():
+    with np.load(os.path.join(os.path.dirname(__file__), "golden", "full_size.npz")) as z:
+        return {k: z[k] for k in z.files}
+
+
+def test_oracle_vocoder_matches_reference_at_500_frames(full_golden):
+    """Config 3 (f32 vocoder, 500 frames): the oracle's F0 and waveform against the
+    reference's, at the full geometry."""
+    wl = pkg("workloads")
+    W = pkg("synth").synthetic_weights("f32", stages=("hift",))
+    h = st.HiFT(W, W.meta)
+    mel = wl.vocoder_mel(1)
+    f0 = h.f0_predict(mel)
+    assert rel_err(f0, full_golden["c3_f0"]) < 1e-6
+    assert np.array_equal(f0 > 10.0, full_golden["c3_f0"] > 10.0)
+    assert rel_err(h.inference(mel), full_golden["c3_wav"]) < 1e-6
+
+
+@needs_ref
+def test_reference_f0_condnet_runs_in_float32():
+    """The reference's F0 predictor hands float64 arrays to ``ops.conv1d``
+    (cv3cpu/models/hift.py:56-72), but ``conv1d`` casts input and weight to float32
+    and returns float32 (cv3cpu/ops.py:183, :186, :198), and ``elu`` keeps float32:
+    the five condnet convolutions run in float32 and only the classifier dot product
+    is float64.  The device path reproduces exactly that."""
+    sys.path.insert(0, REFERENCE)
+    from cv3cpu import ops as rops
+    rng = np.random.default_rng(0)
+    x = rng.normal(size=(80, 40))                       # float64, as f0_predict passes it
+    w = rng.normal(size=(512, 80, 4))
+    b = rng.normal(size=512)
+    y = rops.conv1d(x, w, b, pad=(0, 3))
+    assert y.dtype == np.float32 and rops.elu(y).dtype == np.float32
+    y32 = rops.conv1d(x.astype(np.float32), w.astype(np.float32), b.astype(np.float32), pad=(0, 3))
+    assert np.array_equal(y, y32)
