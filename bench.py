@@ -582,11 +582,30 @@ def run_lm_step(args) -> None:
         eng.max_len.fill_(250)
         eng.done.zero_()
         eng.count.zero_()
+    elif args.persistent:
+        # the persistent kernel: 200 steps in one launch after a 20-step warm-up launch
+        eng = lm.engine(B, 512, 260)
+        eng.run(prompts, 21, persistent=True)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        eng.steps_persistent(200)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / 200 * 1e3
+        import ctypes
+        code = ctypes.c_int(0)
+        pkg("_lib").load().cv3_decode_status(ctypes.byref(code))
+        print(json.dumps({"lm_decode_step_us": round(us, 1), "batch": B, "persistent": True, "status": code.value,
+                          "weight_bytes_per_step": 375255804,
+                          "weight_stream_gbs": round(375255804 / (us * 1e-6) / 1e9, 1)}), flush=True)
+        return
     else:
         eng = lm.engine(B, 512, 260)
         eng.run(prompts, 2, use_graph=True)
-    for _ in range(20):
-        eng.step()
+    if not args.persistent:
+        for _ in range(20):
+            eng.step()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = 200
@@ -615,6 +634,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--lm-step", type=int, default=0, metavar="B",
                     help="time the LM decode step alone at batch B (1..8)")
+    ap.add_argument("--persistent", action="store_true",
+                    help="with --lm-step: the persistent decode kernel (every step in one launch)")
     ap.add_argument("--sampled", action="store_true",
                     help="with --lm-step: the sampled step (device sampler) and the host-sampler path")
     ap.add_argument("--slice", action="store_true", help="profiling slice (see run_slice)")

@@ -82,12 +82,14 @@ SIGNATURES = {
     "cv3_set_dependent_launch": [I32],
     "cv3_conv_tc_last_path": [P],
     "cv3_decode_steps": [P, P],
+    "cv3_decode_sync_words": [I64, I64],
     "cv3_decode_status": [P],
     "cv3_tc_tf32_peak": [P, P],
     "cv3_q8_decode_gemv": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
     "cv3_q8_decode_gemv_mma": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
 }
-_RESTYPE = {"cv3_last_error": ctypes.c_char_p, "cv3_launch_count": ctypes.c_ulonglong}
+_RESTYPE = {"cv3_last_error": ctypes.c_char_p, "cv3_launch_count": ctypes.c_ulonglong,
+            "cv3_decode_sync_words": ctypes.c_int64}
 
 _lib: Optional[ctypes.CDLL] = None
 
@@ -134,11 +136,12 @@ class DecodeParams(ctypes.Structure):
         ("head_q", ctypes.c_void_p), ("head_s", ctypes.c_void_p),
         ("vocab", ctypes.c_int32), ("select", ctypes.c_int32),
         ("emb", ctypes.c_void_p), ("emb_scales", ctypes.c_void_p), ("emb_rows", ctypes.c_int32),
-        ("h", ctypes.c_void_p), ("q", ctypes.c_void_p), ("attn", ctypes.c_void_p), ("act", ctypes.c_void_p),
+        ("h", ctypes.c_void_p), ("h1", ctypes.c_void_p), ("qkv", ctypes.c_void_p), ("attn_part", ctypes.c_void_p),
+        ("part", ctypes.c_void_p), ("act", ctypes.c_void_p),
         ("logits", ctypes.c_void_p), ("logp", ctypes.c_void_p),
         ("pos", ctypes.c_void_p), ("lens", ctypes.c_void_p), ("next_ids", ctypes.c_void_p),
         ("history", ctypes.c_void_p), ("hist_stride", ctypes.c_int64),
-        ("step", ctypes.c_void_p), ("barrier", ctypes.c_void_p),
+        ("step", ctypes.c_void_p), ("sync", ctypes.c_void_p), ("sync_words", ctypes.c_int64),
         ("steps", ctypes.c_int32),
     ]
 

@@ -316,13 +316,15 @@ class DecodeEngine:
 
     # -- persistent decode (cv3_decode_steps): every step of a run in one launch ----------
     def _persistent_setup(self):
-        """Parameter block of the persistent decode kernel, or None where it does not apply
-        (a layer or the head not q8, head dim != 64, more than 8 sequences)."""
+        """Parameter block and scratch of the persistent decode kernel, or None where it does
+        not apply (a layer or the head not q8, head dim != 64, more than 8 sequences,
+        hidden > 1216 or intermediate > 4864)."""
         from .. import _lib
         c, B = self.c, self.B
-        hid = c.hidden_size
+        hid, inter = c.hidden_size, c.intermediate_size
         e = self.emb
-        if (B > 8 or c.head_dim != 64 or hid != c.num_attention_heads * 64 or hid % 64 or c.intermediate_size % 64
+        if (B > 8 or c.head_dim != 64 or hid != c.num_attention_heads * 64 or hid % 64 or hid > 1216
+                or inter % 64 or inter > 4864 or c.num_attention_heads // c.num_key_value_heads > 8
                 or self.fast_head is None or any(F is None for F in self.fast)
                 or any(g.kp != g.k for F in self.fast for g in F) or self.fast_head.kp != hid
                 or (isinstance(e, QTensor) and (e.kind != "q8" or e.padded_k != hid))):
@@ -335,28 +337,49 @@ class DecodeEngine:
                      kc, vc]
         if any(v is None for v in ptrs):
             return None
+        keep = []
         table = torch.tensor(ptrs, dtype=torch.int64, device="cuda")
-        barrier = torch.zeros(max(256, pk_sm_count()), dtype=torch.int32, device="cuda")
+        keep.append(table)
+        # the head in whole 16-row tiles (zero rows past the vocabulary; never read back)
+        if self.fast_head.bias is not None:
+            return None
+        hw = self.fast_head._keep[0]
+        hq, hs = hw.q, hw.scales
+        pad = (-self.vocab) % 16
+        if pad:
+            hq = torch.cat([hq, torch.zeros((pad, hq.shape[1]), dtype=hq.dtype, device="cuda")]).contiguous()
+            hs = torch.cat([hs, torch.zeros((pad, hs.shape[1]), dtype=hs.dtype, device="cuda")]).contiguous()
+        keep += [hq, hs]
+        H, Hk = c.num_attention_heads, c.num_key_value_heads
+        nch = -(-self.cap // 64)
+        parts = -(-(inter // 64) // 19)
+        h1 = D.empty((B, hid))
+        attn_part = D.empty((B, H, nch, 66))
+        part = D.empty((hid // 16, parts, 16, 8))
+        lib = _lib.load()
+        words = int(lib.cv3_decode_sync_words(len(self.fast), hid))
+        sync = torch.zeros(words, dtype=torch.int32, device="cuda")
+        keep += [h1, attn_part, part, sync]
         P = _lib.DecodeParams()
         P.layers = table.data_ptr()
         P.n_layers, P.batch, P.hidden = len(self.fast), B, hid
-        P.heads, P.kv_heads, P.head_dim, P.inter = (c.num_attention_heads, c.num_key_value_heads, c.head_dim,
-                                                    c.intermediate_size)
+        P.heads, P.kv_heads, P.head_dim, P.inter = H, Hk, c.head_dim, inter
         P.eps, P.scale, P.cap = c.rms_norm_eps, self.scale, self.cap
         P.cos_table, P.sin_table = self.cos.data_ptr(), self.sin.data_ptr()
         P.final_norm = self.m.norm_w().data_ptr()
-        P.head_q, P.head_s = self.fast_head.q, self.fast_head.scales
+        P.head_q, P.head_s = hq.data_ptr(), hs.data_ptr()
         P.vocab, P.select = self.vocab, self.select
         if isinstance(e, QTensor):
             P.emb, P.emb_scales, P.emb_rows = e.q.data_ptr(), e.scales.data_ptr(), int(e.shape[0])
         else:
             P.emb, P.emb_scales, P.emb_rows = e.data_ptr(), None, int(e.shape[0])
-        P.h, P.q, P.attn, P.act = self.h.data_ptr(), self.q.data_ptr(), self.a.data_ptr(), self.act.data_ptr()
+        P.h, P.h1, P.qkv, P.attn_part = self.h.data_ptr(), h1.data_ptr(), self.qkv.data_ptr(), attn_part.data_ptr()
+        P.part, P.act = part.data_ptr(), self.act.data_ptr()
         P.logits, P.logp = self.logits.data_ptr(), None
         P.pos, P.lens, P.next_ids = self.pos.data_ptr(), self.lens.data_ptr(), self.next_ids.data_ptr()
         P.history, P.hist_stride = self.history.data_ptr(), self.max_steps
-        P.step, P.barrier = self.step_no.data_ptr(), barrier.data_ptr()
-        return {"params": P, "keep": [table, barrier]}
+        P.step, P.sync, P.sync_words = self.step_no.data_ptr(), sync.data_ptr(), words
+        return {"params": P, "keep": keep, "sync": sync}
 
     @property
     def persistent_ok(self) -> bool:
@@ -365,13 +388,17 @@ class DecodeEngine:
     def steps_persistent(self, n: int, stream=None):
         """``n`` greedy decode steps in one cooperative launch (cv3_decode_steps)."""
         import ctypes
-        from .. import _lib
         if self._mk is None:
             raise RuntimeError("persistent decode needs q8 layers and head, head dim 64, <= 8 sequences")
         P = self._mk["params"]
         P.logp = self.logp.data_ptr() if self.keep_logp else None
         P.steps = int(n)
         call("cv3_decode_steps", ctypes.byref(P), stream if stream is not None else D.stream())
+
+    def reset_persistent(self):
+        """Zero the completion counters (after a reported wait failure left them uneven)."""
+        if self._mk is not None:
+            self._mk["sync"].zero_()
 
     def launches(self, st):
         """One decode step for every sequence (all pointers fixed -> graph-capturable)."""
@@ -521,8 +548,8 @@ class DecodeEngine:
     def run(self, prompts, n_tokens: int, use_graph: bool = True, persistent: bool = False):
         """Greedy-decode ``n_tokens`` tokens for every prompt; returns ``[B][n_tokens]`` ids (device).
         The steps after the prefill run as one CUDA graph per step (``use_graph``), eager launches,
-        or -- ``persistent`` -- one cooperative launch for all of them (same tokens; measured slower
-        on B200 than the graph: 1.30 vs 0.90 ms per step at batch 1, 2.78 vs 1.50 at batch 8)."""
+        or -- ``persistent`` -- one cooperative launch for all of them (cv3_decode_steps: the
+        weights stream into shared memory ahead of the layer chain)."""
         if n_tokens > self.max_steps:
             raise ValueError("n_tokens exceeds max_steps")
         if max(int(np.shape(x)[0]) for x in prompts) + n_tokens > self.cap:

@@ -487,19 +487,24 @@ int cv3_conv_tc_set_window(int enable);
 int cv3_conv_tc_last_path(int* path);
 
 /* Persistent greedy decode of the Qwen2 speech LM (cv3cpu/models/qwen2.py:
- * 139-179 per token, llm.py:114 head + greedy pick): `steps` tokens for a
- * batch of <= 8 sequences in ONE cooperative launch -- every layer's q8 GEMVs
- * (RMSNorm fused in, bias, RoPE + KV append, GQA attention, residuals,
- * SwiGLU), the final norm, the head, log_softmax / first argmax over the
- * speech tokens, bookkeeping (pos, lens, history[b][*step], *step) and the
- * embedding of the chosen token as the next input -- separated by grid-wide
- * barriers (bounded waits; CV3_ERR_CUDA and cv3_decode_status on expiry).
+ * 139-179 per token, llm.py:114 head + greedy pick; replaces the per-token
+ * chain of qwen2.py's ops.* calls): `steps` tokens for a batch of <= 8
+ * sequences in ONE cooperative launch (one CTA per SM) -- every layer's q8
+ * linears (RMSNorm fused in, bias, RoPE + KV append, GQA attention,
+ * residuals, SwiGLU), the final norm, the head, log_softmax / first argmax
+ * over the speech tokens, bookkeeping (pos, lens, history[b][*step], *step)
+ * and the embedding of the chosen token as the next input.  Each CTA streams
+ * its fixed share of every weight matrix into shared memory ahead of the
+ * dependency chain; phases hand over through completion counters in `sync`
+ * (bounded waits; cv3_decode_status reports an expired wait).
  * State on entry is what cv3_head_select + cv3_embedding leave: h holds the
  * embedded current token at position pos[b], lens[b] = pos[b] + 1.
  * Every matrix is q8 ([rows][kp] int8 + fp16 scales [rows][kp/64]) with
- * kp == its K; gate/up rows interleaved (2i gate_i, 2i+1 up_i); qkv rows =
- * q heads, k heads, v heads.  The per-layer table has CV3_DECODE_LAYER_FIELDS
- * device pointers per layer, in this order: */
+ * kp == its K (hidden <= 1216, inter <= 4864, multiples of 64); gate/up rows
+ * interleaved (2i gate_i, 2i+1 up_i); qkv rows = q heads, k heads, v heads;
+ * the head padded to a multiple of 16 rows (rows >= vocab are not read back).
+ * The per-layer table has CV3_DECODE_LAYER_FIELDS device pointers per layer,
+ * in this order: */
 #define CV3_DECODE_LAYER_FIELDS 13
 /*  0 qkv q8, 1 qkv scales, 2 qkv bias (fp32), 3 input RMSNorm weight,
  *  4 o q8, 5 o scales, 6 gate|up q8, 7 gate|up scales, 8 post-attention RMSNorm
@@ -513,15 +518,17 @@ typedef struct cv3_decode_params {
   const float* cos_table; /* [cap][head_dim] */
   const float* sin_table;
   const float* final_norm;
-  const int8_t* head_q;   /* [vocab][hidden] q8 */
+  const int8_t* head_q;   /* [ceil16(vocab)][hidden] q8 */
   const uint16_t* head_s;
   int32_t vocab, select;  /* head rows; tokens eligible for the greedy pick */
   const void* emb;        /* next-token embedding table: fp32 [rows][hidden] or q8 */
   const uint16_t* emb_scales; /* NULL for fp32 */
   int32_t emb_rows;
   float* h;               /* [batch][hidden] residual stream / input */
-  float* q;               /* [batch][heads][head_dim] scratch */
-  float* attn;            /* [batch][heads*head_dim] scratch */
+  float* h1;              /* [batch][hidden] scratch: residual after attention */
+  float* qkv;             /* [batch][(heads + 2 kv_heads) * head_dim] scratch */
+  float* attn_part;       /* [batch][heads][ceil(cap / 64)][head_dim + 2] scratch */
+  float* part;            /* [hidden / 16][ceil(inter / 1216)][16][8] scratch */
   float* act;             /* [batch][inter] scratch */
   float* logits;          /* [batch][vocab] */
   float* logp;            /* [batch][vocab] log-probs of the last step, or NULL */
@@ -531,14 +538,20 @@ typedef struct cv3_decode_params {
   int64_t* history;       /* [batch][hist_stride] */
   int64_t hist_stride;
   int32_t* step;          /* history column of the next token */
-  uint32_t* barrier;      /* one word per SM (>= 256 words; the call zeroes them on its stream) */
+  uint32_t* sync;         /* cv3_decode_sync_words() words, zeroed once before the first call */
+  int64_t sync_words;
   int32_t steps;
 } cv3_decode_params;
 
 int cv3_decode_steps(const cv3_decode_params* params, void* stream);
 
+/* Words of the `sync` buffer cv3_decode_steps needs for this geometry. */
+int64_t cv3_decode_sync_words(int64_t n_layers, int64_t hidden);
+
 /* Error word of the persistent decode kernel (see cv3_tc_gemm_status): 1 a
- * barrier wait expired, 2 a position past the cache, 3 a step past the history. */
+ * completion wait expired, 2 a position past the cache, 3 a step past the
+ * history, 4/5 a weight-ring wait expired, 6 a key/value prefetch wait expired,
+ * 7 a token outside the embedding table. */
 int cv3_decode_status(int* code);
 
 /* Measures the dense kind::tf32 tensor-pipe rate of this GPU (every SM

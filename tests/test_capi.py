@@ -15,7 +15,7 @@ HEADER = os.path.join(REPO, "include", "cv3cuda.h")
 
 def declared():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*|unsigned long long)\s+(cv3_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\*|unsigned long long)\s+(cv3_\w+)\s*\(", text, flags=re.M)))
 
 
 @pytest.fixture(scope="module")

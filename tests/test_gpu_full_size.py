@@ -127,3 +127,22 @@ def test_config4_one_utterance_through_three_balanced_stages(full):
     assert rel_err(mel, full["c4_mel"]) < INT8_TOL
     assert wav.shape == (1, 240000)
     assert rel_err(wav[0], full["c4_wav"]) < INT8_TOL
+
+
+def test_config1_persistent_decode_250_ids(full):
+    """The persistent decode kernel (every step in one launch, weights streamed into shared
+    memory ahead of the layer chain) on config 1: the reference's 250 greedy ids, and the
+    last step's log-probabilities within 1e-4."""
+    import ctypes
+    wl = pkg("workloads")
+    W = pkg("synth").synthetic_weights("balanced", stages=("llm",))
+    lm = pkg("models.llm").CosyVoice3LM(_device(W))
+    x0 = lm._text_emb(wl.lm_prompt_ids(0, vocab=W.meta["qwen2"]["vocab_size"]))
+    eng = lm.engine(1, 512, wl.LM_STEPS)
+    assert eng.persistent_ok
+    eng.keep_logp = True
+    ids = eng.run([x0], wl.LM_STEPS, persistent=True).cpu().numpy()[0]
+    code = ctypes.c_int(-1)
+    assert pkg("_lib").load().cv3_decode_status(ctypes.byref(code)) == 0 and code.value == 0
+    assert ids.tolist() == full["c1_tokens"].tolist(), _first_flip(ids, full["c1_tokens"], full["c1_margin"])
+    assert rel_err(eng.logp[0].cpu().numpy(), full["c1_logp"][-1]) < INT8_TOL
