@@ -342,6 +342,52 @@ def measure_config3(Wf, peaks, reps: int = 3):
                          "peak_source": "measured bf16 dense (MEASURED_PEAKS.json)"}}
 
 
+SWEEP_UTTS, SWEEP_BATCH, SWEEP_TOKENS = 256, 32, 750
+
+
+def sweep_requests(seeds, meta):
+    """Config-5 utterances: 120..240 text ids, the config-4 prompt form, 750 tokens each."""
+    return pkg("workloads").requests(seeds, meta, text_len=(120, 240))
+
+
+def measure_config5(tts, meta, rank: int, world: int, barrier, full: bool = False):
+    """Config 5, the 256 x 30 s throughput sweep: batches of 32 utterances per GPU through the
+    LM (750 greedy tokens each), the CFG flow (batch 2 x 32, N = 2 * (75 + 750) = 1650) and
+    the vocoder (1500 frames -> 720,000 samples).  ``full``: every batch of this rank's share
+    of the 256 utterances is run and timed; otherwise one batch per GPU is timed and the
+    sweep time is that batch's time x the batches per GPU (all batches have the same shape)."""
+    import torch
+    per_gpu = SWEEP_UTTS // world
+    batches = max(per_gpu // SWEEP_BATCH, 1)
+    seeds = list(range(rank * per_gpu, (rank + 1) * per_gpu))
+    groups = [seeds[i:i + SWEEP_BATCH] for i in range(0, len(seeds), SWEEP_BATCH)]
+    first = tts.prepare(sweep_requests(groups[0], meta))
+    tts.run_prepared(first, SWEEP_TOKENS)           # warm-up: engines, graphs, workspaces
+    barrier()
+    if full:
+        prepared = [first] + [tts.prepare(sweep_requests(g, meta)) for g in groups[1:]]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for pr in prepared:
+            tts.run_prepared(pr, SWEEP_TOKENS)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        timed = len(prepared)
+    else:
+        ms = _timed(lambda: tts.run_prepared(first, SWEEP_TOKENS), 1)
+        timed = 1
+    barrier()
+    ms = max_over_ranks(ms, world)
+    sweep_s = ms * 1e-3 * (1 if full else batches)
+    return {"workload": "config5 sweep: 256 utterances x 750 tokens (30 s), batches of 32 per GPU over %d GPU(s); "
+                        "LM batch 32, CFG flow 2 x 32 at 1650 frames, vocoder 1500 frames" % world,
+            "batches_per_gpu": batches, "batches_timed": timed, "batch_ms": ms / timed, "sweep_s": sweep_s,
+            "value": SWEEP_UTTS / sweep_s, "unit": "30s-utterances/s",
+            "lm_tok_s": SWEEP_UTTS * SWEEP_TOKENS / sweep_s, "extrapolated": not full}
+
+
 def measure_strong(tts, meta, rank: int, world: int, reps: int, barrier):
     """Config 4 as a fixed job: 8 utterances in all, split over the ``world`` GPUs
     (1 per GPU at 8); the job's time is the slowest rank's."""
@@ -464,6 +510,7 @@ def run_cuda(args, rank: int, world: int) -> None:
         stages["flow_hift_rtf"] = (stages["config2_flow"]["flow_s"] + stages["config3_vocoder"]["vocoder_s"]) / 10.0
         if world > 1:
             stages["config4_strong"] = measure_strong(tts, W.meta, rank, world, args.steps, barrier)
+        stages["config5_sweep"] = measure_config5(tts, W.meta, rank, world, barrier)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_line(W, reqs[0])
@@ -482,6 +529,21 @@ def run_cuda(args, rank: int, world: int) -> None:
             "cpu_baseline": cpu,
             "stages": stages,
         }), flush=True)
+
+
+def run_sweep(args, rank: int, world: int) -> None:
+    """``--sweep``: the whole config-5 sweep, one JSON line (rank 0)."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    W = pkg("synth").synthetic_weights("balanced")
+    tts = pkg("pipeline").CosyVoice3CUDA(W)
+    barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        r = measure_config5(tts, W.meta, rank, world, barrier, full=True)
+    if rank == 0:
+        r.update({"n_gpus": world, "clocks": clk.summary(), "dtype": "f32", "data": "synthetic"})
+        print(json.dumps(r), flush=True)
 
 
 def run_slice(args) -> None:
@@ -559,6 +621,57 @@ def run_kernel(args) -> None:
     print("kernel %s: 5 launches done" % args.kernel, flush=True)
 
 
+def trace_persistent(eng, B):
+    """One 12-step persistent launch with step 8 traced (%globaltimer per CTA and phase):
+    per phase kind (A qkv, B attention, C out-proj, D gate/up, E down, F head, G select),
+    the mean over layers of the critical-path time (last CTA done minus the previous phase's
+    last CTA done), the hand-over latency (first CTA past its wait minus the previous phase's
+    last signal), the mean per-CTA work time and ring-slot wait."""
+    import numpy as np
+    import torch
+    L = eng.c.num_hidden_layers
+    nph = 5 * L + 2
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    tb = torch.zeros((G, nph, 6), dtype=torch.int64, device="cuda")
+    P = eng._mk["params"]
+    P.trace, P.trace_step = tb.data_ptr(), 8
+    eng.steps_persistent(12)
+    torch.cuda.synchronize()
+    P.trace = None
+    t = tb.cpu().numpy().astype(np.float64)
+    names = ["A qkv", "B attention", "C out", "D gate/up", "E down"]
+    out = {}
+    done_prev = None
+    rows = {}
+    for ph in range(nph):
+        kind = names[ph % 5] if ph < 5 * L else ("F head" if ph == nph - 2 else "G select")
+        act = t[:, ph, 2] > 0
+        if not act.any():
+            continue
+        done = t[act, ph, 2].max()
+        started = t[act, ph, 1].min()
+        r = rows.setdefault(kind, {"critical_us": [], "handover_us": [], "work_us": [], "ring_wait_us": [],
+                                   "stage_us": [], "items_us": [], "signal_us": [], "ctas": int(act.sum())})
+        if done_prev is not None:
+            r["critical_us"].append((done - done_prev) / 1e3)
+            r["handover_us"].append((started - done_prev) / 1e3)
+        r["work_us"].append(float(np.mean(t[act, ph, 2] - t[act, ph, 1])) / 1e3)
+        r["ring_wait_us"].append(float(np.mean(t[act, ph, 3])) / 1e3)
+        st = act & (t[:, ph, 4] > 0)
+        if st.any():
+            r["stage_us"].append(float(np.mean(t[st, ph, 4] - t[st, ph, 1])) / 1e3)
+            r["items_us"].append(float(np.mean(t[st, ph, 5] - t[st, ph, 4])) / 1e3)
+        it = act & (t[:, ph, 5] > 0)
+        if it.any():
+            r["signal_us"].append(float(np.mean(t[it, ph, 2] - t[it, ph, 5])) / 1e3)
+        done_prev = done
+    for k, r in rows.items():
+        out[k] = {kk: (round(float(np.mean(v)), 3) if isinstance(v, list) and v else v) for kk, v in r.items()}
+    first = t[:, 0, 0][t[:, 0, 0] > 0].min() if (t[:, 0, 0] > 0).any() else 0
+    last = t[:, nph - 1, 2].max()
+    return {"trace_batch": B, "step_us": round((last - first) / 1e3, 1), "phases": out}
+
+
 def run_lm_step(args) -> None:
     """Time the LM's graph-replayed decode step alone (full-size balanced LM, ``--lm-step B``
     sequences with 130-165-row prompts, caches of 512 positions; 20 warm-up steps, then 200
@@ -587,6 +700,9 @@ def run_lm_step(args) -> None:
         eng = lm.engine(B, 512, 260)
         eng.run(prompts, 21, persistent=True)
         torch.cuda.synchronize()
+        if args.trace:
+            print(json.dumps(trace_persistent(eng, B)), flush=True)
+            return
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         eng.steps_persistent(200)
@@ -636,6 +752,8 @@ def main():
                     help="time the LM decode step alone at batch B (1..8)")
     ap.add_argument("--persistent", action="store_true",
                     help="with --lm-step: the persistent decode kernel (every step in one launch)")
+    ap.add_argument("--trace", action="store_true",
+                    help="with --lm-step B --persistent: per-phase timestamps of one step")
     ap.add_argument("--sampled", action="store_true",
                     help="with --lm-step: the sampled step (device sampler) and the host-sampler path")
     ap.add_argument("--slice", action="store_true", help="profiling slice (see run_slice)")
@@ -646,7 +764,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-stages", action="store_true", help="skip the config 1-3 stage numbers")
+    ap.add_argument("--no-stages", action="store_true", help="skip the config 1-3 and 5 stage numbers")
+    ap.add_argument("--sweep", action="store_true",
+                    help="config 5 alone: all 256 utterances, sharded over the ranks, every batch timed")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -664,6 +784,8 @@ def main():
             run_slice(args)
         elif args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.sweep:
+            run_sweep(args, rank, world)
         else:
             run_cuda(args, rank, world)
     finally:

@@ -137,12 +137,12 @@ class DecodeParams(ctypes.Structure):
         ("vocab", ctypes.c_int32), ("select", ctypes.c_int32),
         ("emb", ctypes.c_void_p), ("emb_scales", ctypes.c_void_p), ("emb_rows", ctypes.c_int32),
         ("h", ctypes.c_void_p), ("h1", ctypes.c_void_p), ("qkv", ctypes.c_void_p), ("attn_part", ctypes.c_void_p),
-        ("part", ctypes.c_void_p), ("act", ctypes.c_void_p),
+        ("attn", ctypes.c_void_p), ("part", ctypes.c_void_p), ("part_floats", ctypes.c_int64), ("act", ctypes.c_void_p),
         ("logits", ctypes.c_void_p), ("logp", ctypes.c_void_p),
         ("pos", ctypes.c_void_p), ("lens", ctypes.c_void_p), ("next_ids", ctypes.c_void_p),
         ("history", ctypes.c_void_p), ("hist_stride", ctypes.c_int64),
         ("step", ctypes.c_void_p), ("sync", ctypes.c_void_p), ("sync_words", ctypes.c_int64),
-        ("steps", ctypes.c_int32),
+        ("steps", ctypes.c_int32), ("trace_step", ctypes.c_int32), ("trace", ctypes.c_void_p),
     ]
 
 

@@ -24,6 +24,7 @@ torch = D.torch
 
 SPEECH_TOKEN_SIZE = 6561
 SAMPLER_MAX_TOP_K = 32  # cv3_sample_select's largest top_k (larger ones use the host sampler)
+MAX_DECODE_BATCH = 8    # sequences one decode engine advances together
 ENDOFPROMPT_ID = 151646
 
 
@@ -216,9 +217,17 @@ class CosyVoice3LM:
 
         Returns the ``[B, n_tokens]`` device tensor of token ids.  The decode steps run as one
         CUDA graph per step (``use_graph``), eager launches, or one persistent cooperative
-        launch (``persistent``, where the model allows it).
+        launch (``persistent``, where the model allows it).  More than ``MAX_DECODE_BATCH``
+        sequences run as consecutive groups of at most that many (each sequence's tokens do
+        not depend on the others in its batch).
         """
         B = len(prompts)
+        if B > MAX_DECODE_BATCH:
+            groups = [prompts[i:i + MAX_DECODE_BATCH] for i in range(0, B, MAX_DECODE_BATCH)]
+            need = max(int(np.shape(p)[0]) for p in prompts) + n_tokens
+            cap = cap or max(256, -(-need // 256) * 256)
+            return torch.cat([self.generate_greedy(g, n_tokens, cap, use_graph, keep_logp, persistent)
+                              for g in groups], 0)
         need = max(int(np.shape(p)[0]) for p in prompts) + n_tokens
         cap = cap or max(256, -(-need // 256) * 256)
         eng = self.engine(B, cap, max(n_tokens, 1))

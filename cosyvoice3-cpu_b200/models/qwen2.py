@@ -324,6 +324,7 @@ class DecodeEngine:
         hid, inter = c.hidden_size, c.intermediate_size
         e = self.emb
         if (B > 8 or c.head_dim != 64 or hid != c.num_attention_heads * 64 or hid % 64 or hid > 1216
+                or self.cap > 1536
                 or inter % 64 or inter > 4864 or c.num_attention_heads // c.num_key_value_heads > 8
                 or self.fast_head is None or any(F is None for F in self.fast)
                 or any(g.kp != g.k for F in self.fast for g in F) or self.fast_head.kp != hid
@@ -355,7 +356,8 @@ class DecodeEngine:
         parts = -(-(inter // 64) // 19)
         h1 = D.empty((B, hid))
         attn_part = D.empty((B, H, nch, 66))
-        part = D.empty((hid // 16, parts, 16, 8))
+        ntf = -(-self.vocab // 16)
+        part = D.empty((max((hid // 16) * parts * 16 * 8, 8 * ntf * 4),))
         lib = _lib.load()
         words = int(lib.cv3_decode_sync_words(len(self.fast), hid))
         sync = torch.zeros(words, dtype=torch.int32, device="cuda")
@@ -374,7 +376,8 @@ class DecodeEngine:
         else:
             P.emb, P.emb_scales, P.emb_rows = e.data_ptr(), None, int(e.shape[0])
         P.h, P.h1, P.qkv, P.attn_part = self.h.data_ptr(), h1.data_ptr(), self.qkv.data_ptr(), attn_part.data_ptr()
-        P.part, P.act = part.data_ptr(), self.act.data_ptr()
+        P.part, P.part_floats, P.act = part.data_ptr(), int(part.numel()), self.act.data_ptr()
+        P.attn = self.a.data_ptr()
         P.logits, P.logp = self.logits.data_ptr(), None
         P.pos, P.lens, P.next_ids = self.pos.data_ptr(), self.lens.data_ptr(), self.next_ids.data_ptr()
         P.history, P.hist_stride = self.history.data_ptr(), self.max_steps

@@ -527,8 +527,10 @@ typedef struct cv3_decode_params {
   float* h;               /* [batch][hidden] residual stream / input */
   float* h1;              /* [batch][hidden] scratch: residual after attention */
   float* qkv;             /* [batch][(heads + 2 kv_heads) * head_dim] scratch */
-  float* attn_part;       /* [batch][heads][ceil(cap / 64)][head_dim + 2] scratch */
-  float* part;            /* [hidden / 16][ceil(inter / 1216)][16][8] scratch */
+  float* attn_part;       /* [batch][heads][ceil(cap / 64)][head_dim + 2] scratch (cap <= 1536) */
+  float* attn;            /* [batch][heads * head_dim] scratch */
+  float* part;            /* scratch: max([hidden/16][ceil(inter/1216)][16][8], [8][ceil(vocab/16)][4]) floats */
+  int64_t part_floats;
   float* act;             /* [batch][inter] scratch */
   float* logits;          /* [batch][vocab] */
   float* logp;            /* [batch][vocab] log-probs of the last step, or NULL */
@@ -541,6 +543,8 @@ typedef struct cv3_decode_params {
   uint32_t* sync;         /* cv3_decode_sync_words() words, zeroed once before the first call */
   int64_t sync_words;
   int32_t steps;
+  int32_t trace_step;     /* with trace: the step (of this launch) to record */
+  uint64_t* trace;        /* NULL, or [SMs][5 n_layers + 2][6] per-phase timestamps (see decode_stream.cu) */
 } cv3_decode_params;
 
 int cv3_decode_steps(const cv3_decode_params* params, void* stream);
