@@ -406,14 +406,16 @@ def measure_strong(tts, meta, rank: int, world: int, reps: int, barrier):
 
 
 def dominant_kernel_roofline(tts, peaks):
-    """Time the DiT FF GEMM at the bench shape in isolation (the largest kernel of
-    the step) with CUDA events on its launching stream; achieved = 2*M*N*K / time."""
+    """Time the DiT FF1 GEMM at the bench shape in isolation (the largest kernel of the
+    step) with CUDA events on its launching stream; achieved = 2*M*N*K / time.  In the
+    balanced profile it is cv3_tc_gemm_q8 (int8 weights as stored, activations as two fp16
+    parts: two fp16 MMAs per fp32 product)."""
     import torch
-    L = pkg("_lib")
     dit = tts.flow.estimator
     dit.prepare()
     M = 2 * UTTS * 2 * (PROMPT_TOKENS + TOKENS)
     blk = dit.blocks[0].ff1
+    q8 = type(blk).__name__ == "LinQ8"
     x = torch.randn(M, blk.k, device="cuda")
     y = torch.empty(M, blk.n, device="cuda")
     st = torch.cuda.current_stream()
@@ -431,21 +433,18 @@ def dominant_kernel_roofline(tts, peaks):
     flops = 2.0 * M * blk.n * blk.k
     achieved = flops / (ms * 1e-3) / 1e12
     peak = peaks.get("bf16_tflops")
-    # 3xTF32: every fp32 product is three tf32 MMA products on the tensor pipe; its own
-    # measured dense tf32 rate is the ceiling of that pipe
-    import ctypes
-    tf32 = ctypes.c_double(0.0)
-    L.call("cv3_tc_tf32_peak", ctypes.byref(tf32), st.cuda_stream)
-    return {"kernel": "DiT ff1 GEMM (M=%d, N=%d, K=%d, fp32 via 3xTF32)" % (M, blk.n, blk.k), "bound": "tensor",
+    name = ("DiT ff1 GEMM (M=%d, N=%d, K=%d), int8 weights x fp32 activations as 2 fp16 parts (cv3_tc_gemm_q8)"
+            if q8 else "DiT ff1 GEMM (M=%d, N=%d, K=%d, fp32 via 3xTF32)") % (M, blk.n, blk.k)
+    return {"kernel": name, "bound": "tensor",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
             "peak_source": "measured bf16 dense (MEASURED_PEAKS.json, burst)",
-            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this shape (the
-            # committed ncu --set full summary of `bench.py --kernel ff1`); algorithmic 144.6 MB
-            "traffic": 59.5e6 + 43.0e6, "traffic_unit": "bytes per launch",
             "avg_launch_ms": ms,
-            "tensor_pipe": {"tf32_tflops_issued": 3.0 * achieved, "tf32_peak_measured": tf32.value,
-                            "frac_of_measured": 3.0 * achieved / tf32.value if tf32.value else None,
-                            "peak_source": "cv3_tc_tf32_peak (this run)"}}
+            "tensor_pipe": {"fp16_tflops_issued": (2.0 if q8 else 6.0) * achieved,
+                            "frac_of_peak": (2.0 if q8 else 6.0) * achieved / peak if peak else None,
+                            "note": "fp16/bf16-rate products issued per fp32 product: 2 (two fp16 parts of A "
+                                    "against the exact fp16 weights)" if q8 else
+                                    "3 tf32 products per fp32 product at half the bf16 rate"},
+            "traffic": None, "traffic_unit": "bytes per launch"}
 
 
 def run_cuda(args, rank: int, world: int) -> None:
@@ -595,6 +594,13 @@ def run_kernel(args) -> None:
             torch.empty(M, N, device="cuda")
         lin = common.Lin(b)
         fn = lambda: lin.tc(a.data_ptr(), M, c.data_ptr(), 0, stream=st)
+    elif args.kernel == "ff1q8":
+        M, N, K = 2 * UTTS * 2 * (PROMPT_TOKENS + TOKENS), 2048, 1024
+        quant = pkg("quant")
+        w = (np.random.default_rng(0).normal(size=(N, K)) * 0.02).astype(np.float32)
+        lin = common.LinQ8(quant.make_qtensor(w).to_device())
+        a, c = torch.randn(M, K, device="cuda"), torch.empty(M, N, device="cuda")
+        fn = lambda: lin(a.data_ptr(), M, c.data_ptr(), stream=st)
     elif args.kernel == "attention":
         B, H, N, D = 2 * UTTS, 16, 2 * (PROMPT_TOKENS + TOKENS), 64
         qkv, o = torch.randn(B, N, 3 * H * D, device="cuda"), torch.empty(B, N, H * D, device="cuda")
@@ -757,7 +763,7 @@ def main():
     ap.add_argument("--sampled", action="store_true",
                     help="with --lm-step: the sampled step (device sampler) and the host-sampler path")
     ap.add_argument("--slice", action="store_true", help="profiling slice (see run_slice)")
-    ap.add_argument("--kernel", choices=["ff1", "attention", "conv", "gemv"],
+    ap.add_argument("--kernel", choices=["ff1", "ff1q8", "attention", "conv", "gemv"],
                     help="run one hot kernel alone at its bench shape (for ncu captures)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)

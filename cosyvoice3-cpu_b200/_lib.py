@@ -81,6 +81,9 @@ SIGNATURES = {
     "cv3_conv_tc_set_window": [I32],
     "cv3_set_dependent_launch": [I32],
     "cv3_conv_tc_last_path": [P],
+    "cv3_tc_gemm_q8": [P, I64, P, P, P, I64, I64, I64, I64, I32, P, P, I64, I64, P],
+    "cv3_q8_gemm_prepare": [P, P, I64, I64, P, P, P],
+    "cv3_tc_gemm_q8_status": [P],
     "cv3_decode_steps": [P, P],
     "cv3_decode_sync_words": [I64, I64],
     "cv3_decode_status": [P],

@@ -84,6 +84,45 @@ class Lin:
              self.bias, gate, rows_per_group, gate_stride, s)
 
 
+class LinQ8:
+    """A q8 linear on the tensor cores with the int8 weights as stored (``cv3_tc_gemm_q8``):
+    the payload as exact fp16 and the scales transposed, made once; fewer than
+    TC_MIN_ROWS rows of x take the q8 GEMV instead."""
+
+    __slots__ = ("q", "n", "k", "w16", "st", "bias", "_keep")
+
+    def __init__(self, w: QTensor, bias=None, stream=None):
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("LinQ8: weights must be prepared before stream capture")
+        self.n, self.k = int(w.shape[0]), int(w.shape[1])
+        if w.kind != "q8" or w.padded_k != self.k or self.k % 64 or self.n % 128:
+            raise ValueError("LinQ8 needs a q8 matrix with K a multiple of 64 and N of 128")
+        self.q = Lin(w, bias)
+        self.w16 = torch.empty((self.n, self.k), dtype=torch.float16, device="cuda")
+        self.st = D.empty((self.k // 64, self.n))
+        call("cv3_q8_gemm_prepare", w.q.data_ptr(), w.scales.data_ptr(), self.n, self.k, self.w16.data_ptr(),
+             self.st.data_ptr(), stream if stream is not None else D.stream())
+        self.bias = bias.data_ptr() if bias is not None else None
+        self._keep = [w, bias]
+
+    def __call__(self, x: int, m: int, y: int, residual: int = None, ldx: int = None, ldy: int = None,
+                 stream=None):
+        ldx = self.k if ldx is None else ldx
+        ldy = self.n if ldy is None else ldy
+        if m < TC_MIN_ROWS or ldx % 4 or x % 16:
+            return self.q(x, m, y, residual=residual, ldx=ldx, ldy=ldy, stream=stream)
+        if residual is not None and residual != y:
+            raise ValueError("tensor-core linear adds the residual in place (residual must alias y)")
+        self.tc(x, m, y, 3 if residual is not None else 0, ldx=ldx, ldy=ldy, stream=stream)
+
+    def tc(self, x: int, m: int, y: int, mode: int, gate: int = None, rows_per_group: int = 0,
+           gate_stride: int = 0, stream=None, ldx: int = None, ldy: int = None):
+        """Fused epilogue as Lin.tc: 0 bias, 1 GELU-tanh, 2 gated residual into y, 3 residual into y."""
+        s = stream if stream is not None else D.stream()
+        call("cv3_tc_gemm_q8", x, self.k if ldx is None else ldx, self.w16.data_ptr(), self.st.data_ptr(), y,
+             self.n if ldy is None else ldy, m, self.n, self.k, mode, self.bias, gate, rows_per_group, gate_stride, s)
+
+
 class ConvTC:
     """A conv1d weight in the tensor-core layout (``cv3_conv_weight_tc``): Wt[C_out][ci_pad/32][k][32]
     plus the tf32 remainder when the weight is not exactly tf32 (fp16-stored weights are)."""

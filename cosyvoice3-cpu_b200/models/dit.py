@@ -21,7 +21,7 @@ import numpy as np
 from .. import _dev as D
 from .._lib import call
 from ..quant import QTensor
-from ._common import TC_MIN_ROWS, Lin, cat_rows, f32_of, ConvTC
+from ._common import TC_MIN_ROWS, ConvTC, Lin, LinQ8, cat_rows, f32_of
 
 torch = D.torch
 
@@ -81,6 +81,15 @@ class DiT:
         self._ready = False
         self._rope = {}
         self._ws = {}
+        # q8 block matrices (balanced profile) run cv3_tc_gemm_q8 on the stored int8 weights;
+        # False dequantises them to fp32 for the 3xTF32 GEMM instead (the same results
+        # within fp32 rounding; kept for comparisons)
+        self.q8_gemm = True
+
+    def _q8_ok(self, name) -> bool:
+        t = self.w.host_tensor(self.p + name) if hasattr(self.w, "host_tensor") else None
+        return (isinstance(t, QTensor) and t.kind == "q8" and t.padded_k == t.shape[1] and t.shape[1] % 64 == 0
+                and t.shape[0] % 128 == 0)
 
     # -- weights -------------------------------------------------------------------
     def _wt(self, name):
@@ -116,17 +125,28 @@ class DiT:
         for i in range(self.depth):
             b = f"transformer_blocks.{i}."
             B = _Block()
-            B.qkv = Lin(self._dense([b + "attn.to_q.weight", b + "attn.to_k.weight", b + "attn.to_v.weight"]),
-                        self.w.cache((self.p + b + "qkv_bias",), lambda b=b: torch.cat(
-                            [self._f32(b + f"attn.to_{n}.bias") for n in "qkv"]).contiguous()))
-            B.out = Lin(self._dense([b + "attn.to_out.0.weight"]), self._f32(b + "attn.to_out.0.bias"))
-            B.ff1 = Lin(self._dense([b + "ff.ff.0.0.weight"]), self._f32(b + "ff.ff.0.0.bias"))
-            B.ff2 = Lin(self._dense([b + "ff.ff.2.weight"]), self._f32(b + "ff.ff.2.bias"))
+            qkv_names = [b + "attn.to_q.weight", b + "attn.to_k.weight", b + "attn.to_v.weight"]
+            qkv_bias = self.w.cache((self.p + b + "qkv_bias",), lambda b=b: torch.cat(
+                [self._f32(b + f"attn.to_{n}.bias") for n in "qkv"]).contiguous())
+            if self.q8_gemm and all(self._q8_ok(n) for n in qkv_names + [b + "attn.to_out.0.weight",
+                                                                       b + "ff.ff.0.0.weight", b + "ff.ff.2.weight"]):
+                # balanced profile: the int8 weights as stored, on the tensor cores
+                qkv = self.w.cache((self.p + b + "qkv:q8",), lambda: cat_rows([self._wt(n) for n in qkv_names]))
+                B.qkv = LinQ8(qkv, qkv_bias)
+                B.out = LinQ8(self._wt(b + "attn.to_out.0.weight"), self._f32(b + "attn.to_out.0.bias"))
+                B.ff1 = LinQ8(self._wt(b + "ff.ff.0.0.weight"), self._f32(b + "ff.ff.0.0.bias"))
+                B.ff2 = LinQ8(self._wt(b + "ff.ff.2.weight"), self._f32(b + "ff.ff.2.bias"))
+            else:
+                B.qkv = Lin(self._dense(qkv_names), qkv_bias)
+                B.out = Lin(self._dense([b + "attn.to_out.0.weight"]), self._f32(b + "attn.to_out.0.bias"))
+                B.ff1 = Lin(self._dense([b + "ff.ff.0.0.weight"]), self._f32(b + "ff.ff.0.0.bias"))
+                B.ff2 = Lin(self._dense([b + "ff.ff.2.weight"]), self._f32(b + "ff.ff.2.bias"))
             self.blocks.append(B)
         self.proj_out = Lin(f32_of(self._wt("proj_out.weight")), self._f32("proj_out.bias"))
         # the tf32 remainders of the tensor-core weights exist before any graph capture
         for lin in [self.proj_in, self.proj_out] + [l for B in self.blocks for l in (B.qkv, B.out, B.ff1, B.ff2)]:
-            lin.lo()
+            if isinstance(lin, Lin):
+                lin.lo()
         self.ff = self.blocks[0].ff1.n
         self._ready = True
 

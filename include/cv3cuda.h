@@ -444,6 +444,28 @@ int cv3_tc_gemm_split(const float* a, int64_t lda, const float* b, const float* 
                       int64_t ldc, int64_t m, int64_t n, int64_t k, int mode, const float* bias, const float* gate,
                       int64_t rows_per_group, int64_t gate_stride, void* stream);
 
+/* The balanced profile's q8 linears on the tensor cores with the int8 weights as
+ * they are stored (replaces cv3cpu/quant.py:156-204 qmatmul on the DiT's block
+ * matrices, cv3cpu/models/dit.py:114-142):
+ *   C = epilogue( sum_g s[n][g] * (A[:, 64g..64g+63] . q[n][64g..64g+63]) )
+ * A fp32 [m][lda] (16-byte aligned rows), each 64-wide K group of a row split into
+ * two fp16 parts after a power-of-two scaling (22 significant bits, the precision
+ * of the 3xTF32 split); w16 = q as fp16 [n][k] and scales_t = s as fp32 [k/64][n],
+ * both made once by cv3_q8_gemm_prepare.  n % 128 == 0, k % 64 == 0.  Epilogue
+ * modes as cv3_tc_gemm (0 +bias, 1 GELU-tanh, 2 gated residual, 3 residual). */
+int cv3_tc_gemm_q8(const float* a, int64_t lda, const void* w16, const float* scales_t, float* c, int64_t ldc,
+                   int64_t m, int64_t n, int64_t k, int mode, const float* bias, const float* gate,
+                   int64_t rows_per_group, int64_t gate_stride, void* stream);
+
+/* The operands cv3_tc_gemm_q8 reads, from a q8 matrix (quant.py:90-136 layout,
+ * int8 [n][k] with k % 64 == 0, fp16 scales [n][k/64]): w16 fp16 [n][k] (exact)
+ * and scales_t fp32 [k/64][n]. */
+int cv3_q8_gemm_prepare(const int8_t* q, const uint16_t* scales, int64_t n, int64_t k, void* w16, float* scales_t,
+                        void* stream);
+
+/* Error word of cv3_tc_gemm_q8 (see cv3_tc_gemm_status). */
+int cv3_tc_gemm_q8_status(int* code);
+
 /* Rearrange conv weights W[C_out][C_in/groups][k] into the tensor-core
  * layout Wt[C_out][ci_pad/32][k][32] (ci_pad = C_in/groups rounded up to 32, zero
  * filled) and, if wt_lo is not NULL, the tf32 remainders.  Done once per

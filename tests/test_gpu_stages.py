@@ -102,3 +102,25 @@ def test_hift_full_geometry_snake_and_vocoder_length(small_weights):
     got = h.inference(mel)
     assert got.shape == (480 * 40,) and np.abs(got).max() <= 0.99 + 1e-7
     assert rel_err(got, st.HiFT(W, W.meta).inference(mel, chunk=None)) < TOL
+
+
+def test_balanced_dit_forward_full_size_q8_gemm_matches_oracle():
+    """The released DiT geometry in the balanced profile: the block matrices run through
+    cv3_tc_gemm_q8 on the stored int8 weights; one forward at batch 2 x 128 frames
+    against the oracle (which dequantises to fp32, as the reference's qmatmul does) at
+    the fp32 bar, and the dequantised 3xTF32 path agrees as well."""
+    W = pkg("synth").synthetic_weights("balanced", stages=("flow",))
+    rng = np.random.default_rng(12)
+    B, N = 2, 128
+    x, mu, cond = (rng.normal(size=(B, 80, N)).astype(np.float32) for _ in range(3))
+    spk = rng.normal(size=(B, 80)).astype(np.float32)
+    t = np.array([0.2, 0.8], np.float32)
+    dev = pkg("models.dit").DiT(_device(W))
+    dev.prepare()
+    assert type(dev.blocks[0].ff1).__name__ == "LinQ8"
+    got = dev.forward(x, mu, t, spk, cond)
+    ref = st.DiT(W, W.meta).forward(x, mu, t, spk, cond)
+    assert rel_err(got, ref) < TOL
+    f32 = pkg("models.dit").DiT(_device(W))
+    f32.q8_gemm = False
+    assert rel_err(f32.forward(x, mu, t, spk, cond), ref) < TOL

@@ -116,3 +116,66 @@ def test_epilogues(kind):
     ref = h + np.repeat(gate, rows, axis=0) * y
     assert rel_err(_run(a, b, 2, bias, gate, h, rows_per_group=rows, kind=kind), ref) < 1e-5
     assert rel_err(_run(a, b, 3, bias, None, h, kind=kind), h + y) < 1e-5
+
+
+# ---------------------------------------------------------------------------
+# cv3_tc_gemm_q8: the int8 weights as stored (balanced DiT), against fp64 of A . (q * s)^T
+# ---------------------------------------------------------------------------
+
+def _run_q8(a, w, mode=0, bias=None, gate=None, c0=None, rows_per_group=0):
+    import torch
+    L = pkg("_lib")
+    qt = pkg("quant").make_qtensor(w)
+    n, k = w.shape
+    m = a.shape[0]
+    qd, sd = torch.from_numpy(qt.q).cuda(), torch.from_numpy(qt.scales.view(np.uint16)).cuda()
+    w16 = torch.empty((n, k), dtype=torch.float16, device="cuda")
+    stt = torch.empty((k // 64, n), dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    L.call("cv3_q8_gemm_prepare", qd.data_ptr(), sd.data_ptr(), n, k, w16.data_ptr(), stt.data_ptr(), st)
+    ad = torch.from_numpy(a).cuda()
+    c = torch.from_numpy(c0.copy()).cuda() if c0 is not None else torch.zeros(m, n, device="cuda")
+    bb = torch.from_numpy(bias).cuda() if bias is not None else None
+    gg = torch.from_numpy(gate).cuda() if gate is not None else None
+    L.call("cv3_tc_gemm_q8", ad.data_ptr(), k, w16.data_ptr(), stt.data_ptr(), c.data_ptr(), n, m, n, k, mode,
+           bb.data_ptr() if bb is not None else None, gg.data_ptr() if gg is not None else None, rows_per_group,
+           n if gate is not None else 0, st)
+    torch.cuda.synchronize()
+    code = ctypes.c_int()
+    L.call("cv3_tc_gemm_q8_status", ctypes.byref(code))
+    assert code.value == 0, f"bounded wait expired (code {code.value})"
+    wd = qt.q.astype(np.float64) * np.repeat(qt.scales.astype(np.float64), 64, axis=1)[:, :k]
+    return c.cpu().numpy(), wd
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 128, 64), (37, 128, 128), (300, 256, 1024), (1000, 1024, 2048),
+                                   (10400, 2048, 1024), (1300, 3072, 1024)])
+def test_q8_gemm_matches_fp64(m, n, k):
+    rng = np.random.default_rng(m + n + k)
+    a = rng.normal(size=(m, k)).astype(np.float32)
+    a[: m // 3] *= 40.0   # rows of different magnitudes (per-row, per-group scaling)
+    a[:, : k // 4] *= 1e-3
+    w = (rng.normal(size=(n, k)) * 0.02).astype(np.float32)
+    got, wd = _run_q8(a, w)
+    ref = a.astype(np.float64) @ wd.T
+    assert rel_err(got, ref) < 1e-5
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_q8_gemm_epilogues(mode):
+    rng = np.random.default_rng(7 + mode)
+    m, n, k = 650, 1024, 1024
+    a = rng.normal(size=(m, k)).astype(np.float32)
+    w = (rng.normal(size=(n, k)) * 0.03).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    gate = rng.normal(size=(3, n)).astype(np.float32) if mode == 2 else None
+    c0 = rng.normal(size=(m, n)).astype(np.float32) if mode >= 2 else None
+    got, wd = _run_q8(a, w, mode, bias, gate, c0, rows_per_group=256 if mode == 2 else 0)
+    y = a.astype(np.float64) @ wd.T + bias
+    if mode == 1:
+        y = _gelu(y)
+    elif mode == 2:
+        y = c0 + gate[np.arange(m) // 256] * y
+    elif mode == 3:
+        y = c0 + y
+    assert rel_err(got, y) < 1e-5
