@@ -601,6 +601,18 @@ def run_kernel(args) -> None:
         lin = common.LinQ8(quant.make_qtensor(w).to_device())
         a, c = torch.randn(M, K, device="cuda"), torch.empty(M, N, device="cuda")
         fn = lambda: lin(a.data_ptr(), M, c.data_ptr(), stream=st)
+    elif args.kernel == "ff1q8p":
+        # the same GEMM with A as activation planes (what the balanced DiT feeds it)
+        M, N, K = 2 * UTTS * 2 * (PROMPT_TOKENS + TOKENS), 2048, 1024
+        quant = pkg("quant")
+        w = (np.random.default_rng(0).normal(size=(N, K)) * 0.02).astype(np.float32)
+        lin = common.LinQ8(quant.make_qtensor(w).to_device())
+        a, c = torch.randn(M, K, device="cuda"), torch.empty(M, N, device="cuda")
+        lde = -(-M // 16) * 16
+        pl = torch.empty((M, 2 * K), dtype=torch.float16, device="cuda")
+        ex = torch.empty((K // 64, lde), dtype=torch.int8, device="cuda")
+        L.call("cv3_q8_split_rows", a.data_ptr(), K, M, K, pl.data_ptr(), ex.data_ptr(), lde, st)
+        fn = lambda: lin.tc_planes(pl.data_ptr(), ex.data_ptr(), lde, M, c.data_ptr(), 0, stream=st)
     elif args.kernel == "attention":
         B, H, N, D = 2 * UTTS, 16, 2 * (PROMPT_TOKENS + TOKENS), 64
         qkv, o = torch.randn(B, N, 3 * H * D, device="cuda"), torch.empty(B, N, H * D, device="cuda")
@@ -763,7 +775,7 @@ def main():
     ap.add_argument("--sampled", action="store_true",
                     help="with --lm-step: the sampled step (device sampler) and the host-sampler path")
     ap.add_argument("--slice", action="store_true", help="profiling slice (see run_slice)")
-    ap.add_argument("--kernel", choices=["ff1", "ff1q8", "attention", "conv", "gemv"],
+    ap.add_argument("--kernel", choices=["ff1", "ff1q8", "ff1q8p", "attention", "conv", "gemv"],
                     help="run one hot kernel alone at its bench shape (for ncu captures)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)

@@ -84,6 +84,9 @@ SIGNATURES = {
     "cv3_tc_gemm_q8": [P, I64, P, P, P, I64, I64, I64, I64, I32, P, P, I64, I64, P],
     "cv3_q8_gemm_prepare": [P, P, I64, I64, P, P, P],
     "cv3_tc_gemm_q8_status": [P],
+    "cv3_tc_gemm_q8_planes": [P, P, I64, P, P, P, I64, I64, I64, I64, I32, P, P, I64, I64, P, P, I64, P],
+    "cv3_q8_split_rows": [P, I64, I64, I64, P, P, I64, P],
+    "cv3_ln_modulate_planes": [P, I64, I64, F, P, P, I64, I64, P, P, I64, P],
     "cv3_decode_steps": [P, P],
     "cv3_decode_sync_words": [I64, I64],
     "cv3_decode_status": [P],

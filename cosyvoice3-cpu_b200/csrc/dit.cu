@@ -7,6 +7,7 @@
 // operation order (explicit round-to-nearest multiply/add where NumPy would
 // round twice) so that only GEMM/attention summation order differs.
 #include "common.cuh"
+#include "planes.cuh"
 
 namespace {
 
@@ -67,13 +68,17 @@ __global__ void ln_modulate_kernel(const float* __restrict__ h, int dim, float e
 
 // ln_modulate_kernel for dim = 128 * V: one warp per row, the row in registers (V
 // float4 per lane, one coalesced read), mean and variance by warp shuffles (no
-// block barriers), same formulas; 8 rows per CTA.
-template <int V>
+// block barriers), same formulas; 8 rows per CTA.  PLANES: the result goes out as
+// activation planes (planes.cuh) for cv3_tc_gemm_q8_planes instead of fp32 -- float4
+// j of a lane holds columns 4 (lane + 32 j) .., so each half warp covers one 64-wide
+// group, whose exponent is a 16-lane max.
+template <int V, bool PLANES>
 __global__ void __launch_bounds__(256) ln_modulate_warp_kernel(const float* __restrict__ h, int64_t rows, float eps,
                                                                const float* __restrict__ scale,
                                                                const float* __restrict__ shift,
                                                                int64_t rows_per_group, int64_t mod_stride,
-                                                               float* __restrict__ y) {
+                                                               float* __restrict__ y, __half* __restrict__ planes,
+                                                               int8_t* __restrict__ exps, int64_t lde) {
   constexpr int DIM = 128 * V;
   const int lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -97,7 +102,6 @@ __global__ void __launch_bounds__(256) ln_modulate_warp_kernel(const float* __re
   const int64_t g = rows_per_group > 0 ? r / rows_per_group : 0;
   const float4* sc4 = reinterpret_cast<const float4*>(scale + g * mod_stride);
   const float4* sh4 = reinterpret_cast<const float4*>(shift + g * mod_stride);
-  float4* o4 = reinterpret_cast<float4*>(y + r * DIM);
 #pragma unroll
   for (int j = 0; j < V; ++j) {
     const float4 sc = __ldg(sc4 + lane + 32 * j), sh = __ldg(sh4 + lane + 32 * j);
@@ -106,7 +110,23 @@ __global__ void __launch_bounds__(256) ln_modulate_warp_kernel(const float* __re
     o.y = add(mul((v[j].y - mu) / sd, add(1.0f, sc.y)), sh.y);
     o.z = add(mul((v[j].z - mu) / sd, add(1.0f, sc.z)), sh.z);
     o.w = add(mul((v[j].w - mu) / sd, add(1.0f, sc.w)), sh.w);
-    o4[lane + 32 * j] = o;
+    if (!PLANES) {
+      reinterpret_cast<float4*>(y + r * DIM)[lane + 32 * j] = o;
+    } else {
+      float am = fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w)));
+#pragma unroll
+      for (int m = 1; m < 16; m <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, m));
+      const int e = cv3p::group_exponent(am);
+      const float f = cv3p::pow2f(e);
+      const int g = 2 * j + (lane >> 4), c = 4 * (lane & 15);
+      uint32_t h0, l0, h1, l1;
+      cv3p::split_pair(o.x * f, o.y * f, h0, l0);
+      cv3p::split_pair(o.z * f, o.w * f, h1, l1);
+      __half* pr = planes + r * (2 * DIM) + 128 * g + c;
+      *reinterpret_cast<uint2*>(pr) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(pr + 64) = make_uint2(l0, l1);
+      if ((lane & 15) == 0) exps[(int64_t)g * lde + r] = (int8_t)e;
+    }
   }
 }
 
@@ -227,16 +247,37 @@ extern "C" int cv3_ln_modulate(const float* h, int64_t rows, int64_t dim, float 
   if (al && (dim == 1024 || dim == 512)) {
     const unsigned grid = (unsigned)((rows + 7) / 8);
     if (dim == 1024)
-      ln_modulate_warp_kernel<8><<<grid, 256, 0, cv3::as_stream(stream)>>>(h, rows, eps, scale, shift, rows_per_group,
-                                                                           mod_stride, y);
+      ln_modulate_warp_kernel<8, false><<<grid, 256, 0, cv3::as_stream(stream)>>>(
+          h, rows, eps, scale, shift, rows_per_group, mod_stride, y, nullptr, nullptr, 0);
     else
-      ln_modulate_warp_kernel<4><<<grid, 256, 0, cv3::as_stream(stream)>>>(h, rows, eps, scale, shift, rows_per_group,
-                                                                           mod_stride, y);
+      ln_modulate_warp_kernel<4, false><<<grid, 256, 0, cv3::as_stream(stream)>>>(
+          h, rows, eps, scale, shift, rows_per_group, mod_stride, y, nullptr, nullptr, 0);
     return cv3::check_launch("ln_modulate");
   }
   ln_modulate_kernel<<<(unsigned)rows, row_threads(dim), 0, cv3::as_stream(stream)>>>(
       h, (int)dim, eps, scale, shift, rows_per_group, mod_stride, y);
   return cv3::check_launch("ln_modulate");
+}
+
+extern "C" int cv3_ln_modulate_planes(const float* h, int64_t rows, int64_t dim, float eps, const float* scale,
+                                      const float* shift, int64_t rows_per_group, int64_t mod_stride, void* planes,
+                                      int8_t* exps, int64_t lde, void* stream) {
+  CV3_REQUIRE(rows >= 0 && rows < (1LL << 31) && (dim == 1024 || dim == 512), CV3_ERR_UNSUPPORTED,
+              "ln_modulate_planes: dim 512 or 1024");
+  CV3_REQUIRE(lde >= rows && lde % 16 == 0, CV3_ERR_VALUE, "ln_modulate_planes: lde >= rows, a multiple of 16");
+  CV3_REQUIRE((((uintptr_t)h | (uintptr_t)planes | (uintptr_t)scale | (uintptr_t)shift) & 15) == 0 &&
+                  mod_stride % 4 == 0,
+              CV3_ERR_VALUE, "ln_modulate_planes: 16-byte aligned operands");
+  if (rows == 0) return CV3_OK;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  __half* pl = static_cast<__half*>(planes);
+  if (dim == 1024)
+    ln_modulate_warp_kernel<8, true><<<grid, 256, 0, cv3::as_stream(stream)>>>(
+        h, rows, eps, scale, shift, rows_per_group, mod_stride, nullptr, pl, exps, lde);
+  else
+    ln_modulate_warp_kernel<4, true><<<grid, 256, 0, cv3::as_stream(stream)>>>(
+        h, rows, eps, scale, shift, rows_per_group, mod_stride, nullptr, pl, exps, lde);
+  return cv3::check_launch("ln_modulate_planes");
 }
 
 extern "C" int cv3_gate_residual(float* h, const float* y, const float* gate, int64_t rows, int64_t dim,

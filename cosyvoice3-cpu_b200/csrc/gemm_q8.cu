@@ -13,7 +13,8 @@
 // where 3xTF32 on dequantised weights issues 24 tf32 MMAs), and the epilogue warps
 // promote it: acc[m][n] += P * 2^-e[m][g] * s[n][g] in fp32 registers.
 //
-// Persistent CTAs (one per SM) walk 128 x 128 output tiles; 14 warps:
+// Persistent CTAs (one per SM) walk 128 x 128 output tiles; 14 warps (18 with A given
+// as activation planes: no converters, sixteen promotion warps of 32 columns):
 //   warp 0     TMA: per K group the A fp32 tile (two 32-wide SWIZZLE_128B boxes) and the
 //              q tile (fp16, converted once at load); a stage is free again once the
 //              converters have read A and the MMAs B;
@@ -28,6 +29,7 @@
 // (cv3_tc_gemm_q8_status), stops issuing work, lets what it issued finish and exits.
 #include <algorithm>
 
+#include "planes.cuh"
 #include "tc_common.cuh"
 
 namespace {
@@ -35,36 +37,53 @@ namespace {
 using namespace cv3tc;
 
 constexpr int BM = 128, BN = 128, KG = 64;  // KG: one scale group
-constexpr int STAGES = 3;
+constexpr int STAGES = 3;                            // fp32 A: converted in the kernel
+constexpr int STAGES_P = 4;                          // pre-split A planes: hi | lo | B per stage
 constexpr int TILE_A = BM * KG * 4;                  // 32 KB: two 32-wide fp32 boxes
 constexpr int TILE_B = BN * KG * 2;                  // 16 KB: fp16 weights
 constexpr int STAGE_BYTES = TILE_A + TILE_B;        // A | B (1 KB multiples: SW128 tiles)
 constexpr int PLANES_AT = STAGES * STAGE_BYTES;      // 2 buffers x (hi | lo), 16 KB each
 constexpr int PLANE = BM * KG * 2;                   // 16 KB
-constexpr int THREADS = 448;
-constexpr int EPI_COLS = 64;
+// warps: 0 TMA, 1 MMA; fp32 A: 2-5 converters, 6-13 promotion (64 columns each);
+// pre-split A: 2-17 promotion (32 columns each: four warps per TMEM lane quarter)
+template <bool P> struct Layout {
+  static constexpr int THREADS = P ? 576 : 448;
+  static constexpr int PW0 = P ? 2 : 6;    // first promotion warp
+  static constexpr int NPW = P ? 16 : 8;   // promotion warps
+  static constexpr int EPI_COLS = P ? 32 : 64;
+};
 constexpr int NACC = 4;  // TMEM accumulators (one per K group in flight), 128 columns each
+constexpr int NSIDE = 8;                       // side ring: per group the tile's scales and exponents
+constexpr int SIDE_BYTES = BN * 4 + BM;        // 512 B fp32 scales | 128 B int8 exponents
 constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);  // f16 x f16 -> f32
 
 __device__ int g_q8_err = 0;
 
 struct Bars {
-  uint64_t full[STAGES], empty[STAGES], afull[2], aempty[2], pfull[NACC], pempty[NACC], done;
+  uint64_t full[STAGES_P], empty[STAGES_P], afull[2], aempty[2], pfull[NACC], pempty[NACC], done;
+  uint64_t sfull[NSIDE], sempty[NSIDE];
+  int sissued[NSIDE];
   uint32_t tmem;
   int abort_flag;
-  int issued[STAGES];
+  int issued[STAGES_P];
   // per (group mod 8, row): the power of two the converters scaled by.  Depth: converter
   // g waits for MMA g-2, which waits for the promotion of g-2-NACC, so the slot of
   // group g is rewritten only after its promotion when the depth is >= NACC + 2
   int ex[8][BM];
+  float xmax[4][BM];  // mode 4 with 32-column threads: each column quarter's row maxima
 };
-constexpr int SMEM_BYTES = PLANES_AT + 4 * PLANE + 1024 + (int)sizeof(Bars);
+constexpr int SIDE_AT = PLANES_AT + 4 * PLANE;   // after both layouts' stages / planes
+constexpr int SMEM_BYTES = SIDE_AT + NSIDE * SIDE_BYTES + 1024 + (int)sizeof(Bars);
 
 struct Epi {
-  int mode;  // 0: +bias; 1: gelu_tanh(+bias); 2: h += gate * (+bias); 3: h += (+bias)
+  int mode;  // 0: +bias; 1: gelu_tanh(+bias); 2: h += gate * (+bias); 3: h += (+bias);
+             // 4: gelu_tanh(+bias) written as activation planes (oplanes, oexps, olde)
   const float* bias;
   const float* gate;
   int64_t rows_per_group, gate_stride;
+  __half* oplanes;
+  int8_t* oexps;
+  int64_t olde;
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -142,6 +161,7 @@ __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) 
 // One K group's MMAs: 4 k-steps of 16, A hi and A lo into the group's accumulator d,
 // the weights from one descriptor; then the commits that free the stage, the A planes
 // and hand the accumulator to the promotion.
+template <bool PLANES_BAR>
 __device__ __forceinline__ void issue_group(uint32_t d, uint64_t ahi, uint64_t alo, uint64_t b,
                                             uint64_t* bar_stage, uint64_t* bar_planes, uint64_t* bar_acc) {
   asm volatile(
@@ -161,20 +181,26 @@ __device__ __forceinline__ void issue_group(uint32_t d, uint64_t ahi, uint64_t a
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], h3, b3, %4, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], l3, b3, %4, pt;\n\t"
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t"
-      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t"
-      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%8];\n\t}" ::"r"(d),
-      "l"(ahi), "l"(alo), "l"(b), "r"(IDESC), "r"(0), "r"(smem_u32(bar_stage)), "r"(smem_u32(bar_planes)),
-      "r"(smem_u32(bar_acc))
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t}" ::"r"(d),
+      "l"(ahi), "l"(alo), "l"(b), "r"(IDESC), "r"(0), "r"(smem_u32(bar_stage)), "r"(smem_u32(bar_acc))
       : "memory");
+  if (PLANES_BAR) mma_commit(bar_planes);
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+// PRESPLIT: A arrives as activation planes (planes.cuh) by TMA -- hi | lo | B per
+// stage, four stages, no converter warps; the promotion reads the exponents from
+// pexp.  Otherwise A is fp32 and the converter warps split it.
+template <bool PRESPLIT>
+__global__ void __launch_bounds__(Layout<PRESPLIT>::THREADS, 1)
 tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                  const float* __restrict__ scales_t, int M, int N, int K, float* __restrict__ C, int64_t ldc,
-                  Epi ep) {
+                  const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_e, int M, int N,
+                  int K, float* __restrict__ C, int64_t ldc, Epi ep) {
+  constexpr int NST = PRESPLIT ? STAGES_P : STAGES;
+  constexpr int EPI_COLS = Layout<PRESPLIT>::EPI_COLS, NPW = Layout<PRESPLIT>::NPW, PW0 = Layout<PRESPLIT>::PW0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars& S = *reinterpret_cast<Bars*>(smem + PLANES_AT + 4 * PLANE);
+  Bars& S = *reinterpret_cast<Bars*>(smem + SIDE_AT + NSIDE * SIDE_BYTES);
+  uint8_t* side = smem + SIDE_AT;
   volatile int* abort_flag = &S.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ng = K / KG;
@@ -182,9 +208,9 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
   const int ntiles = tiles_n * ((M + BM - 1) / BM);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&S.full[s], 1);
-      mbar_init(&S.empty[s], 1 + 4);  // MMA commit (B), four converter warps (A)
+      mbar_init(&S.empty[s], PRESPLIT ? 1 : 1 + 4);  // MMA commit (B, and A planes), converter warps (fp32 A)
       S.issued[s] = -1;
     }
     for (int i = 0; i < 2; ++i) {
@@ -193,7 +219,12 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
     }
     for (int i = 0; i < NACC; ++i) {
       mbar_init(&S.pfull[i], 1);
-      mbar_init(&S.pempty[i], 8);
+      mbar_init(&S.pempty[i], NPW);
+    }
+    for (int i = 0; i < NSIDE; ++i) {
+      mbar_init(&S.sfull[i], 1);
+      mbar_init(&S.sempty[i], NPW);
+      S.sissued[i] = -1;
     }
     mbar_init(&S.done, 1);
     S.abort_flag = 0;
@@ -224,8 +255,8 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
       for (int tile = blockIdx.x; go && tile < ntiles; tile += gridDim.x) {
         const int n0 = (tile % tiles_n) * BN, m0 = (tile / tiles_n) * BM;
         for (int kg = 0; kg < ng; ++kg, ++g) {
-          const int s = g % STAGES;
-          const uint32_t r = (uint32_t)(g / STAGES);
+          const int s = g % NST;
+          const uint32_t r = (uint32_t)(g / NST);
           if (*abort_flag || !mbar_wait(&S.empty[s], (r & 1) ^ 1, &g_q8_err, 1)) {
             *abort_flag = 1;
             go = false;
@@ -234,9 +265,26 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
           uint8_t* st = smem + s * STAGE_BYTES;
           S.issued[s] = (int)r;
           mbar_expect_tx(&S.full[s], TILE_A + TILE_B);
-          tma_load_2d(st, &map_a, &S.full[s], kg * KG, m0);
-          tma_load_2d(st + TILE_A / 2, &map_a, &S.full[s], kg * KG + KG / 2, m0);
+          if (PRESPLIT) {
+            tma_load_2d(st, &map_a, &S.full[s], 2 * KG * kg, m0);            // hi plane of the group
+            tma_load_2d(st + PLANE, &map_a, &S.full[s], 2 * KG * kg + KG, m0);  // lo plane
+          } else {
+            tma_load_2d(st, &map_a, &S.full[s], kg * KG, m0);
+            tma_load_2d(st + TILE_A / 2, &map_a, &S.full[s], kg * KG + KG / 2, m0);
+          }
           tma_load_2d(st + TILE_A, &map_b, &S.full[s], kg * KG, n0);
+          // the promotion's per-group constants: scales (and the planes' exponents)
+          const int sl = g % NSIDE;
+          if (!mbar_wait(&S.sempty[sl], ((uint32_t)(g / NSIDE) & 1) ^ 1, &g_q8_err, 10)) {
+            *abort_flag = 1;
+            go = false;
+            break;
+          }
+          uint8_t* sd = side + sl * SIDE_BYTES;
+          S.sissued[sl] = g / NSIDE;
+          mbar_expect_tx(&S.sfull[sl], PRESPLIT ? SIDE_BYTES : BN * 4);
+          tma_load_2d(sd, &map_s, &S.sfull[sl], n0, kg);
+          if (PRESPLIT) tma_load_2d(sd + BN * 4, &map_e, &S.sfull[sl], m0, kg);
         }
       }
     }
@@ -246,36 +294,37 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
     int g = 0;
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
       for (int kg = 0; kg < ng; ++kg, ++g) {
-        const int s = g % STAGES;
-        const uint32_t r = (uint32_t)(g / STAGES);
+        const int s = g % NST;
+        const uint32_t r = (uint32_t)(g / NST);
         const int b = g & 1;
         const uint32_t u = (uint32_t)(g >> 1);
         const int ai = g % NACC;
-        if (!ready(&S.full[s], r & 1, 2) || !ready(&S.afull[b], u & 1, 3) ||
+        if (!ready(&S.full[s], r & 1, 2) || (!PRESPLIT && !ready(&S.afull[b], u & 1, 3)) ||
             (g >= NACC && !ready(&S.pempty[ai], (uint32_t)(g / NACC - 1) & 1, 4))) {
           ok = false;
           break;
         }
         fence_after();
-        const uint64_t dah = desc_k_sw128(smem_u32(smem + PLANES_AT + b * 2 * PLANE));
+        const uint64_t dah =
+            desc_k_sw128(smem_u32(PRESPLIT ? smem + s * STAGE_BYTES : smem + PLANES_AT + b * 2 * PLANE));
         const uint64_t dal = dah + (PLANE >> 4);
         const uint64_t db = desc_k_sw128(smem_u32(smem + s * STAGE_BYTES + TILE_A));
-        issue_group(tmem + ai * 128, dah, dal, db, &S.empty[s], &S.aempty[b], &S.pfull[ai]);
+        issue_group<!PRESPLIT>(tmem + ai * 128, dah, dal, db, &S.empty[s], &S.aempty[b], &S.pfull[ai]);
       }
     }
     if (!ok && lane == 0) *abort_flag = 1;
     mma_commit(&S.done);  // also on abort: arrives once whatever was issued has completed
-  } else if (warp < 6) {
-    // ---- converters: thread = A row ----
+  } else if (!PRESPLIT && warp < 6) {
+    // ---- converters: thread = A row (idle with pre-split planes) ----
     const int row = (warp - 2) * 32 + lane;
-    bool ok = true;
+    bool ok = !PRESPLIT;
     int g = 0;
-    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+    for (int tile = blockIdx.x; !PRESPLIT && ok && tile < ntiles; tile += gridDim.x) {
       for (int kg = 0; kg < ng; ++kg, ++g) {
-        const int s = g % STAGES;
+        const int s = g % NST;
         const int b = g & 1;
         const uint32_t u = (uint32_t)(g >> 1);
-        if (!ready(&S.full[s], (uint32_t)(g / STAGES) & 1, 5)) {
+        if (!ready(&S.full[s], (uint32_t)(g / NST) & 1, 5)) {
           ok = false;
           break;
         }
@@ -329,12 +378,12 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         if (lane == 0) mbar_arrive(&S.afull[b]);
       }
     }
-    if (!ok) *abort_flag = 1;
+    if (!ok && !PRESPLIT) *abort_flag = 1;
   } else {
     // ---- promotion and epilogue: thread = output row (its TMEM lane), 64 columns ----
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int cbase = (warp - 6) / 4 * EPI_COLS;
+    const int cbase = (warp - PW0) / 4 * EPI_COLS;
     const uint32_t lane_base = ((uint32_t)(quarter * 32) << 16) + (uint32_t)cbase;
     const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
     bool ok = true;
@@ -345,23 +394,28 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
 #pragma unroll
       for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.f;
       for (int kg = 0; kg < ng; ++kg, ++g) {
-        const int s = g % STAGES;
+        const int s = g % NST;
         const int ai = g % NACC;
         if (!ready(&S.pfull[ai], (uint32_t)(g / NACC) & 1, 7)) {
           ok = false;
           break;
         }
         fence_after();
-        const float f = pow2f(-S.ex[g & 7][row]);
-        // the group's scales of this warp's columns: the same for every lane (L1 broadcast)
-        const float* scl = scales_t + (int64_t)kg * N + n0 + cbase;
+        const int sl = g % NSIDE;
+        if (!ready(&S.sfull[sl], (uint32_t)(g / NSIDE) & 1, 11)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* sd = side + sl * SIDE_BYTES;
+        const float f = pow2f(PRESPLIT ? -(int)reinterpret_cast<const int8_t*>(sd + BN * 4)[row] : -S.ex[g & 7][row]);
+        const float* scl = reinterpret_cast<const float*>(sd) + cbase;  // the same for every lane
 #pragma unroll
         for (int c0 = 0; c0 < EPI_COLS; c0 += 32) {
           float pv[32];
           tmem_ld32(tmem + lane_base + ai * 128 + c0, pv);
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const float4 sv = __ldg(reinterpret_cast<const float4*>(scl + c0 + 4 * q));
+            const float4 sv = *reinterpret_cast<const float4*>(scl + c0 + 4 * q);
             acc[c0 + 4 * q] = fmaf(pv[4 * q] * f, sv.x, acc[c0 + 4 * q]);
             acc[c0 + 4 * q + 1] = fmaf(pv[4 * q + 1] * f, sv.y, acc[c0 + 4 * q + 1]);
             acc[c0 + 4 * q + 2] = fmaf(pv[4 * q + 2] * f, sv.z, acc[c0 + 4 * q + 2]);
@@ -370,10 +424,53 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         }
         fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.pempty[ai]);
+        if (lane == 0) {
+          mbar_arrive(&S.pempty[ai]);
+          mbar_arrive(&S.sempty[sl]);
+        }
+      }
+      const int grow = m0 + row;
+      if (PRESPLIT && ep.mode == 4) {
+        // GELU-tanh, then the tile's columns as planes for the next GEMM: a 64-wide group
+        // spans two 32-column threads of the same row, which exchange their maxima
+        float am = 0.f;
+#pragma unroll
+        for (int j = 0; j < EPI_COLS; ++j) {
+          acc[j] = gelu_tanh(ep.bias ? __fadd_rn(acc[j], __ldg(ep.bias + n0 + cbase + j)) : acc[j]);
+          am = fmaxf(am, fabsf(acc[j]));
+        }
+        const int cq = cbase / 32;
+        S.xmax[cq][row] = am;
+        // every promotion thread reaches this barrier each tile, also after a failed wait
+        // (then it leaves with the others: the barrier also agrees on ok)
+        uint32_t all_ok;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, %2, p;\n\t"
+            "selp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(all_ok)
+            : "r"((uint32_t)ok), "n"(NPW * 32)
+            : "memory");
+        am = fmaxf(am, S.xmax[cq ^ 1][row]);
+        asm volatile("bar.sync 1, %0;" ::"n"(NPW * 32) : "memory");
+        ok = all_ok != 0;
+        if (!ok) break;
+        if (grow >= M) continue;
+        const int e = cv3p::group_exponent(am);
+        const float f = cv3p::pow2f(e);
+        const int gg = (n0 + cbase) / KG, half = cq & 1;
+        __half* ph = ep.oplanes + (int64_t)grow * (2 * N) + 2 * KG * gg + 32 * half;
+#pragma unroll
+        for (int q = 0; q < EPI_COLS / 8; ++q) {
+          uint32_t h[4], l[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) cv3p::split_pair(acc[8 * q + 2 * t] * f, acc[8 * q + 2 * t + 1] * f, h[t], l[t]);
+          *reinterpret_cast<uint4*>(ph + 8 * q) = make_uint4(h[0], h[1], h[2], h[3]);
+          *reinterpret_cast<uint4*>(ph + KG + 8 * q) = make_uint4(l[0], l[1], l[2], l[3]);
+        }
+        if (half == 0) ep.oexps[(int64_t)gg * ep.olde + grow] = (int8_t)e;
+        continue;
       }
       if (!ok) break;
-      const int grow = m0 + row;
       if (grow >= M) continue;
       float* crow = C + (int64_t)grow * ldc + n0 + cbase;
       const float* gate = ep.mode == 2 ? ep.gate + (ep.rows_per_group > 0 ? grow / ep.rows_per_group : 0) *
@@ -432,8 +529,11 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
   if (warp == 0) {
     if (lane == 0) {
       if (*abort_flag)
-        for (int s = 0; s < STAGES; ++s)
+        for (int s = 0; s < NST; ++s)
           if (S.issued[s] >= 0) mbar_wait(&S.full[s], (uint32_t)S.issued[s] & 1, &g_q8_err, 8);
+      if (*abort_flag)
+        for (int i = 0; i < NSIDE; ++i)
+          if (S.sissued[i] >= 0) mbar_wait(&S.sfull[i], (uint32_t)S.sissued[i] & 1, &g_q8_err, 12);
       mbar_wait(&S.done, 0, &g_q8_err, 9);  // every MMA (and its barrier arrivals) finished
     }
     __syncwarp();
@@ -456,6 +556,28 @@ int map_2d(CUtensorMap* map, CUtensorMapDataType type, int esize, const void* pt
                       swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   CV3_REQUIRE(r == CUDA_SUCCESS, CV3_ERR_CUDA, "tc_gemm_q8: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return CV3_OK;
+}
+
+// fp32 rows -> activation planes: one warp per row, two values per lane per group
+__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ x, int64_t ldx, int64_t rows,
+                                                         int k, __half* __restrict__ planes, int8_t* __restrict__ exps,
+                                                         int64_t lde) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float* xr = x + r * ldx;
+  __half* pr = planes + r * (2 * (int64_t)k);
+  for (int g = 0; g < k / KG; ++g) {
+    const float2 v = *reinterpret_cast<const float2*>(xr + KG * g + 2 * lane);
+    const float am = warp_max(fmaxf(fabsf(v.x), fabsf(v.y)));
+    const int e = cv3p::group_exponent(am);
+    const float f = cv3p::pow2f(e);
+    uint32_t h, l;
+    cv3p::split_pair(v.x * f, v.y * f, h, l);
+    *reinterpret_cast<uint32_t*>(pr + 2 * KG * g + 2 * lane) = h;
+    *reinterpret_cast<uint32_t*>(pr + 2 * KG * g + KG + 2 * lane) = l;
+    if (lane == 0) exps[(int64_t)g * lde + r] = (int8_t)e;
+  }
 }
 
 // q int8 [n][k] -> fp16 [n][k] (exact); scales fp16 [n][k/64] -> fp32 [k/64][n]
@@ -483,6 +605,38 @@ extern "C" int cv3_q8_gemm_prepare(const int8_t* q, const uint16_t* scales, int6
   return cv3::check_launch("q8_gemm_prepare");
 }
 
+namespace {
+
+int launch_q8(bool presplit, const CUtensorMap& ma, const void* w16, const float* scales_t, const int8_t* pexp,
+              int64_t lde, float* c, int64_t ldc, int64_t m, int64_t n, int64_t k, const Epi& ep, void* stream) {
+  CUtensorMap mb, ms, me;
+  int rc = map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w16, n, k, k, KG, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = map_2d(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, scales_t, k / KG, n, n, BN, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (presplit) {
+    rc = map_2d(&me, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, pexp, k / KG, lde, lde, BM, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    me = ms;  // (not read)
+  }
+  const void* fn = presplit ? (const void*)tc_gemm_q8_kernel<true> : (const void*)tc_gemm_q8_kernel<false>;
+  rc = cv3::allow_smem(fn, SMEM_BYTES);
+  if (rc) return rc;
+  const int64_t ntiles = (n / BN) * ((m + BM - 1) / BM);
+  CV3_REQUIRE(ntiles < (1LL << 31), CV3_ERR_VALUE, "tc_gemm_q8: too many tiles");
+  const int grid = (int)std::min<int64_t>(ntiles, cv3::sm_count());
+  if (presplit)
+    tc_gemm_q8_kernel<true><<<grid, Layout<true>::THREADS, SMEM_BYTES, cv3::as_stream(stream)>>>(
+        ma, mb, ms, me, (int)m, (int)n, (int)k, c, ldc, ep);
+  else
+    tc_gemm_q8_kernel<false><<<grid, Layout<false>::THREADS, SMEM_BYTES, cv3::as_stream(stream)>>>(
+        ma, mb, ms, me, (int)m, (int)n, (int)k, c, ldc, ep);
+  return cv3::check_launch("tc_gemm_q8");
+}
+
+}  // namespace
+
 extern "C" int cv3_tc_gemm_q8(const float* a, int64_t lda, const void* w16, const float* scales_t, float* c,
                               int64_t ldc, int64_t m, int64_t n, int64_t k, int mode, const float* bias,
                               const float* gate, int64_t rows_per_group, int64_t gate_stride, void* stream) {
@@ -492,21 +646,47 @@ extern "C" int cv3_tc_gemm_q8(const float* a, int64_t lda, const void* w16, cons
   CV3_REQUIRE(lda >= k && ldc >= n && lda % 4 == 0, CV3_ERR_VALUE, "tc_gemm_q8: leading dimensions");
   if (m == 0 || n == 0) return CV3_OK;
   CV3_REQUIRE(k > 0 && m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31), CV3_ERR_VALUE, "tc_gemm_q8: sizes");
-  CUtensorMap ma, mb;
+  CUtensorMap ma;
   int rc = map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a, m, k, lda, KG / 2, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w16, n, k, k, KG, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  Epi ep{mode, bias, gate, rows_per_group, gate_stride, nullptr, nullptr, 0};
+  return launch_q8(false, ma, w16, scales_t, nullptr, 0, c, ldc, m, n, k, ep, stream);
+}
+
+extern "C" int cv3_tc_gemm_q8_planes(const void* planes, const int8_t* exps, int64_t lde, const void* w16,
+                                     const float* scales_t, float* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                                     int mode, const float* bias, const float* gate, int64_t rows_per_group,
+                                     int64_t gate_stride, void* out_planes, int8_t* out_exps, int64_t out_lde,
+                                     void* stream) {
+  CV3_REQUIRE(m >= 0 && n >= 0 && k >= 0 && mode >= 0 && mode <= 4, CV3_ERR_VALUE, "tc_gemm_q8_planes: bad arguments");
+  CV3_REQUIRE(mode != 2 || gate != nullptr, CV3_ERR_VALUE, "tc_gemm_q8_planes: gated residual needs a gate");
+  CV3_REQUIRE(n % BN == 0 && k % KG == 0, CV3_ERR_VALUE, "tc_gemm_q8_planes: N a multiple of %d and K of %d", BN,
+              KG);
+  CV3_REQUIRE(lde >= m && lde % 16 == 0 && exps != nullptr, CV3_ERR_VALUE,
+              "tc_gemm_q8_planes: exponents [k/64][lde], lde >= m and a multiple of 16");
+  CV3_REQUIRE(mode == 4 ? (out_planes && out_exps && out_lde >= m && out_lde % 16 == 0 &&
+                           ((uintptr_t)out_planes & 15) == 0)
+                        : ldc >= n,
+              CV3_ERR_VALUE, "tc_gemm_q8_planes: output (mode 4: planes [m][2n] and exponents [n/64][out_lde])");
+  if (m == 0 || n == 0) return CV3_OK;
+  CV3_REQUIRE(k > 0 && m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 30), CV3_ERR_VALUE, "tc_gemm_q8_planes: sizes");
+  CUtensorMap ma;
+  int rc = map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, planes, m, 2 * k, 2 * k, KG, BM,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  CV3_REQUIRE(((uintptr_t)scales_t & 15) == 0, CV3_ERR_VALUE, "tc_gemm_q8: 16-byte aligned scales");
-  rc = cv3::allow_smem((const void*)tc_gemm_q8_kernel, SMEM_BYTES);
-  if (rc) return rc;
-  const int64_t ntiles = (n / BN) * ((m + BM - 1) / BM);
-  CV3_REQUIRE(ntiles < (1LL << 31), CV3_ERR_VALUE, "tc_gemm_q8: too many tiles");
-  const int grid = (int)std::min<int64_t>(ntiles, cv3::sm_count());
-  Epi ep{mode, bias, gate, rows_per_group, gate_stride};
-  tc_gemm_q8_kernel<<<grid, THREADS, SMEM_BYTES, cv3::as_stream(stream)>>>(ma, mb, scales_t, (int)m, (int)n, (int)k,
-                                                                          c, ldc, ep);
-  return cv3::check_launch("tc_gemm_q8");
+  Epi ep{mode, bias, gate, rows_per_group, gate_stride, static_cast<__half*>(out_planes), out_exps, out_lde};
+  return launch_q8(true, ma, w16, scales_t, exps, lde, c, ldc, m, n, k, ep, stream);
+}
+
+extern "C" int cv3_q8_split_rows(const float* x, int64_t ldx, int64_t rows, int64_t k, void* planes, int8_t* exps,
+                                 int64_t lde, void* stream) {
+  CV3_REQUIRE(rows >= 0 && k > 0 && k % KG == 0 && ldx >= k && ldx % 2 == 0 && lde >= rows && lde % 16 == 0,
+              CV3_ERR_VALUE, "q8_split_rows: K a multiple of 64, lde >= rows and a multiple of 16");
+  CV3_REQUIRE(((uintptr_t)x & 7) == 0 && ((uintptr_t)planes & 3) == 0, CV3_ERR_VALUE, "q8_split_rows: alignment");
+  if (rows == 0) return CV3_OK;
+  split_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, cv3::as_stream(stream)>>>(
+      x, ldx, rows, (int)k, static_cast<__half*>(planes), exps, lde);
+  return cv3::check_launch("q8_split_rows");
 }
 
 extern "C" int cv3_tc_gemm_q8_status(int* code) {

@@ -115,6 +115,15 @@ class LinQ8:
             raise ValueError("tensor-core linear adds the residual in place (residual must alias y)")
         self.tc(x, m, y, 3 if residual is not None else 0, ldx=ldx, ldy=ldy, stream=stream)
 
+    def tc_planes(self, planes: int, exps: int, lde: int, m: int, y: int, mode: int, gate: int = None,
+                  rows_per_group: int = 0, gate_stride: int = 0, stream=None, out_planes: int = None,
+                  out_exps: int = None, out_lde: int = 0):
+        """cv3_tc_gemm_q8_planes: x given as activation planes; modes as tc, plus 4 (GELU-tanh
+        written as activation planes to out_planes / out_exps)."""
+        s = stream if stream is not None else D.stream()
+        call("cv3_tc_gemm_q8_planes", planes, exps, lde, self.w16.data_ptr(), self.st.data_ptr(), y, self.n, m,
+             self.n, self.k, mode, self.bias, gate, rows_per_group, gate_stride, out_planes, out_exps, out_lde, s)
+
     def tc(self, x: int, m: int, y: int, mode: int, gate: int = None, rows_per_group: int = 0,
            gate_stride: int = 0, stream=None, ldx: int = None, ldy: int = None):
         """Fused epilogue as Lin.tc: 0 bias, 1 GELU-tanh, 2 gated residual into y, 3 residual into y."""

@@ -457,6 +457,33 @@ int cv3_tc_gemm_q8(const float* a, int64_t lda, const void* w16, const float* sc
                    int64_t m, int64_t n, int64_t k, int mode, const float* bias, const float* gate,
                    int64_t rows_per_group, int64_t gate_stride, void* stream);
 
+/* Activation planes (cv3_tc_gemm_q8_planes' A operand and mode-4 output): an fp32
+ * matrix X[m][k] (k % 64 == 0) as planes fp16 [m][2k] -- per row and 64-wide group g,
+ * hi = fp16(x * 2^e) at columns 128g..128g+63 and lo = fp16(x * 2^e - hi) at
+ * 128g+64..128g+127 -- and exps int8 [k/64][lde] (lde >= m, a multiple of 16), e
+ * bringing the group's max |x| into [2^14, 2^15): 22 significant bits per value,
+ * the fp32 matrix's bytes.  No counterpart in the reference (an operand format). */
+
+/* cv3_tc_gemm_q8 with A given as activation planes (read by TMA, no conversion in
+ * the GEMM).  Modes 0-3 as cv3_tc_gemm_q8 into c; mode 4: GELU-tanh(+bias)
+ * written as activation planes (out_planes [m][2n], out_exps [n/64][out_lde]) --
+ * the DiT feed-forward's first linear feeding the second (cv3cpu/models/dit.py:
+ * 131-142). */
+int cv3_tc_gemm_q8_planes(const void* planes, const int8_t* exps, int64_t lde, const void* w16,
+                          const float* scales_t, float* c, int64_t ldc, int64_t m, int64_t n, int64_t k, int mode,
+                          const float* bias, const float* gate, int64_t rows_per_group, int64_t gate_stride,
+                          void* out_planes, int8_t* out_exps, int64_t out_lde, void* stream);
+
+/* fp32 rows x [rows][ldx] -> activation planes (k % 64 == 0). */
+int cv3_q8_split_rows(const float* x, int64_t ldx, int64_t rows, int64_t k, void* planes, int8_t* exps,
+                      int64_t lde, void* stream);
+
+/* cv3_ln_modulate (dit.py:162-169 AdaLN: LayerNorm without affine, * (1 + scale) +
+ * shift) writing activation planes instead of fp32; dim 512 or 1024. */
+int cv3_ln_modulate_planes(const float* h, int64_t rows, int64_t dim, float eps, const float* scale,
+                           const float* shift, int64_t rows_per_group, int64_t mod_stride, void* planes,
+                           int8_t* exps, int64_t lde, void* stream);
+
 /* The operands cv3_tc_gemm_q8 reads, from a q8 matrix (quant.py:90-136 layout,
  * int8 [n][k] with k % 64 == 0, fp16 scales [n][k/64]): w16 fp16 [n][k] (exact)
  * and scales_t fp32 [k/64][n]. */

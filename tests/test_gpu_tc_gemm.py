@@ -179,3 +179,135 @@ def test_q8_gemm_epilogues(mode):
     elif mode == 3:
         y = c0 + y
     assert rel_err(got, y) < 1e-5
+
+
+# ---------------------------------------------------------------------------
+# activation planes: split, the planes GEMM, GELU written as planes, LN as planes
+# ---------------------------------------------------------------------------
+
+def _planes_of(x):
+    """Device activation planes of a host fp32 matrix (cv3_q8_split_rows)."""
+    import torch
+    L = pkg("_lib")
+    m, k = x.shape
+    lde = -(-m // 16) * 16
+    xd = torch.from_numpy(x).cuda()
+    pl = torch.empty((m, 2 * k), dtype=torch.float16, device="cuda")
+    ex = torch.empty((k // 64, lde), dtype=torch.int8, device="cuda")
+    L.call("cv3_q8_split_rows", xd.data_ptr(), k, m, k, pl.data_ptr(), ex.data_ptr(), lde,
+           torch.cuda.current_stream().cuda_stream)
+    return pl, ex, lde
+
+
+def _unplanes(pl, ex, m, k):
+    """fp64 values the planes carry: (hi + lo) * 2^-e."""
+    p = pl.cpu().numpy().astype(np.float64).reshape(m, k // 64, 2, 64)
+    e = ex.cpu().numpy()[:, :m].astype(np.float64).T          # [m][k/64]
+    return ((p[:, :, 0] + p[:, :, 1]) * np.exp2(-e)[:, :, None]).reshape(m, k)
+
+
+def _w16(w):
+    import torch
+    L = pkg("_lib")
+    qt = pkg("quant").make_qtensor(w)
+    n, k = w.shape
+    qd, sd = torch.from_numpy(qt.q).cuda(), torch.from_numpy(qt.scales.view(np.uint16)).cuda()
+    w16 = torch.empty((n, k), dtype=torch.float16, device="cuda")
+    stt = torch.empty((k // 64, n), dtype=torch.float32, device="cuda")
+    L.call("cv3_q8_gemm_prepare", qd.data_ptr(), sd.data_ptr(), n, k, w16.data_ptr(), stt.data_ptr(),
+           torch.cuda.current_stream().cuda_stream)
+    wd = qt.q.astype(np.float64) * np.repeat(qt.scales.astype(np.float64), 64, axis=1)[:, :k]
+    return w16, stt, wd
+
+
+def test_split_rows_carries_22_bits():
+    import torch
+    rng = np.random.default_rng(1)
+    x = (rng.normal(size=(37, 256)) * np.exp(rng.normal(size=(37, 1)) * 4)).astype(np.float32)
+    x[3, :64] = 0.0
+    pl, ex, lde = _planes_of(x)
+    torch.cuda.synchronize()
+    back = _unplanes(pl, ex, 37, 256)
+    assert np.all(np.abs(back - x) <= np.abs(x) * 2.0 ** -21 + 1e-30)
+
+
+@pytest.mark.parametrize("m,n,k,mode", [(300, 256, 1024, 0), (10400, 2048, 1024, 0), (650, 1024, 2048, 2),
+                                        (650, 1024, 1024, 3), (129, 128, 64, 0)])
+def test_q8_planes_gemm_matches_fp64(m, n, k, mode):
+    import torch
+    L = pkg("_lib")
+    rng = np.random.default_rng(m + k + mode)
+    a = rng.normal(size=(m, k)).astype(np.float32)
+    a[: m // 4] *= 30.0
+    w = (rng.normal(size=(n, k)) * 0.02).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    gate = rng.normal(size=(2, n)).astype(np.float32)
+    c0 = rng.normal(size=(m, n)).astype(np.float32)
+    pl, ex, lde = _planes_of(a)
+    w16, stt, wd = _w16(w)
+    c = torch.from_numpy(c0.copy()).cuda()
+    gg = torch.from_numpy(gate).cuda()
+    bb = torch.from_numpy(bias).cuda()
+    L.call("cv3_tc_gemm_q8_planes", pl.data_ptr(), ex.data_ptr(), lde, w16.data_ptr(), stt.data_ptr(), c.data_ptr(),
+           n, m, n, k, mode, bb.data_ptr(), gg.data_ptr() if mode == 2 else None, 400 if mode == 2 else 0,
+           n if mode == 2 else 0, None, None, 0, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    code = ctypes.c_int()
+    L.call("cv3_tc_gemm_q8_status", ctypes.byref(code))
+    assert code.value == 0
+    y = a.astype(np.float64) @ wd.T + bias
+    if mode == 2:
+        y = c0 + gate[np.arange(m) // 400] * y
+    elif mode == 3:
+        y = c0 + y
+    assert rel_err(c.cpu().numpy(), y) < 1e-5
+
+
+def test_q8_planes_gelu_chain_matches_fp64():
+    """ff1 with GELU written as planes (mode 4), then ff2 reading them: the DiT feed-forward."""
+    import torch
+    L = pkg("_lib")
+    rng = np.random.default_rng(5)
+    m, d, f = 650, 1024, 2048
+    a = rng.normal(size=(m, d)).astype(np.float32)
+    w1 = (rng.normal(size=(f, d)) * 0.03).astype(np.float32)
+    w2 = (rng.normal(size=(d, f)) * 0.03).astype(np.float32)
+    b1 = rng.normal(size=f).astype(np.float32)
+    pl, ex, lde = _planes_of(a)
+    w16a, sta, wd1 = _w16(w1)
+    w16b, stb, wd2 = _w16(w2)
+    st = torch.cuda.current_stream().cuda_stream
+    pl2 = torch.empty((m, 2 * f), dtype=torch.float16, device="cuda")
+    ex2 = torch.empty((f // 64, lde), dtype=torch.int8, device="cuda")
+    bb = torch.from_numpy(b1).cuda()
+    L.call("cv3_tc_gemm_q8_planes", pl.data_ptr(), ex.data_ptr(), lde, w16a.data_ptr(), sta.data_ptr(), None, 0,
+           m, f, d, 4, bb.data_ptr(), None, 0, 0, pl2.data_ptr(), ex2.data_ptr(), lde, st)
+    c = torch.zeros((m, d), device="cuda")
+    L.call("cv3_tc_gemm_q8_planes", pl2.data_ptr(), ex2.data_ptr(), lde, w16b.data_ptr(), stb.data_ptr(),
+           c.data_ptr(), d, m, d, f, 0, None, None, 0, 0, None, None, 0, st)
+    torch.cuda.synchronize()
+    h = _gelu(a.astype(np.float64) @ wd1.T + b1)
+    assert rel_err(_unplanes(pl2, ex2, m, f), h) < 1e-5
+    assert rel_err(c.cpu().numpy(), h @ wd2.T) < 1e-5
+
+
+def test_ln_modulate_planes_match_fp32():
+    import torch
+    L = pkg("_lib")
+    rng = np.random.default_rng(9)
+    rows, d = 300, 1024
+    h = (rng.normal(size=(rows, d)) * 3 + 1).astype(np.float32)
+    mods = rng.normal(size=(2, 2 * d)).astype(np.float32) * 0.3
+    hd, md = torch.from_numpy(h).cuda(), torch.from_numpy(mods).cuda()
+    st = torch.cuda.current_stream().cuda_stream
+    y = torch.empty((rows, d), device="cuda")
+    sc, sh = md.data_ptr(), md.data_ptr() + d * 4
+    L.call("cv3_ln_modulate", hd.data_ptr(), rows, d, 1e-6, sc, sh, 160, 2 * d, y.data_ptr(), st)
+    lde = 304
+    pl = torch.empty((rows, 2 * d), dtype=torch.float16, device="cuda")
+    ex = torch.empty((d // 64, lde), dtype=torch.int8, device="cuda")
+    L.call("cv3_ln_modulate_planes", hd.data_ptr(), rows, d, 1e-6, sc, sh, 160, 2 * d, pl.data_ptr(), ex.data_ptr(),
+           lde, st)
+    torch.cuda.synchronize()
+    ref = y.cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(_unplanes(pl, ex, rows, d) - ref) <= np.abs(ref) * 2.0 ** -21 + 1e-30)
