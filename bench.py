@@ -408,34 +408,57 @@ def measure_strong(tts, meta, rank: int, world: int, reps: int, barrier):
 def dominant_kernel_roofline(tts, peaks):
     """Time the DiT FF1 GEMM at the bench shape in isolation (the largest kernel of the
     step) with CUDA events on its launching stream; achieved = 2*M*N*K / time.  In the
-    balanced profile it is cv3_tc_gemm_q8 (int8 weights as stored, activations as two fp16
-    parts: two fp16 MMAs per fp32 product)."""
+    balanced profile it is cv3_tc_gemm_q8_planes as the step runs it: int8 weights as
+    stored, the activations as fp16 hi/lo planes (two fp16 MMAs per fp32 product), GELU
+    written back as planes for FF2."""
     import torch
+    L = pkg("_lib")
     dit = tts.flow.estimator
     dit.prepare()
     M = 2 * UTTS * 2 * (PROMPT_TOKENS + TOKENS)
     blk = dit.blocks[0].ff1
     q8 = type(blk).__name__ == "LinQ8"
-    x = torch.randn(M, blk.k, device="cuda")
-    y = torch.empty(M, blk.n, device="cuda")
+    planes = q8 and dit.q8_planes
     st = torch.cuda.current_stream()
+    x = torch.randn(M, blk.k, device="cuda")
+    if planes:
+        lde = (M + 15) // 16 * 16
+        xp = torch.empty(M, 2 * blk.k, dtype=torch.float16, device="cuda")
+        xe = torch.empty(blk.k // 64, lde, dtype=torch.int8, device="cuda")
+        yp = torch.empty(M, 2 * blk.n, dtype=torch.float16, device="cuda")
+        ye = torch.empty(blk.n // 64, lde, dtype=torch.int8, device="cuda")
+        L.call("cv3_q8_split_rows", x.data_ptr(), blk.k, M, blk.k, xp.data_ptr(), xe.data_ptr(), lde, st.cuda_stream)
+
+        def launch():
+            blk.tc_planes(xp.data_ptr(), xe.data_ptr(), lde, M, None, 4, stream=st.cuda_stream,
+                          out_planes=yp.data_ptr(), out_exps=ye.data_ptr(), out_lde=lde)
+    else:
+        y = torch.empty(M, blk.n, device="cuda")
+
+        def launch():
+            blk(x.data_ptr(), M, y.data_ptr(), stream=st.cuda_stream)
     for _ in range(3):
-        blk(x.data_ptr(), M, y.data_ptr(), stream=st.cuda_stream)
+        launch()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 20
     torch.cuda.synchronize()
     e0.record(st)
     for _ in range(reps):
-        blk(x.data_ptr(), M, y.data_ptr(), stream=st.cuda_stream)
+        launch()
     e1.record(st)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
     flops = 2.0 * M * blk.n * blk.k
     achieved = flops / (ms * 1e-3) / 1e12
     peak = peaks.get("bf16_tflops")
-    name = ("DiT ff1 GEMM (M=%d, N=%d, K=%d), int8 weights x fp32 activations as 2 fp16 parts (cv3_tc_gemm_q8)"
-            if q8 else "DiT ff1 GEMM (M=%d, N=%d, K=%d, fp32 via 3xTF32)") % (M, blk.n, blk.k)
-    return {"kernel": name, "bound": "tensor",
+    if planes:
+        name = ("DiT ff1 GEMM (M=%d, N=%d, K=%d), int8 weights x activation planes (2 fp16 parts), "
+                "GELU out as planes (cv3_tc_gemm_q8_planes mode 4)")
+    elif q8:
+        name = "DiT ff1 GEMM (M=%d, N=%d, K=%d), int8 weights x fp32 activations split in the GEMM (cv3_tc_gemm_q8)"
+    else:
+        name = "DiT ff1 GEMM (M=%d, N=%d, K=%d, fp32 via 3xTF32)"
+    return {"kernel": name % (M, blk.n, blk.k), "bound": "tensor",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
             "peak_source": "measured bf16 dense (MEASURED_PEAKS.json, burst)",
             "avg_launch_ms": ms,

@@ -61,6 +61,20 @@ class Workspace:
         self.f1 = D.empty((R, ff))
         self.c2 = D.empty((B, dim, N))
         self.out = D.empty((R, mel))
+        self.dim, self.ff = dim, ff
+        self.zp = None
+
+    def planes(self):
+        """Activation-plane buffers of the q8 GEMMs (fp16 [R][2k] + int8 exponents [k/64][lde]):
+        zp/ze for the normalised rows and the attention output, fp/fe for the GELU output."""
+        if self.zp is None:
+            R = self.R
+            self.lde = (R + 15) // 16 * 16
+            self.zp = torch.empty((R, 2 * self.dim), dtype=torch.float16, device="cuda")
+            self.ze = torch.empty((self.dim // 64, self.lde), dtype=torch.int8, device="cuda")
+            self.fp = torch.empty((R, 2 * self.ff), dtype=torch.float16, device="cuda")
+            self.fe = torch.empty((self.ff // 64, self.lde), dtype=torch.int8, device="cuda")
+        return self
 
 
 class DiT:
@@ -85,6 +99,9 @@ class DiT:
         # False dequantises them to fp32 for the 3xTF32 GEMM instead (the same results
         # within fp32 rounding; kept for comparisons)
         self.q8_gemm = True
+        # with q8_gemm: the GEMM operands as activation planes made by the producing kernels
+        # (False splits fp32 rows inside each GEMM instead)
+        self.q8_planes = True
 
     def _q8_ok(self, name) -> bool:
         t = self.w.host_tensor(self.p + name) if hasattr(self.w, "host_tensor") else None
@@ -160,7 +177,10 @@ class DiT:
         key = (B, N)
         if key not in self._ws:
             self.prepare()
-            self._ws[key] = Workspace(B, N, self.dim, self.ff)
+            ws = Workspace(B, N, self.dim, self.ff)
+            if self.q8_planes and isinstance(self.blocks[0].qkv, LinQ8) and ws.R >= TC_MIN_ROWS:
+                ws.planes()  # before any graph capture reuses the workspace
+            self._ws[key] = ws
         return self._ws[key]
 
     # -- pieces ------------------------------------------------------------------
@@ -196,6 +216,10 @@ class DiT:
         for i, blk in enumerate(self.blocks):
             base = mp + i * 6 * d * F
             sh_a, sc_a, g_a, sh_f, sc_f, g_f = (base + j * d * F for j in range(6))
+            if R >= TC_MIN_ROWS and isinstance(blk.qkv, LinQ8) and self.q8_planes:
+                self._block_planes(ws.planes(), blk, rows_per_group, (sh_a, sc_a, g_a, sh_f, sc_f, g_f),
+                                   cos, sin, scale, (mk, ma, mb), st)
+                continue
             call("cv3_ln_modulate", ws.h.data_ptr(), R, d, 1e-6, sc_a, sh_a, rows_per_group, mw, ws.z.data_ptr(), st)
             blk.qkv(ws.z.data_ptr(), R, ws.qkv.data_ptr(), stream=st)
             call("cv3_partial_rope", ws.qkv.data_ptr(), R, 3 * d, d, N, hd, cos.data_ptr(), sin.data_ptr(), st)
@@ -222,6 +246,30 @@ class DiT:
         call("cv3_ln_modulate", ws.h.data_ptr(), R, d, 1e-6, base, base + d * F, rows_per_group, mw,
              ws.z.data_ptr(), st)
         self.proj_out(ws.z.data_ptr(), R, ws.out.data_ptr(), stream=st)
+
+    def _block_planes(self, ws: Workspace, blk, rows_per_group: int, mod, cos, sin, scale, mask, st):
+        """One transformer block (dit.py:171-185 DiTBlock) with every GEMM reading activation
+        planes: AdaLN and the attention output are split once into fp16 hi/lo planes, the
+        first feed-forward linear writes GELU(x) as planes for the second."""
+        d, R, N = self.dim, ws.R, ws.N
+        mw = self.mod_width
+        sh_a, sc_a, g_a, sh_f, sc_f, g_f = mod
+        H, hd = self.heads, self.dim_head
+        zp, ze, lde = ws.zp.data_ptr(), ws.ze.data_ptr(), ws.lde
+        call("cv3_ln_modulate_planes", ws.h.data_ptr(), R, d, 1e-6, sc_a, sh_a, rows_per_group, mw, zp, ze, lde, st)
+        blk.qkv.tc_planes(zp, ze, lde, R, ws.qkv.data_ptr(), 0, stream=st)
+        call("cv3_partial_rope", ws.qkv.data_ptr(), R, 3 * d, d, N, hd, cos.data_ptr(), sin.data_ptr(), st)
+        q = ws.qkv.data_ptr()
+        F = 4
+        call("cv3_attention", q, N * 3 * d, hd, 3 * d, q + d * F, N * 3 * d, hd, 3 * d,
+             q + 2 * d * F, N * 3 * d, hd, 3 * d, ws.a.data_ptr(), N * d, hd, d,
+             ws.B, H, H, N, N, hd, scale, mask[0], mask[1], mask[2], st)
+        call("cv3_q8_split_rows", ws.a.data_ptr(), d, R, d, zp, ze, lde, st)
+        blk.out.tc_planes(zp, ze, lde, R, ws.h.data_ptr(), 2, g_a, rows_per_group, mw, st)
+        call("cv3_ln_modulate_planes", ws.h.data_ptr(), R, d, 1e-6, sc_f, sh_f, rows_per_group, mw, zp, ze, lde, st)
+        fp, fe = ws.fp.data_ptr(), ws.fe.data_ptr()
+        blk.ff1.tc_planes(zp, ze, lde, R, None, 4, stream=st, out_planes=fp, out_exps=fe, out_lde=lde)
+        blk.ff2.tc_planes(fp, fe, lde, R, ws.h.data_ptr(), 2, g_f, rows_per_group, mw, st)
 
     # -- reference-compatible forward ----------------------------------------------
     def forward(self, x, mu, t, spks, cond, streaming: bool = False, seq_chunk: int = 512):

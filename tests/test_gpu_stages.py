@@ -106,7 +106,7 @@ def test_hift_full_geometry_snake_and_vocoder_length(small_weights):
 
 def test_balanced_dit_forward_full_size_q8_gemm_matches_oracle():
     """The released DiT geometry in the balanced profile: the block matrices run through
-    cv3_tc_gemm_q8 on the stored int8 weights; one forward at batch 2 x 128 frames
+    cv3_tc_gemm_q8_planes on the stored int8 weights; one forward at batch 2 x 128 frames
     against the oracle (which dequantises to fp32, as the reference's qmatmul does) at
     the fp32 bar, and the dequantised 3xTF32 path agrees as well."""
     W = pkg("synth").synthetic_weights("balanced", stages=("flow",))
@@ -121,6 +121,9 @@ def test_balanced_dit_forward_full_size_q8_gemm_matches_oracle():
     got = dev.forward(x, mu, t, spk, cond)
     ref = st.DiT(W, W.meta).forward(x, mu, t, spk, cond)
     assert rel_err(got, ref) < TOL
+    split = pkg("models.dit").DiT(_device(W))
+    split.q8_planes = False  # fp32 rows split inside each GEMM instead of activation planes
+    assert rel_err(split.forward(x, mu, t, spk, cond), ref) < TOL
     f32 = pkg("models.dit").DiT(_device(W))
     f32.q8_gemm = False
     assert rel_err(f32.forward(x, mu, t, spk, cond), ref) < TOL
