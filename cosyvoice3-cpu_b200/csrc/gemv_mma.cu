@@ -19,15 +19,25 @@
 // and every (8 / RT)-th scale group); all of a warp's weight loads are issued
 // first, with the epilogue's bias and the RMSNorm weight (constants); after
 // the dependency wait the residual is read at once and the activations are
-// copied to shared memory asynchronously (cp.async: every 16-byte piece in
-// flight at once, no registers); RMSNorm is applied there by one warp per
-// sequence, and the warps' partial sums are added in a fixed order in shared
-// memory (deterministic).  Epilogues: bias, residual add
+// copied to shared memory by one bulk copy per row (few large L2 requests: every
+// CTA reads the same rows), completing on an mbarrier.  A fused RMSNorm
+// (qwen2.py:145-150: (x * r) * w) is folded: the MMAs take x * w, each warp adds
+// up x^2 for the groups it multiplies, and the row factor r multiplies the
+// finished dot product -- no separate pass over x; the results differ from
+// normalising first by fp32 rounding only.  The warps' partial sums are added in
+// a fixed order in shared memory (deterministic).  Epilogues: bias, residual add
 // (y may alias it), SwiGLU of interleaved gate/up rows (cv3cpu/models/qwen2.py:
 // 155-177, llm.py:74-78).
-#include "common.cuh"
+#include "tc_common.cuh"
+
+__device__ int g_gemv_err = 0;  // 1: an activation copy did not land in time (cv3_decode_gemv_status)
 
 namespace {
+
+using cv3tc::bulk_load;
+using cv3tc::mbar_expect_tx;
+using cv3tc::mbar_init;
+using cv3tc::mbar_wait;
 
 constexpr int NWARP = 8, MAXB = 8;
 
@@ -124,59 +134,38 @@ q8_gemv_mma_kernel(MmaArgs a) {
   const float bias_v = (epi && a.bias) ? a.bias[row] : 0.f;
   const float bias_u = (epi && a.bias && a.swiglu && row + 1 < a.n) ? a.bias[row + 1] : 0.f;
 
+  // rows >= m read as zeros; the barrier of the activation copies
+  __shared__ __align__(8) uint64_t xbar;
+  for (int i = tid; i < (MAXB - a.m) * k4; i += NWARP * 32)
+    reinterpret_cast<float4*>(xs + a.m * kw)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (tid == 0) {
+    mbar_init(&xbar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");  // the RMSNorm weight
+  __syncthreads();
+
   // everything below reads what the previous kernels wrote
   dep_wait();
   dep_release();
-  // the residual row is read now, so that its latency hides behind the staging and math
+  if (tid == 0) {
+    mbar_expect_tx(&xbar, (uint32_t)(a.m * kw * 4));
+    for (int mr = 0; mr < a.m; ++mr)
+      bulk_load(xs + mr * kw, a.x + (int64_t)mr * a.ldx + 64 * g0, (uint32_t)(kw * 4), &xbar);
+  }
+  // the residual row is read now, so that its latency hides behind the copies and math
   // (y may alias it: each element is read and written by this same thread only)
   const float res_v = (epi && !a.swiglu && a.residual) ? a.residual[(int64_t)bb * a.ldy + row] : 0.f;
-
-  // -- stage x asynchronously (all pieces in flight at once), optional RMSNorm -----------
-  for (int i = tid; i < MAXB * k4; i += NWARP * 32) {
-    const int mr = i / k4;
-    float4* dst = reinterpret_cast<float4*>(xs) + i;
-    if (mr < a.m) {
-      const float* src = a.x + (int64_t)mr * a.ldx + 64 * g0 + 4 * (i - mr * k4);
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-                   "l"(src)
-                   : "memory");
-    } else {
-      *dst = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
-  if (a.norm_w) {
-    // RMSNorm, one warp per sequence: the statistic, then (x * r) * w in place, rounded
-    // as ops.rms_norm (not split: kw == k)
-    if (warp < a.m) {
-      float4* xr = reinterpret_cast<float4*>(xs + warp * kw);
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int cc = lane; cc < k4; cc += 32) {
-        const float4 v = xr[cc];
-        s4[0] += v.x * v.x;
-        s4[1] += v.y * v.y;
-        s4[2] += v.z * v.z;
-        s4[3] += v.w * v.w;
-      }
-      const float ssum = warp_sum((s4[0] + s4[1]) + (s4[2] + s4[3]));
-      const float r = 1.0f / sqrtf(ssum / (float)a.k + a.eps);
-      const float4* wr = reinterpret_cast<const float4*>(nws);
-      for (int cc = lane; cc < k4; cc += 32) {
-        const float4 w4 = wr[cc];
-        float4 v = xr[cc];
-        v.x = (v.x * r) * w4.x;
-        v.y = (v.y * r) * w4.y;
-        v.z = (v.z * r) * w4.z;
-        v.w = (v.w * r) * w4.w;
-        xr[cc] = v;
-      }
-    }
-    __syncthreads();
+  const bool landed = mbar_wait(&xbar, 0, &g_gemv_err, 1);
+  if (!__syncthreads_and(landed)) {
+    // a copy that never lands: once more (bounded) before the CTA's shared memory goes
+    if (tid == 0 && !landed) mbar_wait(&xbar, 0, &g_gemv_err, 1);
+    return;
   }
 
   // -- per scale group: 4 k-steps x 3 activation parts = 12 MMAs, then * scale ------------
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float ssq = 0.f;  // sum of x^2 of sequence g over this lane's columns (RMSNorm)
 #pragma unroll
   for (int i = 0; i < GMAX; ++i) {
     const int G = gw + GSTEP * i;
@@ -190,6 +179,20 @@ q8_gemv_mma_kernel(MmaArgs a) {
         xv[4 * v + 1] = t.y;
         xv[4 * v + 2] = t.z;
         xv[4 * v + 3] = t.w;
+      }
+      if (a.norm_w) {
+        // RMSNorm folded: sum of squares of x, then x * w into the MMAs
+        const float4* wp = reinterpret_cast<const float4*>(nws + 64 * G + 16 * c);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float4 w4 = wp[v];
+          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            ssq = fmaf(xv[4 * v + e], xv[4 * v + e], ssq);
+            xv[4 * v + e] *= wv[e];
+          }
+        }
       }
       // x = hi + mid + lo exactly: hi = x truncated to bf16, mid = the remainder
       // truncated, lo = what is left (<= 8 significant bits, itself a bf16 value)
@@ -226,6 +229,13 @@ q8_gemv_mma_kernel(MmaArgs a) {
       }
     }
   }
+  // the row tile-0 warps together cover every column once: their sums of squares
+  __shared__ float sq[GSTEP][MAXB];
+  if (a.norm_w) {
+    ssq += __shfl_xor_sync(0xffffffffu, ssq, 1);
+    ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
+    if (tile == 0 && c == 0) sq[gw][g] = ssq;
+  }
   // D fragment: rows g / g+8 of the warp's tile, sequences 2c, 2c+1
   red[warp][g][2 * c] = acc[0];
   red[warp][g][2 * c + 1] = acc[1];
@@ -235,6 +245,7 @@ q8_gemv_mma_kernel(MmaArgs a) {
 
   // -- reduce the warps of each tile in a fixed order, then the K splits ---------------------
   __shared__ float tot[16 * RT][MAXB];
+  __shared__ float rnorm[MAXB];
   __shared__ int last_cta;
   if (tid < ROWS * MAXB) {
     const int tl = rt / 16, rr = rt % 16;
@@ -242,6 +253,12 @@ q8_gemv_mma_kernel(MmaArgs a) {
 #pragma unroll
     for (int w = 0; w < GSTEP; ++w) v += red[tl + RT * w][rr][bb];
     tot[rt][bb] = v;
+  }
+  if (a.norm_w && tid < MAXB) {
+    float q = 0.f;
+#pragma unroll
+    for (int w = 0; w < GSTEP; ++w) q += sq[w][tid];
+    rnorm[tid] = 1.0f / sqrtf(q / (float)a.k + a.eps);
   }
   if (gridDim.y > 1 && a.cluster) {
     // the K splits of this row tile are one cluster: split 0 adds the others' sums from
@@ -284,12 +301,13 @@ q8_gemv_mma_kernel(MmaArgs a) {
   __syncthreads();
   if (tid < ROWS * MAXB) {
     const int rr = rt % 16;
-    float v = tot[rt][bb];
+    const float rn = a.norm_w ? rnorm[bb] : 1.f;
+    float v = tot[rt][bb] * rn;
     if (epi) {
       if (a.bias) v += bias_v;
       if (a.swiglu) {
         if ((rr & 1) == 0) {  // rows 2i (gate) and 2i+1 (up)
-          float up = tot[rt + 1][bb];
+          float up = tot[rt + 1][bb] * rn;
           if (a.bias) up += bias_u;
           a.y[(int64_t)bb * a.ldy + row / 2] = (v / (1.0f + expf(-v))) * up;
         }
@@ -302,6 +320,17 @@ q8_gemv_mma_kernel(MmaArgs a) {
 }
 
 }  // namespace
+
+extern "C" int cv3_decode_gemv_status(int* code) {
+  int v = 0;
+  CV3_CUDA(cudaMemcpyFromSymbol(&v, g_gemv_err, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    CV3_CUDA(cudaMemcpyToSymbol(g_gemv_err, &zero, sizeof(int)));
+  }
+  if (code) *code = v;
+  return 0;
+}
 
 extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
                                       const uint16_t* scales, int64_t n, int64_t kp, const float* bias,

@@ -99,6 +99,11 @@ int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int64_t ldx, co
                            const float* norm_w, float eps, int swiglu, float* y, int64_t ldy, int64_t splits,
                            float* workspace, int64_t workspace_floats, int* counters, void* stream);
 
+/* Error word of cv3_q8_decode_gemv_mma, read and cleared: 0, or 1 when a CTA's
+ * bulk copy of the activation rows did not land within 2 s (that CTA then wrote
+ * nothing).  No counterpart in the reference (a device-side wait bound). */
+int cv3_decode_gemv_status(int* code);
+
 /* Same contract for an fp32 weight W[n][k] (row stride ldw); replaces the
  * plain-array branch of cv3cpu/quant.py:165-170. fp32-exact SIMT math. */
 int cv3_f32_linear(const float* x, int64_t m, int64_t k, int64_t ldx,
