@@ -15,8 +15,8 @@
 // g+8 and activations 16c .. 16c+15 of sequence g: one 16-byte load per row per
 // group, straight into the MMA fragments.
 //
-// CTA = 16 x RT weight rows x all of K, 8 warps (warp w takes row tile w % RT
-// and every (8 / RT)-th scale group); all of a warp's weight loads are issued
+// CTA = 16 x RT weight rows x all of K, 8 warps (warp w takes every 8th scale
+// group, for all RT row tiles); all of a warp's weight loads are issued
 // first, with the epilogue's bias and the RMSNorm weight (constants); after
 // the dependency wait the residual is read at once and the activations are
 // copied to shared memory by one bulk copy per row (few large L2 requests: every
@@ -61,13 +61,15 @@ struct MmaArgs {
   int cluster;       // 1: the K splits of a row tile form one thread-block cluster
 };
 
-__device__ __forceinline__ void widen16(const int4 w, float f[16]) {
-  const uint32_t words[4] = {(uint32_t)w.x ^ 0x80808080u, (uint32_t)w.y ^ 0x80808080u,
-                             (uint32_t)w.z ^ 0x80808080u, (uint32_t)w.w ^ 0x80808080u};
+// the 4 int8 values of one 32-bit word of a weight fragment as floats (exact)
+__device__ __forceinline__ void widen4(uint32_t word, float f[4]) {
+  const uint32_t u = word ^ 0x80808080u;
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int b = 0; b < 4; ++b) f[4 * i + b] = __int_as_float(__byte_perm(words[i], 0x4B000000u, 0x7440u | b)) - 8388736.0f;
+  for (int b = 0; b < 4; ++b) f[b] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7440u | b)) - 8388736.0f;
+}
+
+__device__ __forceinline__ uint32_t word_of(const int4& v, int j) {
+  return (uint32_t)(j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w)));
 }
 
 // two floats that are exact bf16 values (low 16 bits zero) as one bf16x2
@@ -87,36 +89,38 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// RT: 16-row tiles per CTA; GMAX: most scale groups one warp takes
-// (K <= 64 * (NWARP / RT) * GMAX)
+// RT: 16-row tiles per CTA, every warp multiplying its scale groups into all of them
+// (the activation split is done once per group and CTA); GMAX: most scale groups one
+// warp takes (K <= 64 * NWARP * GMAX)
 template <int RT, int GMAX>
 __global__ void __launch_bounds__(NWARP * 32, GMAX <= 4 ? 3 : 1)  // short K: 3 CTAs per SM (9728 rows in one wave)
 q8_gemv_mma_kernel(MmaArgs a) {
-  constexpr int ROWS = 16 * RT, GSTEP = NWARP / RT;
-  extern __shared__ float xs[];  // [MAXB][k] staged (and normalised) activations, rows >= m zero
-  __shared__ float red[NWARP][16][MAXB];
+  constexpr int ROWS = 16 * RT;
+  extern __shared__ float xs[];  // [MAXB][k] staged activations, rows >= m zero
+  __shared__ float red[NWARP][ROWS][MAXB];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int tile = warp % RT, gw = warp / RT;
-  const int row0 = blockIdx.x * ROWS + 16 * tile;
   const int ks = a.k >> 6;
   // this CTA's K split: scale groups [g0, g0 + ng); x columns [64 g0, 64 (g0 + ng))
   const int g0 = blockIdx.y * a.gsplit;
   const int ng = min(a.gsplit, ks - g0);
   const int kw = 64 * ng;  // staged row width
-  const int r0 = min(row0 + g, a.n - 1), r1 = min(row0 + g + 8, a.n - 1);
 
   // -- weights first: they do not depend on x --------------------------------------------
-  int4 w0[GMAX], w1[GMAX];
-  float s0[GMAX], s1[GMAX];
+  int4 w0[GMAX][RT], w1[GMAX][RT];
+  float s0[GMAX][RT], s1[GMAX][RT];
 #pragma unroll
   for (int i = 0; i < GMAX; ++i) {
-    const int G = gw + GSTEP * i;
+    const int G = warp + NWARP * i;
     const bool in = G < ng;
-    w0[i] = in ? ld_stream16(a.q + (int64_t)r0 * a.k + 64 * (g0 + G) + 16 * c) : make_int4(0, 0, 0, 0);
-    w1[i] = in ? ld_stream16(a.q + (int64_t)r1 * a.k + 64 * (g0 + G) + 16 * c) : make_int4(0, 0, 0, 0);
-    s0[i] = in ? h2f(a.sc[(int64_t)r0 * ks + g0 + G]) : 0.f;
-    s1[i] = in ? h2f(a.sc[(int64_t)r1 * ks + g0 + G]) : 0.f;
+#pragma unroll
+    for (int t = 0; t < RT; ++t) {
+      const int r0 = min(blockIdx.x * ROWS + 16 * t + g, a.n - 1), r1 = min(blockIdx.x * ROWS + 16 * t + g + 8, a.n - 1);
+      w0[i][t] = in ? ld_stream16(a.q + (int64_t)r0 * a.k + 64 * (g0 + G) + 16 * c) : make_int4(0, 0, 0, 0);
+      w1[i][t] = in ? ld_stream16(a.q + (int64_t)r1 * a.k + 64 * (g0 + G) + 16 * c) : make_int4(0, 0, 0, 0);
+      s0[i][t] = in ? h2f(a.sc[(int64_t)r0 * ks + g0 + G]) : 0.f;
+      s1[i][t] = in ? h2f(a.sc[(int64_t)r1 * ks + g0 + G]) : 0.f;
+    }
   }
 
   // constants of the epilogue and the RMSNorm weight (staged behind x) do not depend on
@@ -163,12 +167,14 @@ q8_gemv_mma_kernel(MmaArgs a) {
     return;
   }
 
-  // -- per scale group: 4 k-steps x 3 activation parts = 12 MMAs, then * scale ------------
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  // -- per scale group: 4 k-steps x 3 activation parts x RT tiles MMAs, then * scale -------
+  float acc[RT][4];
+#pragma unroll
+  for (int t = 0; t < RT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
   float ssq = 0.f;  // sum of x^2 of sequence g over this lane's columns (RMSNorm)
 #pragma unroll
   for (int i = 0; i < GMAX; ++i) {
-    const int G = gw + GSTEP * i;
+    const int G = warp + NWARP * i;
     if (G < ng) {
       float xv[16];
       const float4* xp = reinterpret_cast<const float4*>(xs + g * kw + 64 * G + 16 * c);
@@ -195,69 +201,82 @@ q8_gemv_mma_kernel(MmaArgs a) {
         }
       }
       // x = hi + mid + lo exactly: hi = x truncated to bf16, mid = the remainder
-      // truncated, lo = what is left (<= 8 significant bits, itself a bf16 value)
-      float part[3][16];
+      // truncated, lo = what is left (<= 8 significant bits, itself a bf16 value);
+      // packed once as the MMA's B fragments
+      uint32_t bp[3][4][2];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const float hi = bf16_trunc(xv[e]);
-        const float r1v = xv[e] - hi;
-        const float mid = bf16_trunc(r1v);
-        part[0][e] = hi;
-        part[1][e] = mid;
-        part[2][e] = bf16_trunc(r1v - mid);
-      }
-      float f0[16], f1[16];
-      widen16(w0[i], f0);
-      widen16(w1[i], f1);
-      // one accumulator chain per part (three independent MMA chains of four)
-      float t[3][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t A0 = pack(f0[4 * j], f0[4 * j + 1]);      // row g,     k 2c, 2c+1
-        const uint32_t A1 = pack(f1[4 * j], f1[4 * j + 1]);      // row g + 8, k 2c, 2c+1
-        const uint32_t A2 = pack(f0[4 * j + 2], f0[4 * j + 3]);  // row g,     k 2c+8, 2c+9
-        const uint32_t A3 = pack(f1[4 * j + 2], f1[4 * j + 3]);  // row g + 8, k 2c+8, 2c+9
+        for (int h = 0; h < 2; ++h) {
+          float pv[3][2];
 #pragma unroll
-        for (int pp = 0; pp < 3; ++pp)
-          mma_bf16(t[pp], A0, A1, A2, A3, pack(part[pp][4 * j], part[pp][4 * j + 1]),
-                   pack(part[pp][4 * j + 2], part[pp][4 * j + 3]));
-      }
+          for (int u = 0; u < 2; ++u) {
+            const float x = xv[4 * j + 2 * h + u];
+            const float hi = bf16_trunc(x);
+            const float r1v = x - hi;
+            const float mid = bf16_trunc(r1v);
+            pv[0][u] = hi;
+            pv[1][u] = mid;
+            pv[2][u] = bf16_trunc(r1v - mid);
+          }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float v = (t[2][e] + t[1][e]) + t[0][e];  // small parts first
-        acc[e] = fmaf(v, e < 2 ? s0[i] : s1[i], acc[e]);
+          for (int pp = 0; pp < 3; ++pp) bp[pp][j][h] = pack(pv[pp][0], pv[pp][1]);
+        }
+#pragma unroll
+      for (int t = 0; t < RT; ++t) {
+        // one accumulator chain per part (three independent MMA chains of four)
+        float d[3][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float f0[4], f1[4];
+          widen4(word_of(w0[i][t], j), f0);
+          widen4(word_of(w1[i][t], j), f1);
+          const uint32_t A0 = pack(f0[0], f0[1]);  // row g,     k 2c, 2c+1
+          const uint32_t A1 = pack(f1[0], f1[1]);  // row g + 8, k 2c, 2c+1
+          const uint32_t A2 = pack(f0[2], f0[3]);  // row g,     k 2c+8, 2c+9
+          const uint32_t A3 = pack(f1[2], f1[3]);  // row g + 8, k 2c+8, 2c+9
+#pragma unroll
+          for (int pp = 0; pp < 3; ++pp) mma_bf16(d[pp], A0, A1, A2, A3, bp[pp][j][0], bp[pp][j][1]);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float v = (d[2][e] + d[1][e]) + d[0][e];  // small parts first
+          acc[t][e] = fmaf(v, e < 2 ? s0[i][t] : s1[i][t], acc[t][e]);
+        }
       }
     }
   }
-  // the row tile-0 warps together cover every column once: their sums of squares
-  __shared__ float sq[GSTEP][MAXB];
+  // every column is in exactly one warp: the warps' sums of squares
+  __shared__ float sq[NWARP][MAXB];
   if (a.norm_w) {
     ssq += __shfl_xor_sync(0xffffffffu, ssq, 1);
     ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
-    if (tile == 0 && c == 0) sq[gw][g] = ssq;
+    if (c == 0) sq[warp][g] = ssq;
   }
-  // D fragment: rows g / g+8 of the warp's tile, sequences 2c, 2c+1
-  red[warp][g][2 * c] = acc[0];
-  red[warp][g][2 * c + 1] = acc[1];
-  red[warp][g + 8][2 * c] = acc[2];
-  red[warp][g + 8][2 * c + 1] = acc[3];
+  // D fragments: rows 16t + g / 16t + g + 8, sequences 2c, 2c+1
+#pragma unroll
+  for (int t = 0; t < RT; ++t) {
+    red[warp][16 * t + g][2 * c] = acc[t][0];
+    red[warp][16 * t + g][2 * c + 1] = acc[t][1];
+    red[warp][16 * t + g + 8][2 * c] = acc[t][2];
+    red[warp][16 * t + g + 8][2 * c + 1] = acc[t][3];
+  }
   __syncthreads();
 
-  // -- reduce the warps of each tile in a fixed order, then the K splits ---------------------
-  __shared__ float tot[16 * RT][MAXB];
+  // -- reduce the warps in a fixed order, then the K splits -----------------------------------
+  __shared__ float tot[ROWS][MAXB];
   __shared__ float rnorm[MAXB];
   __shared__ int last_cta;
   if (tid < ROWS * MAXB) {
-    const int tl = rt / 16, rr = rt % 16;
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < GSTEP; ++w) v += red[tl + RT * w][rr][bb];
+    for (int w = 0; w < NWARP; ++w) v += red[w][rt][bb];
     tot[rt][bb] = v;
   }
   if (a.norm_w && tid < MAXB) {
     float q = 0.f;
 #pragma unroll
-    for (int w = 0; w < GSTEP; ++w) q += sq[w][tid];
+    for (int w = 0; w < NWARP; ++w) q += sq[w][tid];
     rnorm[tid] = 1.0f / sqrtf(q / (float)a.k + a.eps);
   }
   if (gridDim.y > 1 && a.cluster) {
@@ -352,8 +371,8 @@ extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int6
   const int ngroups = (int)(k / 64);
   const int gsplit = (ngroups + (int)splits - 1) / (int)splits;
   const int nsplit = (ngroups + gsplit - 1) / gsplit;
-  // big matrices: 32-row CTAs (one wave on 148 SMs for 9728 rows); small ones 16
-  const bool wide = n >= 4096;
+  // big matrices with K <= 1024: 32-row CTAs (one wave on 148 SMs for 9728 rows); else 16
+  const bool wide = n >= 4096 && (ngroups + (int)splits - 1) / (int)splits <= NWARP * 2;
   const int rows = wide ? 32 : 16;
   const int tiles = (int)((n + rows - 1) / rows);
   if (nsplit > 1) {
@@ -368,8 +387,8 @@ extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int6
   dim3 grid((unsigned)tiles, (unsigned)nsplit);
   cudaStream_t st = cv3::as_stream(stream);
   void (*fn)(MmaArgs);
-  if (wide) fn = (gsplit <= 4 * 4) ? q8_gemv_mma_kernel<2, 4> : q8_gemv_mma_kernel<2, 20>;
-  else fn = (gsplit <= 8 * 2) ? q8_gemv_mma_kernel<1, 2> : q8_gemv_mma_kernel<1, 10>;
+  if (wide) fn = q8_gemv_mma_kernel<2, 2>;
+  else fn = (gsplit <= NWARP * 2) ? q8_gemv_mma_kernel<1, 2> : q8_gemv_mma_kernel<1, 10>;
   if (smem > 48 * 1024) {
     int rc = cv3::allow_smem((const void*)fn, smem);
     if (rc) return rc;

@@ -198,11 +198,12 @@ class DecodeGemv:
         # from 2 splits (112 CTAs instead of 56), 4 splits and the out projection lose.
         self.mma = self.kp == self.k and self.k % 64 == 0 and self.k <= 5120
         if self.mma:
-            tiles = -(-self.n // (32 if self.n >= 4096 else 16))
             groups = self.k // 64
             self.splits = max(1, min(int(mma_splits), groups)) if norm_w is None else 1
             gs = -(-groups // self.splits)
             eff = -(-groups // gs)
+            # the kernel's row tiles: 32 rows for n >= 4096 with <= 16 scale groups per CTA, else 16
+            tiles = -(-self.n // (32 if self.n >= 4096 and gs <= 16 else 16))
         else:
             tiles = -(-self.n // 32)
             self.splits = max(1, min(64, -(-target_ctas // tiles), self.kp // 64))

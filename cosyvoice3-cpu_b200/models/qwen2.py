@@ -307,7 +307,7 @@ class DecodeEngine:
                 self.fast.append((DecodeGemv(ws[0], L.qkv._keep[1], L.ln1, c.rms_norm_eps),
                                   DecodeGemv(ws[1]),
                                   DecodeGemv(gu, norm_w=L.ln2, eps=c.rms_norm_eps, swiglu=True),
-                                  DecodeGemv(ws[4], mma_splits=2)))
+                                  DecodeGemv(ws[4], mma_splits=5)))
             else:
                 self.fast.append(None)
         self.fast_head = DecodeGemv(head_w, norm_w=model.norm_w(), eps=c.rms_norm_eps) \

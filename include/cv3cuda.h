@@ -93,7 +93,8 @@ int cv3_q8_decode_gemv(const float* x, int64_t m, int64_t k, int64_t ldx, const 
  * padding (kp == k), K <= 5120, 16-byte aligned x rows.  `splits` > 1 (no
  * fused RMSNorm) spreads K over that many CTAs per row tile with a
  * deterministic reduction: workspace >= splits*n*8 floats and counters (one
- * per 16-row tile, or 32-row when n >= 4096) zeroed once, left zeroed. */
+ * per 16-row tile, or 32-row when n >= 4096 and a CTA takes at most 16 scale
+ * groups) zeroed once, left zeroed. */
 int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
                            const uint16_t* scales, int64_t n, int64_t kp, const float* bias, const float* residual,
                            const float* norm_w, float eps, int swiglu, float* y, int64_t ldy, int64_t splits,
