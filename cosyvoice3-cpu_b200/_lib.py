@@ -94,6 +94,7 @@ SIGNATURES = {
     "cv3_q8_decode_gemv": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
     "cv3_q8_decode_gemv_mma": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
     "cv3_decode_gemv_status": [P],
+    "cv3_decode_attention_status": [P],
 }
 _RESTYPE = {"cv3_last_error": ctypes.c_char_p, "cv3_launch_count": ctypes.c_ulonglong,
             "cv3_decode_sync_words": ctypes.c_int64}

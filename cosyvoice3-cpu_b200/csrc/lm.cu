@@ -7,9 +7,18 @@
 // KV cache layout: k/v [seq][kv_head][cap][head_dim] fp32 (cv3cpu/models/qwen2.py:74-121
 // keeps (kv_head, cap, head_dim) per layer; here all sequences of a batch are
 // stacked and the capacity is reserved up front).
-#include "common.cuh"
+#include <algorithm>
+
+#include "tc_common.cuh"
+
+__device__ int g_attn_err = 0;  // 1: a staged key/value copy did not land in time (cv3_decode_attention_status)
 
 namespace {
+
+using cv3tc::bulk_load;
+using cv3tc::mbar_expect_tx;
+using cv3tc::mbar_init;
+using cv3tc::mbar_wait;
 
 // rows r of qkv [R][(H + 2Hk) * D]: sequence seq[r] at position pos[r].
 // q -> qout[r][H][D] rotated; k rotated and v copied into the caches.
@@ -67,29 +76,61 @@ constexpr int PG = AT / 16;  // key groups of the V pass (16 lanes x float4 per 
 // from shared memory; the first CTA of the group also appends them to the cache.
 // So RoPE, the cache append and attention are one launch, and no CTA reads a
 // cache row another CTA of the launch writes.
+// STAGING (ROPE only): the cached rows [0, pos[b]) were written at earlier steps
+// and pos[b] three or more launches back, all complete before this launch's CTAs
+// start (every kernel of the chain releases its successor only after its own
+// dependency wait).  So before the wait, bulk copies bring up to `kmax` of those
+// key and value rows into shared memory, overlapping the qkv projection; after
+// the wait the position is read again and the staged rows are used only if it is
+// unchanged (else every row is read from global memory).  Staged keys are read
+// with the float4 columns rotated by the row index (conflict-free banks), which
+// changes only the order of a dot product's sums.
 template <bool ROPE>
 __global__ void __launch_bounds__(AT)
 decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ cosT,
                         const float* __restrict__ sinT, const int* __restrict__ pos, float* kc, float* vc,
                         const int* __restrict__ lens, int heads, int kv_heads, int64_t cap, float scale,
-                        float* __restrict__ out) {
-  extern __shared__ float sc[];  // [HC][cap] scores, then probabilities
+                        float* __restrict__ out, int kmax, int64_t kv_off) {
+  extern __shared__ float sc[];  // [HC][cap] scores, then probabilities; staged K, V rows at kv_off
   __shared__ float4 qs[HC][DM / 4];
   __shared__ float4 knew[DM / 4], vnew[DM / 4];
   __shared__ float4 part[PG][HC][DM / 4];
   __shared__ float stat[HC];
+  __shared__ __align__(8) uint64_t kvbar;
   const int g = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float* kb = kc + ((int64_t)b * kv_heads + g) * cap * DM;
+  const float* vb = vc + ((int64_t)b * kv_heads + g) * cap * DM;
+  float4* sk = reinterpret_cast<float4*>(sc + kv_off);  // [kmax][DM / 4]
+  float4* sv = sk + (int64_t)kmax * (DM / 4);
+  int ns = 0, p_pre = -1;  // rows staged in shared memory; the position they were staged for
+  if (ROPE && kmax > 0) {
+    p_pre = *(const volatile int*)(pos + b);
+    ns = (int)min((int64_t)min(max(p_pre, 0), kmax), cap);
+    if (tid == 0) {
+      mbar_init(&kvbar, 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      if (ns > 0) {
+        mbar_expect_tx(&kvbar, (uint32_t)(2 * ns * DM * 4));
+        constexpr int CH = 64;  // rows per copy (16 KB)
+        for (int r = 0; r < ns; r += CH) {
+          const uint32_t bytes = (uint32_t)(min(CH, ns - r) * DM * 4);
+          bulk_load(sk + (int64_t)r * (DM / 4), kb + (int64_t)r * DM, bytes, &kvbar);
+          bulk_load(sv + (int64_t)r * (DM / 4), vb + (int64_t)r * DM, bytes, &kvbar);
+        }
+      }
+    }
+  }
   if (threadIdx.x == 0) {
-    // Warm L2 with this (sequence, kv head)'s cached keys and values while the previous
-    // kernel still runs.  Only a hint: L2 is coherent, so even a stale length (read
-    // before the wait) cannot change what the loads below see; the range stays inside
-    // the cache rows of this (sequence, kv head).
-    const int64_t rows = min((int64_t)max(*(const volatile int*)(lens + b), 0), cap);
-    const uint32_t bytes = (uint32_t)(rows * DM * 4);
+    // Warm L2 with the cached rows that are not staged while the previous kernel still
+    // runs.  Only a hint: L2 is coherent, so even a stale length (read before the wait)
+    // cannot change what the loads below see; the range stays inside the cache rows of
+    // this (sequence, kv head).
+    const int64_t rows = min((int64_t)max(*(const volatile int*)(lens + b), 0), cap) - ns;
+    const uint32_t bytes = rows > 0 ? (uint32_t)(rows * DM * 4) : 0u;
     if (bytes >= 16) {
-      const int64_t base = ((int64_t)b * kv_heads + g) * cap * DM;
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kc + base), "r"(bytes) : "memory");
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vc + base), "r"(bytes) : "memory");
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kb + (int64_t)ns * DM), "r"(bytes) : "memory");
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vb + (int64_t)ns * DM), "r"(bytes) : "memory");
     }
   }
   dep_wait();
@@ -98,10 +139,10 @@ decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* _
   const int h0 = blockIdx.z * HC;            // this CTA's first query head within the group
   const int nh = min(HC, hpg - h0);          // >= 1: the grid covers ceil(hpg / HC) pairs
   const int m = (int)min((int64_t)lens[b], cap);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int pnew = -1;  // position whose key and value come from shared memory
   if (ROPE) {
     const int p = pos[b];
+    if (p != p_pre) ns = 0;  // not the position staged for: every row from global memory
     const bool in_cache = p >= 0 && p < cap;  // a position past the cache is not stored
     const int pt = in_cache ? p : 0;
     const float* row = q + (int64_t)b * ldq;
@@ -130,12 +171,21 @@ decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* _
       qs[h][c] = v;
     }
   }
-  __syncthreads();
-  const float* kb = kc + ((int64_t)b * kv_heads + g) * cap * DM;
-  const float* vb = vc + ((int64_t)b * kv_heads + g) * cap * DM;
+  // the staged rows (a copy issued before the wait lands even when it is not used)
+  bool landed = true;
+  if (ROPE && kmax > 0 && p_pre > 0 && min((int64_t)min(p_pre, kmax), cap) > 0) landed = mbar_wait(&kvbar, 0, &g_attn_err, 1);
+  if (!__syncthreads_and(landed)) {
+    if (tid == 0 && !landed) mbar_wait(&kvbar, 0, &g_attn_err, 1);  // once more (bounded) before leaving
+    return;
+  }
   for (int j = tid; j < m; j += AT) {
     float4 kr[DM / 4];
-    if (j == pnew) {
+    int rot = 0;  // staged rows: float4 column c of kr holds column (c + rot) % 16
+    if (j < ns) {
+      rot = j & (DM / 4 - 1);
+#pragma unroll
+      for (int c = 0; c < DM / 4; ++c) kr[c] = sk[(int64_t)j * (DM / 4) + ((c + rot) & (DM / 4 - 1))];
+    } else if (j == pnew) {
 #pragma unroll
       for (int c = 0; c < DM / 4; ++c) kr[c] = knew[c];
     } else {
@@ -149,7 +199,7 @@ decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* _
         float s = 0.f;
 #pragma unroll
         for (int c = 0; c < DM / 4; ++c) {
-          const float4 qq = qs[h][c];
+          const float4 qq = qs[h][(c + rot) & (DM / 4 - 1)];
           s = fmaf(qq.x, kr[c].x, s);
           s = fmaf(qq.y, kr[c].y, s);
           s = fmaf(qq.z, kr[c].z, s);
@@ -186,7 +236,8 @@ decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* _
     for (int u = 0; u < VU; ++u) {
       const int jj = j + u * PG;
       v[u] = jj >= m ? make_float4(0.f, 0.f, 0.f, 0.f)
-                     : (jj == pnew ? vnew[l] : reinterpret_cast<const float4*>(vb + (int64_t)jj * DM)[l]);
+                     : (jj < ns ? sv[(int64_t)jj * (DM / 4) + l]
+                                : (jj == pnew ? vnew[l] : reinterpret_cast<const float4*>(vb + (int64_t)jj * DM)[l]));
     }
 #pragma unroll
     for (int u = 0; u < VU; ++u) {
@@ -312,8 +363,12 @@ int launch_decode_attention(bool rope, const float* q, int64_t ldq, const float*
   CV3_REQUIRE(head_dim == DM, CV3_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (built for %d)",
               (long long)head_dim, DM);
   CV3_REQUIRE(heads / kv_heads <= HPG, CV3_ERR_UNSUPPORTED, "decode_attention: more than %d heads per kv head", HPG);
-  const int64_t smem = HC * cap * 4;
-  CV3_REQUIRE(cap > 0 && smem <= 150 * 1024, CV3_ERR_UNSUPPORTED, "decode_attention: cap too large");
+  const int64_t score_bytes = HC * cap * 4;
+  CV3_REQUIRE(cap > 0 && score_bytes <= 150 * 1024, CV3_ERR_UNSUPPORTED, "decode_attention: cap too large");
+  // staged key/value rows (RoPE launches): as many as fit next to the scores in 200 KB
+  const int64_t kv_off = (HC * cap + 3) / 4 * 4;  // floats, 16-byte aligned
+  const int64_t kmax = rope ? std::min<int64_t>(cap, (200 * 1024 - kv_off * 4) / (2 * DM * 4)) : 0;
+  const int64_t smem = kv_off * 4 + kmax * 2 * DM * 4;
   CV3_REQUIRE(((uintptr_t)q & 15) == 0 && ((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0,
               CV3_ERR_VALUE, "decode_attention: 16-byte aligned tensors required");
   if (batch == 0) return CV3_OK;
@@ -325,10 +380,21 @@ int launch_decode_attention(bool rope, const float* q, int64_t ldq, const float*
   return cv3::check_launch("decode_attention",
                            cv3::launch_dep(fn, grid, dim3(AT), (size_t)smem, cv3::as_stream(stream), q, ldq,
                                            cos_table, sin_table, pos, k_cache, v_cache, lens, (int)heads,
-                                           (int)kv_heads, cap, scale, out));
+                                           (int)kv_heads, cap, scale, out, (int)kmax, kv_off));
 }
 
 }  // namespace
+
+extern "C" int cv3_decode_attention_status(int* code) {
+  int v = 0;
+  CV3_CUDA(cudaMemcpyFromSymbol(&v, g_attn_err, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    CV3_CUDA(cudaMemcpyToSymbol(g_attn_err, &zero, sizeof(int)));
+  }
+  if (code) *code = v;
+  return CV3_OK;
+}
 
 extern "C" int cv3_decode_attention(const float* q, const float* k_cache, const float* v_cache, const int* lens,
                                     int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap,

@@ -307,7 +307,17 @@ int cv3_decode_attention(const float* q, const float* k_cache, const float* v_ca
  * pos[b] (half-split RoPE with the [position][64] cos / sin tables, rounded as
  * cv3_rope_qkv_append), appends key and value at pos[b] (not stored outside
  * [0, cap)), then attends like cv3_decode_attention over lens[b] cached rows.
- * Same results as cv3_rope_qkv_append followed by cv3_decode_attention. */
+ * Same results as cv3_rope_qkv_append followed by cv3_decode_attention, up to the
+ * order of a score's sums.  The cached rows below pos[b] are copied into shared
+ * memory before the launch's dependency wait, so pos[b] and those rows must have
+ * been written at least two launches earlier on the stream (the decode chain
+ * writes them one step earlier); a position that changed by the wait falls back
+ * to global reads. */
+/* Error word of cv3_decode_rope_attention, read and cleared: 0, or 1 when a CTA's
+ * staged key/value copy did not land within 2 s (that CTA then wrote nothing).
+ * No counterpart in the reference (a device-side wait bound). */
+int cv3_decode_attention_status(int* code);
+
 int cv3_decode_rope_attention(const float* qkv, int64_t ldq, const float* cos_table, const float* sin_table,
                               const int* pos, float* k_cache, float* v_cache, const int* lens, int64_t batch,
                               int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t cap, float scale, float* out,
