@@ -158,6 +158,22 @@ __device__ __forceinline__ int group_exponent(float amax) {
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
+// 256-bit global accesses (sm_100): a thread writes or reads a whole 32-byte sector of
+// its row at once (32-byte aligned addresses)
+__device__ __forceinline__ void st8(void* p, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t a4,
+                                    uint32_t a5, uint32_t a6, uint32_t a7) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a0), "r"(a1), "r"(a2), "r"(a3),
+               "r"(a4), "r"(a5), "r"(a6), "r"(a7)
+               : "memory");
+}
+
+__device__ __forceinline__ void ld8(const float* p, float* v) {
+  asm volatile("ld.global.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+               : "l"(p)
+               : "memory");
+}
+
 // One K group's MMAs: 4 k-steps of 16, A hi and A lo into the group's accumulator d,
 // the weights from one descriptor; then the commits that free the stage, the A planes
 // and hand the accumulator to the promotion.
@@ -385,7 +401,7 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
     const int row = quarter * 32 + lane;
     const int cbase = (warp - PW0) / 4 * EPI_COLS;
     const uint32_t lane_base = ((uint32_t)(quarter * 32) << 16) + (uint32_t)cbase;
-    const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    const bool vec = (ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(C) & 31) == 0);  // 32-byte rows pieces
     bool ok = true;
     int g = 0;
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
@@ -459,13 +475,14 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         const float f = cv3p::pow2f(e);
         const int gg = (n0 + cbase) / KG, half = cq & 1;
         __half* ph = ep.oplanes + (int64_t)grow * (2 * N) + 2 * KG * gg + 32 * half;
+        // 16 columns per 256-bit store (the planes rows are 32-byte aligned: N % 8 == 0)
 #pragma unroll
-        for (int q = 0; q < EPI_COLS / 8; ++q) {
-          uint32_t h[4], l[4];
+        for (int q = 0; q < EPI_COLS / 16; ++q) {
+          uint32_t h[8], l[8];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) cv3p::split_pair(acc[8 * q + 2 * t] * f, acc[8 * q + 2 * t + 1] * f, h[t], l[t]);
-          *reinterpret_cast<uint4*>(ph + 8 * q) = make_uint4(h[0], h[1], h[2], h[3]);
-          *reinterpret_cast<uint4*>(ph + KG + 8 * q) = make_uint4(l[0], l[1], l[2], l[3]);
+          for (int t = 0; t < 8; ++t) cv3p::split_pair(acc[16 * q + 2 * t] * f, acc[16 * q + 2 * t + 1] * f, h[t], l[t]);
+          st8(ph + 16 * q, h[0], h[1], h[2], h[3], h[4], h[5], h[6], h[7]);
+          st8(ph + KG + 16 * q, l[0], l[1], l[2], l[3], l[4], l[5], l[6], l[7]);
         }
         if (half == 0) ep.oexps[(int64_t)gg * ep.olde + grow] = (int8_t)e;
         continue;
@@ -480,26 +497,20 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
       // stores: the residual is C itself
 #pragma unroll
       for (int c0 = 0; c0 < EPI_COLS; c0 += 16) {
-        float bv[16], gv[16], rv[16];
+        float bv[16], gv[16], cv[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           bv[j] = ep.bias ? __ldg(ep.bias + n0 + cbase + c0 + j) : 0.f;
           gv[j] = ep.mode == 2 ? __ldg(gate + c0 + j) : 0.f;
-          rv[j] = 0.f;
+          cv[j] = 0.f;
         }
         if (ep.mode >= 2) {
           if (vec) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float4 t = *reinterpret_cast<const float4*>(crow + c0 + 4 * q);
-              rv[4 * q] = t.x;
-              rv[4 * q + 1] = t.y;
-              rv[4 * q + 2] = t.z;
-              rv[4 * q + 3] = t.w;
-            }
+            ld8(crow + c0, cv);
+            ld8(crow + c0 + 8, cv + 8);
           } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) rv[j] = crow[c0 + j];
+            for (int j = 0; j < 16; ++j) cv[j] = crow[c0 + j];
           }
         }
         float o[16];
@@ -508,14 +519,16 @@ tc_gemm_q8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
           float y = acc[c0 + j];
           if (ep.bias) y = __fadd_rn(y, bv[j]);
           if (ep.mode == 1) y = gelu_tanh(y);
-          else if (ep.mode == 2) y = __fadd_rn(rv[j], __fmul_rn(gv[j], y));
-          else if (ep.mode == 3) y = __fadd_rn(rv[j], y);
+          else if (ep.mode == 2) y = __fadd_rn(cv[j], __fmul_rn(gv[j], y));
+          else if (ep.mode == 3) y = __fadd_rn(cv[j], y);
           o[j] = y;
         }
         if (vec) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<float4*>(crow + c0 + 4 * q) = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+          for (int q = 0; q < 2; ++q)
+            st8(crow + c0 + 8 * q, __float_as_uint(o[8 * q]), __float_as_uint(o[8 * q + 1]), __float_as_uint(o[8 * q + 2]),
+                __float_as_uint(o[8 * q + 3]), __float_as_uint(o[8 * q + 4]), __float_as_uint(o[8 * q + 5]),
+                __float_as_uint(o[8 * q + 6]), __float_as_uint(o[8 * q + 7]));
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) crow[c0 + j] = o[j];
@@ -665,9 +678,10 @@ extern "C" int cv3_tc_gemm_q8_planes(const void* planes, const int8_t* exps, int
   CV3_REQUIRE(lde >= m && lde % 16 == 0 && exps != nullptr, CV3_ERR_VALUE,
               "tc_gemm_q8_planes: exponents [k/64][lde], lde >= m and a multiple of 16");
   CV3_REQUIRE(mode == 4 ? (out_planes && out_exps && out_lde >= m && out_lde % 16 == 0 &&
-                           ((uintptr_t)out_planes & 15) == 0)
+                           ((uintptr_t)out_planes & 31) == 0)
                         : ldc >= n,
-              CV3_ERR_VALUE, "tc_gemm_q8_planes: output (mode 4: planes [m][2n] and exponents [n/64][out_lde])");
+              CV3_ERR_VALUE,
+              "tc_gemm_q8_planes: output (mode 4: 32-byte aligned planes [m][2n] and exponents [n/64][out_lde])");
   if (m == 0 || n == 0) return CV3_OK;
   CV3_REQUIRE(k > 0 && m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 30), CV3_ERR_VALUE, "tc_gemm_q8_planes: sizes");
   CUtensorMap ma;
