@@ -90,7 +90,6 @@ SIGNATURES = {
     "cv3_decode_steps": [P, P],
     "cv3_decode_sync_words": [I64, I64],
     "cv3_decode_status": [P],
-    "cv3_tc_tf32_peak": [P, P],
     "cv3_q8_decode_gemv": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
     "cv3_q8_decode_gemv_mma": [P, I64, I64, I64, P, P, I64, I64, P, P, P, F, I32, P, I64, I64, P, I64, P, P],
     "cv3_decode_gemv_status": [P],

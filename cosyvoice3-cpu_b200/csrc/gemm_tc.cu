@@ -701,79 +701,3 @@ extern "C" int cv3_tc_gemm_split(const float* a, int64_t lda, const float* b, co
       ma, mb, mbl, (int)m, (int)n, (int)k, c, ldc, ep);
   return cv3::check_launch("tc_gemm_split");
 }
-
-// ---------------------------------------------------------------------------
-// Tensor-pipe peak probe: every SM issues back-to-back kind::tf32 MMAs
-// (M = 128, N = 256, K = 8, operands from shared memory, one accumulator) and
-// the rate is reported in TFLOP/s -- the denominator the 3xTF32 kernels'
-// tensor-pipe utilisation is quoted against.
-// ---------------------------------------------------------------------------
-namespace {
-
-__global__ void __launch_bounds__(64, 1) tf32_peak_kernel(int reps, int* err) {
-  extern __shared__ uint8_t sm_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar;
-  __shared__ uint32_t slot;
-  const int warp = threadIdx.x >> 5;
-  for (int i = threadIdx.x; i < 48 * 1024 / 4; i += blockDim.x) reinterpret_cast<float*>(sm)[i] = 0.0f;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&slot)), "r"(256)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  fence_before();
-  __syncthreads();
-  fence_after();
-  const uint32_t tmem = slot;
-  constexpr uint32_t ID = idesc_tf32(128, 256);
-  const uint32_t a = smem_u32(sm), b = a + 16384;
-  if (warp == 1) {
-    for (int i = 0; i < reps; ++i)
-      mma_ss(tmem, desc_k_sw128(a + (i & 3) * 32), desc_k_sw128(b + (i & 3) * 32), ID, i > 0 ? 1u : 0u);
-    mma_commit(&bar);
-    if ((threadIdx.x & 31) == 0) cv3tc::mbar_wait(&bar, 0, err, 1);
-  }
-  fence_before();
-  __syncthreads();
-  fence_after();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
-}
-
-__device__ int g_probe_err = 0;
-
-}  // namespace
-
-extern "C" int cv3_tc_tf32_peak(double* tflops, void* stream) {
-  CV3_REQUIRE(tflops != nullptr, CV3_ERR_VALUE, "tc_tf32_peak: no output");
-  const int smem = 50 * 1024;
-  int rc = cv3::allow_smem((const void*)tf32_peak_kernel, smem);
-  if (rc) return rc;
-  int* err = nullptr;
-  CV3_CUDA(cudaGetSymbolAddress((void**)&err, g_probe_err));
-  cudaStream_t st = cv3::as_stream(stream);
-  const int grid = cv3::sm_count(), reps = 8192;
-  tf32_peak_kernel<<<grid, 64, smem, st>>>(256, err);  // warm-up
-  rc = cv3::check_launch("tc_tf32_peak");
-  if (rc) return rc;
-  cudaEvent_t e0, e1;
-  CV3_CUDA(cudaEventCreate(&e0));
-  CV3_CUDA(cudaEventCreate(&e1));
-  CV3_CUDA(cudaEventRecord(e0, st));
-  tf32_peak_kernel<<<grid, 64, smem, st>>>(reps, err);
-  rc = cv3::check_launch("tc_tf32_peak");
-  CV3_CUDA(cudaEventRecord(e1, st));
-  CV3_CUDA(cudaEventSynchronize(e1));
-  float ms = 0.f;
-  CV3_CUDA(cudaEventElapsedTime(&ms, e0, e1));
-  cudaEventDestroy(e0);
-  cudaEventDestroy(e1);
-  if (rc) return rc;
-  *tflops = 2.0 * 128 * 256 * 8 * (double)reps * grid / (ms * 1e-3) / 1e12;
-  return CV3_OK;
-}

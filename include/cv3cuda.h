@@ -623,9 +623,6 @@ int64_t cv3_decode_sync_words(int64_t n_layers, int64_t hidden);
  * 7 a token outside the embedding table. */
 int cv3_decode_status(int* code);
 
-/* Measures the dense kind::tf32 tensor-pipe rate of this GPU (every SM
- * issuing 128x256x8 MMAs back to back) in TFLOP/s.  Synchronises. */
-int cv3_tc_tf32_peak(double* tflops, void* stream);
 
 /* Error word of the tensor-core kernels (0 = none; else the code of the
  * first bounded wait that expired), read and cleared.  Synchronises. */
