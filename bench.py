@@ -405,6 +405,19 @@ def measure_strong(tts, meta, rank: int, world: int, reps: int, barrier):
 
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the FF1 planes
+# GEMM at the bench shape, from an ncu capture of `bench.py --kernel ff1q8p` (47,250,944 read,
+# 38,543,360 written: part of the output planes is still in L2 when the kernel ends)
+FF1_PLANES_DRAM_BYTES = 85_794_304
+
+
+def ff1_planes_bytes(M: int, N: int, K: int) -> int:
+    """Algorithmic bytes of one FF1 planes launch: A planes and exponents, the fp16 weights
+    and fp32 transposed scales, the GELU output planes and exponents."""
+    lde = -(-M // 16) * 16
+    return M * 2 * K * 2 + (K // 64) * lde + N * K * 2 + (K // 64) * N * 4 + M * 2 * N * 2 + (N // 64) * lde
+
+
 def dominant_kernel_roofline(tts, peaks):
     """Time the DiT FF1 GEMM at the bench shape in isolation (the largest kernel of the
     step) with CUDA events on its launching stream; achieved = 2*M*N*K / time.  In the
@@ -467,7 +480,8 @@ def dominant_kernel_roofline(tts, peaks):
                             "note": "fp16/bf16-rate products issued per fp32 product: 2 (two fp16 parts of A "
                                     "against the exact fp16 weights)" if q8 else
                                     "3 tf32 products per fp32 product at half the bf16 rate"},
-            "traffic": None, "traffic_unit": "bytes per launch"}
+            "traffic": FF1_PLANES_DRAM_BYTES if planes else None, "traffic_unit": "bytes per launch",
+            "algorithmic_bytes": ff1_planes_bytes(M, blk.n, blk.k) if planes else None}
 
 
 def run_cuda(args, rank: int, world: int) -> None:
@@ -625,17 +639,21 @@ def run_kernel(args) -> None:
         a, c = torch.randn(M, K, device="cuda"), torch.empty(M, N, device="cuda")
         fn = lambda: lin(a.data_ptr(), M, c.data_ptr(), stream=st)
     elif args.kernel == "ff1q8p":
-        # the same GEMM with A as activation planes (what the balanced DiT feeds it)
+        # the same GEMM as the balanced DiT runs it: A as activation planes, GELU written
+        # back as planes (mode 4)
         M, N, K = 2 * UTTS * 2 * (PROMPT_TOKENS + TOKENS), 2048, 1024
         quant = pkg("quant")
         w = (np.random.default_rng(0).normal(size=(N, K)) * 0.02).astype(np.float32)
         lin = common.LinQ8(quant.make_qtensor(w).to_device())
-        a, c = torch.randn(M, K, device="cuda"), torch.empty(M, N, device="cuda")
+        a = torch.randn(M, K, device="cuda")
         lde = -(-M // 16) * 16
         pl = torch.empty((M, 2 * K), dtype=torch.float16, device="cuda")
         ex = torch.empty((K // 64, lde), dtype=torch.int8, device="cuda")
+        op = torch.empty((M, 2 * N), dtype=torch.float16, device="cuda")
+        oe = torch.empty((N // 64, lde), dtype=torch.int8, device="cuda")
         L.call("cv3_q8_split_rows", a.data_ptr(), K, M, K, pl.data_ptr(), ex.data_ptr(), lde, st)
-        fn = lambda: lin.tc_planes(pl.data_ptr(), ex.data_ptr(), lde, M, c.data_ptr(), 0, stream=st)
+        fn = lambda: lin.tc_planes(pl.data_ptr(), ex.data_ptr(), lde, M, None, 4, stream=st,
+                                   out_planes=op.data_ptr(), out_exps=oe.data_ptr(), out_lde=lde)
     elif args.kernel == "attention":
         B, H, N, D = 2 * UTTS, 16, 2 * (PROMPT_TOKENS + TOKENS), 64
         qkv, o = torch.randn(B, N, 3 * H * D, device="cuda"), torch.empty(B, N, H * D, device="cuda")
@@ -814,8 +832,12 @@ def main():
     if world > 1 and args.impl == "cuda":
         import datetime
         import torch.distributed as dist
+        import torch
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        local = int(os.environ.get("LOCAL_RANK", 0))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
     try:
         if args.lm_step:
             run_lm_step(args)
