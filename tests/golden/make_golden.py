@@ -29,10 +29,14 @@ Run in a checkout that has the reference project importable (its root on
   waveform the default chunked inference returns) and one config-4 utterance
   through all three balanced stages (ids, mel, waveform).
 
+* ``config5_dit.npz`` (``--only c5``) -- one forward of the reference's DiT in the
+  balanced profile at config 5's flow length: CFG batch 2 x 1500 frames
+  (``workloads.dit_inputs(5, 2, 1500)``).
+
 It also asserts that the synthetic generator reproduces the reference's own
 random-model generator tensor for tensor.
 
-    python tests/golden/make_golden.py --reference /path/to/cosyvoice3-cpu [--only sampling|full]
+    python tests/golden/make_golden.py --reference /path/to/cosyvoice3-cpu [--only sampling|full|c5]
 """
 
 from __future__ import annotations
@@ -220,10 +224,27 @@ def make_full(reference: str) -> None:
     print("wrote full_size.npz", {k: v.shape for k, v in out.items()})
 
 
+def make_c5(reference: str) -> None:
+    """Config 5's DiT length (one forward, balanced profile, batch 2 x 1500 frames)."""
+    from cv3cpu.io.weights import WeightFile
+    from cv3cpu.models.dit import DiT
+    synth, weights, wl = _pkg("synth"), _pkg("weights"), _pkg("workloads")
+    tmp = tempfile.mkdtemp()
+    W = synth.synthetic_weights("balanced", stages=("flow",))
+    path = os.path.join(tmp, "balanced_flow.safetensors")
+    weights.write_weights(path, dict(W), W.meta)
+    f = WeightFile(path)
+    print("config 5: DiT forward at (2, 80, 1500)", flush=True)
+    out = {"c5_dit_out": DiT(f, "flow.decoder.estimator.").forward(*wl.dit_inputs(5, 2, 1500)).astype(np.float32)}
+    f.close()
+    np.savez_compressed(os.path.join(HERE, "config5_dit.npz"), **out)
+    print("wrote config5_dit.npz", {k: v.shape for k, v in out.items()})
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference checkout")
-    ap.add_argument("--only", choices=["sampling", "full"], help="regenerate only this fixture")
+    ap.add_argument("--only", choices=["sampling", "full", "c5"], help="regenerate only this fixture")
     a = ap.parse_args()
     sys.path.insert(0, a.reference)
     sys.path.insert(0, os.path.join(a.reference, "tools"))
@@ -232,6 +253,9 @@ def main() -> None:
         return
     if a.only == "full":
         make_full(a.reference)
+        return
+    if a.only == "c5":
+        make_c5(a.reference)
         return
     from cv3cpu.io.weights import WeightFile
     from cv3cpu.models.flow import Flow

@@ -14,6 +14,8 @@ the same seeded weights and inputs).
   reference's default 250-frame chunked inference).
 * config 4 -- one utterance through the balanced LM, flow and vocoder: ids
   identical, mel within 1e-4, waveform within 1e-4 (three stages compounded).
+* config 5 -- the balanced DiT at CFG batch 2 x 1500 frames within 1e-5 of the
+  reference; batch-32 greedy decode identical to batch-1 decode per sequence.
 """
 
 import os
@@ -146,3 +148,35 @@ def test_config1_persistent_decode_250_ids(full):
     assert pkg("_lib").load().cv3_decode_status(ctypes.byref(code)) == 0 and code.value == 0
     assert ids.tolist() == full["c1_tokens"].tolist(), _first_flip(ids, full["c1_tokens"], full["c1_margin"])
     assert rel_err(eng.logp[0].cpu().numpy(), full["c1_logp"][-1]) < INT8_TOL
+
+
+def test_config5_dit_forward_batch2_1500_frames():
+    """Config 5's flow length: one forward of the balanced DiT (int8-weight GEMMs on
+    activation planes, attention over 1500 keys) at CFG batch 2 x 1500 frames against the
+    reference's own output (``config5_dit.npz``, ``make_golden.py --only c5``)."""
+    wl = pkg("workloads")
+    with np.load(os.path.join(GOLDEN, "config5_dit.npz")) as z:
+        ref = z["c5_dit_out"]
+    W = pkg("synth").synthetic_weights("balanced", stages=("flow",))
+    dit = pkg("models.dit").DiT(_device(W))
+    got = dit.forward(*wl.dit_inputs(5, 2, 1500))
+    assert type(dit.blocks[0].ff1).__name__ == "LinQ8"
+    assert got.shape == ref.shape == (2, 80, 1500)
+    assert rel_err(got, ref) < FP32_TOL
+
+
+def test_config5_lm_batch32_ids_equal_batch1():
+    """Config 5 decodes 32 sequences per GPU: the full-size balanced LM on 32 prompts of
+    40-80 text ids (four graph-replayed groups of eight) gives every sequence exactly the
+    ids it gets when decoded alone."""
+    W = pkg("synth").synthetic_weights("balanced", stages=("llm",))
+    lm = pkg("models.llm").CosyVoice3LM(_device(W))
+    rng = np.random.default_rng(32)
+    vocab = W.meta["qwen2"]["vocab_size"]
+    prompts = [lm._text_emb(rng.integers(0, vocab, size=int(rng.integers(40, 81))).tolist()) for _ in range(32)]
+    steps = 40
+    batch = lm.generate_greedy(prompts, steps).cpu().numpy()
+    assert batch.shape == (32, steps)
+    for i, p in enumerate(prompts):
+        alone = lm.generate_greedy([p], steps).cpu().numpy()[0]
+        assert alone.tolist() == batch[i].tolist(), i
