@@ -200,28 +200,39 @@ attn_decode_kernel(AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core path for head dim 64: flash-attention tiling on tcgen05, 3xTF32.
+// Tensor-core path for head dim 64: flash-attention tiling on tcgen05 with fp16
+// operands carrying fp32 precision.
+//
+// Every fp32 operand enters as two fp16 parts, hi = fp16(x * 2^e) and
+// lo = fp16(x * 2^e - hi), with e a power of two chosen per query row (Q), per
+// 64-key tile (K and V) or not at all (P, which lies in [0, 1]): 22 significant
+// bits relative to the row's / tile's largest value.  Products are hi*hi + hi*lo
+// + lo*hi in kind::f16 (K = 16 per MMA: half the instructions of 3xTF32, whose
+// K is 8), accumulated in fp32; the scales come off in the softmax (per row and
+// tile) and in the output fold (per tile).  Measured against fp64 this matches
+// the 3xTF32 scheme it replaces.
 //
 // CTA = one (batch, head) and 128 queries; keys in 64-key tiles through a
 // 3-stage TMA ring (K and V read in place through 4-D tensor maps over the
 // strided layout).  10 warps:
-//   warp 0     TMA producer (K and V tiles, SWIZZLE_128B);
-//   warp 1     MMA issuer: S_t = Q.K_t^T into TMEM, O_t = P_t.V_t into TMEM,
-//              both as hi*lo + lo*hi + hi*hi tf32 products (fp32-accurate);
+//   warp 0     TMA producer (K and V tiles as fp32, SWIZZLE_128B);
+//   warp 1     MMA issuer: S_t = Q.K_t^T into TMEM, O_t = P_t.V_t into TMEM;
 //              S_{t+2} is issued right behind O_t so the tensor pipe has work
 //              while the softmax warps handle tile t+1;
 //   warps 2-5  softmax, one query row per thread (= TMEM lane): running max,
-//              P_t = 2^(s*log2e - m*log2e) split into tf32 hi/lo and written
-//              back to TMEM, the row sum, and the rescale factor alpha_t of the
-//              running output (shared memory);
-//   warps 6-9  the scaled Q rows into TMEM once; then per tile the K tile split
-//              in place into hi/lo, the V tile transposed and split (tf32 MMAs
-//              take K-major operands only), and the fold o = o*alpha_u + O_u of
-//              an earlier tile's output into registers; finally o / l stored.
-// TMEM columns: Q hi | Q lo | S/P-hi x2 | P-lo x2 | O x2 (512).  Q and P are
-// the A operands straight from TMEM; K and the transposed V are K-major B
-// operands in shared memory.  Every wait is bounded; on a timeout the CTA
-// records an error (cv3_tc_attention_status), drains what it issued and exits.
+//              P_t = 2^(s*log2e - m*log2e) split into fp16 hi/lo written back
+//              over S_t in TMEM, the row sum, and the rescale factor alpha_t of
+//              the running output (shared memory); then K_{t+2} as fp16 hi/lo
+//              tiles (UMMA K-major, 128 B swizzle) with the tile's exponent;
+//   warps 6-9  the scaled Q rows into TMEM once; then per tile V as fp16 hi/lo
+//              tiles in its stored [key][dim] order (an MN-major B operand of
+//              P.V) with the tile's exponent, and the fold o = o*alpha +
+//              O_u*2^-e_v(u) of an earlier tile's output into registers;
+//              finally o / l stored.
+// TMEM columns: Q hi | Q lo (32 each: two fp16 per column) | S/P x2 | O x2.
+// Q and P are the A operands straight from TMEM; K (K-major) and V (MN-major)
+// are B operands in shared memory.  Every wait is bounded; on a timeout the CTA records an error
+// (cv3_tc_attention_status), drains what it issued and exits.
 // ---------------------------------------------------------------------------
 namespace tc {
 
@@ -230,11 +241,15 @@ using namespace cv3tc;
 constexpr int BQ = 128, BKV = 64, HD = 64, STAGES = 3;
 constexpr int HALF = BKV * 32 * 4;  // 8 KB: 64 keys x 32 floats (one TMA box, 128-byte rows)
 constexpr int TILE = 2 * HALF;      // 16 KB: 64 keys x 64 floats
-constexpr int STAGE = 4 * TILE;     // K hi | K lo | V hi | V lo
+constexpr int T16 = BKV * HD * 2;   // 8 KB: a 64 x 64 fp16 tile, 128-byte rows
+// stage: K fp32 | V fp32 | K hi | K lo | V hi | V lo
+constexpr int ST_K = 0, ST_V = TILE, ST_KH = 2 * TILE, ST_KL = ST_KH + T16, ST_VH = ST_KL + T16, ST_VL = ST_VH + T16;
+constexpr int STAGE = ST_VL + T16;  // 64 KB
 constexpr int THREADS = 320;
-constexpr uint32_t C_QHI = 0, C_QLO = 64, C_S = 128, C_PLO = 256, C_O = 384;
-constexpr uint32_t ID_S = idesc_tf32(BQ, BKV);
-constexpr uint32_t ID_PV = idesc_tf32(BQ, HD);
+constexpr uint32_t C_QHI = 0, C_QLO = 32, C_S = 64, C_O = 192;
+constexpr uint32_t ID_S = (1u << 4) | ((uint32_t)(BKV >> 3) << 17) | ((uint32_t)(BQ >> 4) << 24);  // f16 x f16 -> f32
+// P.V: B = V as stored, [key][dim] -- MN-major (bit 16), 8-key x 128 B swizzle atoms
+constexpr uint32_t ID_PV = (1u << 4) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(BQ >> 4) << 24);
 constexpr float LOG2E = 1.4426950408889634f;
 
 // byte offset of element (row, col) of a [rows][64] fp32 tile held as two
@@ -242,6 +257,71 @@ constexpr float LOG2E = 1.4426950408889634f;
 // chunks XOR row % 8); boxes HALF bytes apart
 __device__ __forceinline__ uint32_t swz(int row, int col) {
   return (uint32_t)((col >> 5) * HALF + row * 128 + ((((col & 31) >> 2) ^ (row & 7)) << 4) + (col & 3) * 4);
+}
+
+// byte offset of the 16-byte chunk holding fp16 elements [8 c, 8 c + 8) of row `row`
+// of a [rows][64] fp16 tile in the UMMA K-major 128 B-swizzled layout
+__device__ __forceinline__ uint32_t swz16(int row, int c) { return (uint32_t)(row * 128 + ((c ^ (row & 7)) << 4)); }
+
+// the exponent e with max * 2^e in [2^14, 2^15) (0 for an all-zero block), clamped
+__device__ __forceinline__ int scale_exp(float amax) {
+  if (!(amax > 0.f)) return 0;
+  const int e = 14 - (((__float_as_int(amax) >> 23) & 0xFF) - 127);
+  return e > 126 ? 126 : (e < -126 ? -126 : e);
+}
+
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
+
+// (a0, a1) -> fp16 hi and lo pairs, a0 in the low halves
+__device__ __forceinline__ void split2(float a0, float a1, uint32_t& hi, uint32_t& lo) {
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(a1), "f"(a0));
+  const __half2 h = *reinterpret_cast<const __half2*>(&hi);
+  const float r0 = a0 - __low2float(h), r1 = a1 - __high2float(h);
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(r1), "f"(r0));
+}
+
+// 32 lanes x 32 columns of packed words into TMEM
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+// 12 kind::f16 MMAs (4 k-steps x hi*lo, lo*hi, hi*hi) into d, A from TMEM (hi at ah, lo
+// at al; 8 columns per k-step), B from shared memory (descriptors bh, bl; BSTEP per
+// k-step in 16-byte units: 2 for a K-major tile, 128 for two 8-row atoms of an MN-major
+// one), one elected lane; d is overwritten by the first
+template <int BSTEP>
+__device__ __forceinline__ void mma12(uint32_t d, uint32_t ah, uint32_t al, uint64_t bh, uint64_t bl, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, pt;\n\t.reg .b32 a1, a2, a3, c1, c2, c3;\n\t"
+      ".reg .b64 h1, h2, h3, l1, l2, l3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 pf, %5, %5;\n\tsetp.eq.b32 pt, %5, %5;\n\t"
+      "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+      "add.u32 c1, %2, 8;\n\tadd.u32 c2, %2, 16;\n\tadd.u32 c3, %2, 24;\n\t"
+      "add.s64 h1, %3, %7;\n\tadd.s64 h2, %3, %8;\n\tadd.s64 h3, %3, %9;\n\t"
+      "add.s64 l1, %4, %7;\n\tadd.s64 l2, %4, %8;\n\tadd.s64 l3, %4, %9;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %4, %6, pf;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %3, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %3, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], l1, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [c1], h1, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], h1, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], l2, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [c2], h2, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], h2, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], l3, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [c3], h3, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], h3, %6, pt;\n\t}" ::"r"(d),
+      "r"(ah), "r"(al), "l"(bh), "l"(bl), "r"(0), "r"(idesc), "n"(BSTEP), "n"(2 * BSTEP), "n"(3 * BSTEP)
+      : "memory");
 }
 
 struct Bars {
@@ -253,8 +333,65 @@ struct Bars {
   int issued_k[STAGES], issued_v[STAGES];
   float alpha[4][BQ];  // rescale factor of the running output, per tile (mod 4) and row
   float lfin[BQ];      // final softmax denominators
+  float qf[BQ];        // 2^-e of each query row's scaling
+  float kf[8], vf[8];  // 2^-e of each key / value tile's scaling (tile mod 8)
+  float red[2][4];     // the converter warps' tile maxima (K, V)
 };
 constexpr int SMEM = STAGES * STAGE + 1024 + (int)sizeof(Bars);
+
+// The four warps of a role (softmax: named barrier 2, converters: 1) agree on `ok`: a
+// barrier over their 128 threads that every thread reaches, so they leave together.
+__device__ __forceinline__ bool agree128(bool ok, int bar) {
+  uint32_t all;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(all)
+      : "r"((uint32_t)ok), "r"(bar)
+      : "memory");
+  return all != 0;
+}
+
+// the largest of the four warps' values m (named barrier `bar` + four shared slots)
+__device__ __forceinline__ float max128(float m, float* red4, int w, int lane, int bar) {
+  m = warp_max(m);
+  if (lane == 0) red4[w] = m;
+  asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+  return fmaxf(fmaxf(red4[0], red4[1]), fmaxf(red4[2], red4[3]));
+}
+
+// A K or V tile (fp32 [key][dim], as TMA wrote it at `src`) -> fp16 hi / lo tiles at `dh`
+// / `dl`, [key][dim] rows of 128 B with the 128 B swizzle -- K-major for K (dims are its
+// MMA K), MN-major for V (keys are its MMA K) -- scaled by the tile's exponent (2^-e into
+// *kf); thread i of the 128 takes key i / 2, dims 32 (i % 2) .. + 31
+__device__ __forceinline__ void convert_rows(uint8_t* st, int src, int dh, int dl, int i, float* kf, float* red4, int w,
+                                             int lane, int bar) {
+  const int kr = i >> 1, kh = i & 1;
+  float kv[32];
+  float am = 0.f;
+#pragma unroll
+  for (int i4 = 0; i4 < 8; ++i4) {
+    const float4 x = *reinterpret_cast<const float4*>(st + src + swz(kr, 32 * kh + 4 * i4));
+    kv[4 * i4] = x.x;
+    kv[4 * i4 + 1] = x.y;
+    kv[4 * i4 + 2] = x.z;
+    kv[4 * i4 + 3] = x.w;
+    am = fmaxf(fmaxf(am, fmaxf(fabsf(x.x), fabsf(x.y))), fmaxf(fabsf(x.z), fabsf(x.w)));
+  }
+  const int e = scale_exp(max128(am, red4, w, lane, bar));
+  const float sc = pow2i(e);
+  if (i == 0) *kf = pow2i(-e);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {  // 8 dims per 16-byte chunk
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) split2(kv[8 * c + 2 * j] * sc, kv[8 * c + 2 * j + 1] * sc, hi[j], lo[j]);
+    const uint32_t off = swz16(kr, 4 * kh + c);
+    *reinterpret_cast<uint4*>(st + dh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(st + dl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 __device__ int g_attn_err = 0;
 
@@ -345,16 +482,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         }
         B.issued_k[s] = (int)r;
         mbar_expect_tx(&B.kfull[s], TILE);
-        tma_load_4d(st, &kmap, &B.kfull[s], 0, key0, hk, b);
-        tma_load_4d(st + HALF, &kmap, &B.kfull[s], 32, key0, hk, b);
+        tma_load_4d(st + ST_K, &kmap, &B.kfull[s], 0, key0, hk, b);
+        tma_load_4d(st + ST_K + HALF, &kmap, &B.kfull[s], 32, key0, hk, b);
         if (*abort_flag || !bwait(&B.vempty[s], (r & 1) ^ 1, 2)) {
           *abort_flag = 1;
           break;
         }
         B.issued_v[s] = (int)r;
         mbar_expect_tx(&B.vfull[s], TILE);
-        tma_load_4d(st + 2 * TILE, &vmap, &B.vfull[s], 0, key0, hk, b);
-        tma_load_4d(st + 2 * TILE + HALF, &vmap, &B.vfull[s], 32, key0, hk, b);
+        tma_load_4d(st + ST_V, &vmap, &B.vfull[s], 0, key0, hk, b);
+        tma_load_4d(st + ST_V + HALF, &vmap, &B.vfull[s], 32, key0, hk, b);
       }
     }
   } else if (warp == 1) {
@@ -365,41 +502,27 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         const bool ok = !*abort_flag && bwait(bar, parity, code);
         return __all_sync(0xffffffffu, ok);
       };
+      auto sbuf = [&](int t) -> uint32_t { return tmem + C_S + 64u * (uint32_t)(t & 1); };
+      constexpr uint64_t T16D = T16 >> 4;  // the lo tile, in descriptor address units
       auto issue_s = [&](int t) -> bool {
         const int s = t % STAGES;
-        const uint32_t r = (uint32_t)(t / STAGES);
-        if (!ready(&B.kconv[s], r & 1, 3)) return false;
+        if (!ready(&B.kconv[s], (uint32_t)(t / STAGES) & 1, 3)) return false;
         fence_after();
-        const uint32_t khi = smem_u32(smem + s * STAGE), klo = khi + TILE;
-        const uint32_t d = tmem + C_S + 64u * (t & 1);
-#pragma unroll
-        for (int kk = 0; kk < HD / 8; ++kk) {
-          const uint32_t off = (uint32_t)((kk >> 2) * HALF + (kk & 3) * 32);
-          mma_ts(d, tmem + C_QHI + 8 * kk, desc_k_sw128(klo + off), ID_S, kk > 0 ? 1u : 0u);
-          mma_ts(d, tmem + C_QLO + 8 * kk, desc_k_sw128(khi + off), ID_S, 1u);
-          mma_ts(d, tmem + C_QHI + 8 * kk, desc_k_sw128(khi + off), ID_S, 1u);
-        }
+        const uint64_t kd = desc_k_sw128(smem_u32(smem + s * STAGE + ST_KH));
+        mma12<2>(sbuf(t), tmem + C_QHI, tmem + C_QLO, kd, kd + T16D, ID_S);
         mma_commit(&B.sfull[t & 1]);
         mma_commit(&B.kempty[s]);
         return true;
       };
       auto issue_pv = [&](int t) -> bool {
         const int s = t % STAGES;
-        const uint32_t r = (uint32_t)(t / STAGES);
         if (!ready(&B.pready[t & 1], (uint32_t)(t >> 1) & 1, 4)) return false;
-        if (!ready(&B.vconv[s], r & 1, 5)) return false;
+        if (!ready(&B.vconv[s], (uint32_t)(t / STAGES) & 1, 5)) return false;
         if (t >= 2 && !ready(&B.ofree[t & 1], (uint32_t)((t - 2) >> 1) & 1, 6)) return false;
         fence_after();
-        const uint32_t vhi = smem_u32(smem + s * STAGE + 2 * TILE), vlo = vhi + TILE;
-        const uint32_t d = tmem + C_O + 64u * (t & 1);
-        const uint32_t phi = tmem + C_S + 64u * (t & 1), plo = tmem + C_PLO + 64u * (t & 1);
-#pragma unroll
-        for (int kk = 0; kk < BKV / 8; ++kk) {
-          const uint32_t off = (uint32_t)((kk >> 2) * HALF + (kk & 3) * 32);
-          mma_ts(d, phi + 8 * kk, desc_k_sw128(vlo + off), ID_PV, kk > 0 ? 1u : 0u);
-          mma_ts(d, plo + 8 * kk, desc_k_sw128(vhi + off), ID_PV, 1u);
-          mma_ts(d, phi + 8 * kk, desc_k_sw128(vhi + off), ID_PV, 1u);
-        }
+        const uint64_t vd = desc_k_sw128(smem_u32(smem + s * STAGE + ST_VH));
+        // P hi in columns 0-31 of the S buffer, P lo in 32-63
+        mma12<128>(tmem + C_O + 64u * (t & 1), sbuf(t), sbuf(t) + 32, vd, vd + T16D, ID_PV);
         mma_commit(&B.ofull[t & 1]);
         mma_commit(&B.vempty[s]);
         return true;
@@ -420,17 +543,32 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     const int qi = q0 + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     float mrun = -INFINITY, l = 0.f;
-    for (int t = 0; t < nt; ++t) {
+    const int sw = warp - 2, stid = threadIdx.x - 64;  // softmax warp 0..3, thread 0..127
+    // the softmax warps also turn each K tile into fp16 parts: tiles 0 and 1 first, then
+    // tile t + 2 right after the softmax of tile t (S_{t+2} is issued after O_t, which
+    // waits for that softmax anyway)
+    auto conv_k = [&](int t) -> bool {
+      const int s = t % STAGES;
+      if (!agree128(!*abort_flag && bwait(&B.kfull[s], (uint32_t)(t / STAGES) & 1, 8), 2)) return false;
+      convert_rows(smem + s * STAGE, ST_K, ST_KH, ST_KL, stid, &B.kf[t & 7], B.red[0], sw, lane, 2);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.kconv[s]);
+      return true;
+    };
+    bool sok = nt == 0 || (conv_k(0) && (nt < 2 || conv_k(1)));
+    // Q's row scale is written before qready, which the first S waited for
+    float qf = 0.f;
+    for (int t = 0; sok && t < nt; ++t) {
       const int key0 = (tbeg + t) * BKV;
-      // S_t done also means O_{t-2} is done (the pipe runs in issue order), so the
-      // P-lo buffer of this parity is free again
-      bool go = !*abort_flag && bwait(&B.sfull[t & 1], (uint32_t)(t >> 1) & 1, 11);
-      go = __all_sync(0xffffffffu, go);
-      if (!go) {
-        *abort_flag = 1;
+      // S_t done also means O_{t-2}, the last reader of this buffer's P, is done (the
+      // pipe runs in issue order)
+      if (!agree128(!*abort_flag && bwait(&B.sfull[t & 1], (uint32_t)(t >> 1) & 1, 11), 2)) {
+        sok = false;
         break;
       }
       fence_after();
+      if (t == 0) qf = B.qf[row];
+      const float f = qf * B.kf[t & 7];  // S = S' * 2^-(e_q + e_k)
       float sv[BKV];
       tmem_ld64(tmem + lane_base + C_S + 64u * (t & 1), sv);
       if (MASK != 0 || key0 + BKV > a.m) {
@@ -445,20 +583,21 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
       for (int w = BKV / 4; w >= 1; w >>= 1)
 #pragma unroll
         for (int j = 0; j < w; ++j) mx[j] = fmaxf(mx[j], mx[j + w]);
-      const float mnew = fmaxf(mrun, mx[0]);
+      const float mnew = fmaxf(mrun, mx[0] * f);
       const float mlog = mnew == -INFINITY ? 0.f : mnew * LOG2E;
       const float alpha = mrun == -INFINITY ? 0.f : ex2(fmaf(mrun, LOG2E, -mlog));
-      float lo[BKV];
+      const float fl = f * LOG2E;
+      uint32_t ph[BKV / 2], pl[BKV / 2];
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < BKV; ++j) {
-        const float p = ex2(fmaf(sv[j], LOG2E, -mlog));
-        ps[j & 3] += p;
-        sv[j] = tf32_hi(p);
-        lo[j] = p - sv[j];
+      for (int j = 0; j < BKV; j += 2) {
+        const float p0 = ex2(fmaf(sv[j], fl, -mlog)), p1 = ex2(fmaf(sv[j + 1], fl, -mlog));
+        ps[j & 3] += p0;
+        ps[(j + 1) & 3] += p1;
+        split2(p0, p1, ph[j / 2], pl[j / 2]);
       }
-      tmem_st64(tmem + lane_base + C_S + 64u * (t & 1), sv);
-      tmem_st64(tmem + lane_base + C_PLO + 64u * (t & 1), lo);
+      tmem_st32u(tmem + lane_base + C_S + 64u * (t & 1), ph);
+      tmem_st32u(tmem + lane_base + C_S + 64u * (t & 1) + 32, pl);
       l = l * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
       mrun = mnew;
       B.alpha[t & 3][row] = alpha;
@@ -470,9 +609,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         mbar_arrive(&B.pready[t & 1]);
         mbar_arrive(&B.aready[t & 3]);
       }
+      if (t + 2 < nt && !conv_k(t + 2)) sok = false;
     }
+    if (!sok) *abort_flag = 1;
   } else {
-    // ---- Q into TMEM; K/V tiles split; output folds (warps 6-9) ---------------------------
+    // ---- Q into TMEM; V tiles to fp16 parts; output folds (warps 6-9) ----------------------
     const int quarter = warp & 3;
     const int cw = warp - 6;          // converter warp 0..3
     const int ctid = threadIdx.x - 192;
@@ -481,20 +622,27 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     if (nt > 0) {
       const float* qp = a.q + (int64_t)b * a.qsb + (int64_t)h * a.qsh + (int64_t)min(qi, a.n - 1) * a.qsn;
-      float hi[HD], lo[HD];
+      float xs[HD];
+      float am = 0.f;
 #pragma unroll
       for (int c4 = 0; c4 < HD / 4; ++c4) {
         float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
         if (qi < a.n) x = *reinterpret_cast<const float4*>(qp + c4 * 4);
-        const float xs[4] = {x.x * a.scale, x.y * a.scale, x.z * a.scale, x.w * a.scale};
+        xs[4 * c4] = x.x * a.scale;
+        xs[4 * c4 + 1] = x.y * a.scale;
+        xs[4 * c4 + 2] = x.z * a.scale;
+        xs[4 * c4 + 3] = x.w * a.scale;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          hi[c4 * 4 + e] = tf32_hi(xs[e]);
-          lo[c4 * 4 + e] = xs[e] - hi[c4 * 4 + e];
-        }
+        for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(xs[4 * c4 + e]));
       }
-      tmem_st64(tmem + lane_base + C_QHI, hi);
-      tmem_st64(tmem + lane_base + C_QLO, lo);
+      const int e = scale_exp(am);
+      const float sc = pow2i(e);
+      uint32_t hi[HD / 2], lo[HD / 2];
+#pragma unroll
+      for (int j = 0; j < HD; j += 2) split2(xs[j] * sc, xs[j + 1] * sc, hi[j / 2], lo[j / 2]);
+      B.qf[row] = pow2i(-e);
+      tmem_st32u(tmem + lane_base + C_QHI, hi);
+      tmem_st32u(tmem + lane_base + C_QLO, lo);
       tmem_st_wait();
       fence_before();
       __syncwarp();
@@ -504,7 +652,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
 #pragma unroll
     for (int c = 0; c < HD; ++c) o[c] = 0.f;
     bool ok = true;
-    // o = o * alpha_u + O_u, then hand the O buffer back to the MMA warp
+    // o = o * alpha_u + O_u * 2^-e_v(u), then hand the O buffer back to the MMA warp
 #define CV3_FOLD(u)                                                                               \
   {                                                                                               \
     const int u_ = (u);                                                                           \
@@ -516,64 +664,26 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     } else {                                                                                      \
       fence_after();                                                                              \
       const float al_ = B.alpha[u_ & 3][row];                                                     \
+      const float vf_ = B.vf[u_ & 7];                                                             \
       float ov_[HD];                                                                              \
       tmem_ld64(tmem + lane_base + C_O + 64u * (u_ & 1), ov_);                                    \
-      _Pragma("unroll") for (int c = 0; c < HD; ++c) o[c] = fmaf(o[c], al_, ov_[c]);              \
+      _Pragma("unroll") for (int c = 0; c < HD; ++c) o[c] = fmaf(o[c], al_, ov_[c] * vf_);        \
       fence_before();                                                                             \
       __syncwarp();                                                                               \
       if (lane == 0) mbar_arrive(&B.ofree[u_ & 1]);                                               \
     }                                                                                             \
   }
-    for (int t = 0; ok && t < nt; ++t) {
+    // every converter warp reaches each agreement (a failed fold included), so the four
+    // leave the loop together and no named barrier waits for a warp that has left
+    for (int t = 0; t < nt; ++t) {
       const int s = t % STAGES;
       const uint32_t r = (uint32_t)(t / STAGES);
       uint8_t* st = smem + s * STAGE;
-      bool go = !*abort_flag && bwait(&B.kfull[s], r & 1, 8);
-      go = __all_sync(0xffffffffu, go);
-      if (!go) {
+      if (!agree128(ok && !*abort_flag && bwait(&B.vfull[s], r & 1, 9), 1)) {
         ok = false;
         break;
       }
-      split_tile(reinterpret_cast<float*>(st), reinterpret_cast<float*>(st + TILE), TILE, ctid, 128);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B.kconv[s]);
-      go = !*abort_flag && bwait(&B.vfull[s], r & 1, 9);
-      go = __all_sync(0xffffffffu, go);
-      if (!go) {
-        ok = false;
-        break;
-      }
-      {
-        // V_t arrives as [key][d]; the MMA wants V_t^T [d][key] as a K-major operand,
-        // so the tile is transposed while it is split.  Reads: float4 along d, eight
-        // consecutive keys per quarter-warp (distinct swizzled chunks); writes: a warp
-        // covers 32 consecutive keys of one d row (32 distinct banks).  All reads
-        // finish (barrier of the four converter warps) before the in-place writes.
-        uint8_t* vraw = st + 2 * TILE;
-        uint8_t* vlo = st + 3 * TILE;
-        float4 rv[2][4];
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int i4 = 0; i4 < 4; ++i4)
-            rv[kb][i4] = *reinterpret_cast<const float4*>(vraw + swz(lane + 32 * kb, 4 * (cw * 4 + i4)));
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int i4 = 0; i4 < 4; ++i4) {
-            const float xv[4] = {rv[kb][i4].x, rv[kb][i4].y, rv[kb][i4].z, rv[kb][i4].w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint32_t off = swz(4 * (cw * 4 + i4) + e, lane + 32 * kb);
-              const float hv = tf32_hi(xv[e]);
-              *reinterpret_cast<float*>(vraw + off) = hv;
-              *reinterpret_cast<float*>(vlo + off) = xv[e] - hv;
-            }
-          }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      convert_rows(st, ST_V, ST_VH, ST_VL, ctid, &B.vf[t & 7], B.red[1], cw, lane, 1);
       __syncwarp();
       if (lane == 0) mbar_arrive(&B.vconv[s]);
       if (t >= 2) CV3_FOLD(t - 2);
