@@ -408,17 +408,30 @@ conv_gather_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
 // ---------------------------------------------------------------------------------
 namespace wk {
 
-constexpr int THREADS = 384;
 constexpr int MAX_STAGES = 8;            // weight ring (as many stages as shared memory leaves, >= 2)
-constexpr int NSET = 6;                  // main accumulators: K blocks in flight between MMA and drain
-constexpr uint32_t C_CROSS = NSET * 64;  // remainder accumulators of even / odd tiles at 384 / 448
+constexpr int NSET_MAX = 6;
 constexpr int FMAX = 256;                // window rows (TMA box limit)
+
+// Tile width: 64 output channels, or 128 where a group has that many (one MMA then does
+// twice the work: at these widths the tensor pipe is paced by the reduction length, not
+// by N).  TMEM holds NSET main accumulators (K blocks in flight between MMA and drain)
+// and two remainder accumulators (even / odd tiles), BNW columns each; the drain warps
+// (two per TMEM lane quarter at BNW = 128) fold 64 channels each.
+template <int BNW>
+struct Wide {
+  static constexpr int THREADS = BNW == 64 ? 384 : 512;
+  static constexpr int NSET = BNW == 64 ? 6 : 2;
+  static constexpr int NDRAIN = BNW / 16;  // drain warps
+  static constexpr uint32_t C_CROSS = NSET * BNW;
+  static constexpr int TILE = BNW * BK * 4;  // one BNW x 32 weight tile
+  static constexpr uint32_t IDESC = idesc_tf32(BM, BNW);
+};
 
 struct Bars {
   uint64_t full[MAX_STAGES], empty[MAX_STAGES];
   uint64_t afull[2], aempty[2];      // A tile pair nb: built / free again
   uint64_t winfull[2];               // token-major window nb landed in A tile nb
-  uint64_t accfull[NSET], drained[NSET];
+  uint64_t accfull[NSET_MAX], drained[NSET_MAX];
   uint64_t crossdrained[2];
   uint64_t done;
   uint32_t tmem;
@@ -458,7 +471,7 @@ __device__ __forceinline__ int sw_off(int f, int q) { return f * 128 + ((q ^ (f 
 template <bool LO>
 __device__ __forceinline__ void issue_kblock(uint32_t d_main, uint32_t d_cross, uint64_t a_hi, uint64_t a_lo,
                                              uint64_t w, uint64_t w_lo, uint32_t cross_acc, uint64_t* bar_empty,
-                                             uint64_t* bar_acc) {
+                                             uint64_t* bar_acc, uint32_t idesc) {
   if (LO) {
     asm volatile(
         "{\n\t.reg .pred e, pf, pt, pc;\n\t.reg .b64 h1, h2, h3, l1, l2, l3, w1, w2, w3, v0, v1, v2, v3;\n\t"
@@ -482,7 +495,7 @@ __device__ __forceinline__ void issue_kblock(uint32_t d_main, uint32_t d_cross, 
         "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], h3, v3, %2, pt;\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%3];\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%9];\n\t}" ::"r"(d_main),
-        "r"(d_cross), "r"(IDESC), "r"(smem_u32(bar_empty)), "r"(cross_acc), "l"(a_hi), "l"(a_lo), "l"(w), "l"(w_lo),
+        "r"(d_cross), "r"(idesc), "r"(smem_u32(bar_empty)), "r"(cross_acc), "l"(a_hi), "l"(a_lo), "l"(w), "l"(w_lo),
         "r"(smem_u32(bar_acc))
         : "memory");
   } else {
@@ -503,7 +516,7 @@ __device__ __forceinline__ void issue_kblock(uint32_t d_main, uint32_t d_cross, 
         "@e tcgen05.mma.cta_group::1.kind::tf32 [%1], l3, w3, %2, pt;\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%3];\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%8];\n\t}" ::"r"(d_main),
-        "r"(d_cross), "r"(IDESC), "r"(smem_u32(bar_empty)), "r"(cross_acc), "l"(a_hi), "l"(a_lo), "l"(w),
+        "r"(d_cross), "r"(idesc), "r"(smem_u32(bar_empty)), "r"(cross_acc), "l"(a_hi), "l"(a_lo), "l"(w),
         "r"(smem_u32(bar_acc))
         : "memory");
   }
@@ -513,9 +526,29 @@ __device__ __forceinline__ float4 split_lo(float4 h) {
   return make_float4(h.x - tf32_hi(h.x), h.y - tf32_hi(h.y), h.z - tf32_hi(h.z), h.w - tf32_hi(h.w));
 }
 
+// acc[j] += TMEM row columns j (64 of them), rounded to nearest; one 64-column load, or
+// two of 32 where registers are tighter (the 128-wide tile's 512 threads)
+template <bool ONE_LOAD>
+__device__ __forceinline__ void fold64(uint32_t taddr, float (&acc)[64]) {
+  if (ONE_LOAD) {
+    float m[64];
+    tmem_ld64(taddr, m);
+#pragma unroll
+    for (int j = 0; j < 64; ++j) acc[j] = __fadd_rn(acc[j], m[j]);
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float m[32];
+      tmem_ld32(taddr + 32 * h, m);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[32 * h + j] = __fadd_rn(acc[32 * h + j], m[j]);
+    }
+  }
+}
+
 // LAYOUT 1: channel-major x (frames contiguous); 2: token-major x (channels contiguous)
-template <int ACT, bool SNAKE, int LAYOUT>
-__global__ void __launch_bounds__(THREADS, 1)
+template <int ACT, bool SNAKE, int LAYOUT, int BNW>
+__global__ void __launch_bounds__(Wide<BNW>::THREADS, 1)
 conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_wlo,
                    const __grid_constant__ CUtensorMap map_x, WinArgs p) {
   const ConvArgs& a = p.c;
@@ -527,7 +560,8 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
   volatile int* abort_flag = &S.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = a.k * a.cblocks;
-  const uint32_t tx_bytes = (uint32_t)(a.has_lo ? 2 * TILE_B : TILE_B);
+  using C = Wide<BNW>;
+  const uint32_t tx_bytes = (uint32_t)(a.has_lo ? 2 * C::TILE : C::TILE);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
@@ -539,12 +573,12 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
       mbar_init(&S.afull[i], 4);
       mbar_init(&S.aempty[i], 1);
       mbar_init(&S.winfull[i], 1);
-      mbar_init(&S.crossdrained[i], 4);
+      mbar_init(&S.crossdrained[i], C::NDRAIN);
       S.issued_win[i] = -1;
     }
-    for (int i = 0; i < NSET; ++i) {
+    for (int i = 0; i < C::NSET; ++i) {
       mbar_init(&S.accfull[i], 1);
-      mbar_init(&S.drained[i], 4);
+      mbar_init(&S.drained[i], C::NDRAIN);
     }
     mbar_init(&S.done, 1);
     S.abort_flag = 0;
@@ -572,7 +606,7 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
     const int tx = tile % p.nx, rest = tile / p.nx;
     const int ty = rest % p.ny, z = rest / p.ny;
     t0 = tx * BM;
-    co0 = ty * BN;
+    co0 = ty * BNW;
     b = z / a.groups;
     g = z - b * a.groups;
   };
@@ -596,7 +630,7 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
           S.issued[s] = r;
           mbar_expect_tx(&S.full[s], tx_bytes);
           tma_load_2d(st, &map_w, &S.full[s], kb * BK, wrow0);
-          if (a.has_lo) tma_load_2d(st + TILE_B, &map_wlo, &S.full[s], kb * BK, wrow0);
+          if (a.has_lo) tma_load_2d(st + C::TILE, &map_wlo, &S.full[s], kb * BK, wrow0);
           if (++s == ns) s = 0, ++r;
         }
       }
@@ -612,7 +646,7 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
         ok = false;
         break;
       }
-      const uint32_t d_cross = tmem + C_CROSS + 64u * cp;
+      const uint32_t d_cross = tmem + C::C_CROSS + (uint32_t)BNW * cp;
       for (int cb = 0; ok && cb < a.cblocks; ++cb, ++gcb) {
         const int nb = gcb & 1;
         if (!ready(&S.afull[nb], (uint32_t)(gcb >> 1) & 1, 3)) {
@@ -624,8 +658,8 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
         const uint64_t d_ahi = desc_k_sw128(smem_u32(abase + nb * p.abytes));
         const uint64_t d_alo = desc_k_sw128(smem_u32(abase + (2 + nb) * p.abytes));
         for (int j = 0; j < a.k; ++j, ++gkb) {
-          const int set = gkb % NSET;
-          if (gkb >= NSET && !ready(&S.drained[set], ((uint32_t)(gkb / NSET) & 1) ^ 1, 8)) {
+          const int set = gkb % C::NSET;
+          if (gkb >= C::NSET && !ready(&S.drained[set], ((uint32_t)(gkb / C::NSET) & 1) ^ 1, 8)) {
             ok = false;
             break;
           }
@@ -634,16 +668,16 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
             break;
           }
           fence_after();
-          const uint32_t d_main = tmem + 64u * set;
-          const uint64_t d_w = desc_k_sw128(smem_u32(smem + s * p.stage_bytes)), d_wlo = d_w + (TILE_B >> 4);
+          const uint32_t d_main = tmem + (uint32_t)BNW * set;
+          const uint64_t d_w = desc_k_sw128(smem_u32(smem + s * p.stage_bytes)), d_wlo = d_w + (C::TILE >> 4);
           const uint64_t shift = (uint64_t)(j * a.dil) * 8;  // tap j reads the window shifted by j*dil frames
           const uint32_t first = (cb == 0 && j == 0) ? 0u : 1u;
           if (has_lo)
             issue_kblock<true>(d_main, d_cross, d_ahi + shift, d_alo + shift, d_w, d_wlo, first, &S.empty[s],
-                               &S.accfull[set]);
+                               &S.accfull[set], C::IDESC);
           else
             issue_kblock<false>(d_main, d_cross, d_ahi + shift, d_alo + shift, d_w, d_wlo, first, &S.empty[s],
-                                &S.accfull[set]);
+                                &S.accfull[set], C::IDESC);
           if (++s == ns) s = 0, ++r;
         }
         if (!ok) break;
@@ -748,35 +782,31 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
     }
     if (!ok) *abort_flag = 1;
   } else if (warp >= 8) {
-    // drainers + epilogue: thread = output frame t0 + row (its TMEM lane)
-    const int quarter = warp & 3;
+    // drainers + epilogue: thread = output frame t0 + row (its TMEM lane), channels
+    // 64 half .. 64 half + 63 of the tile
+    const int quarter = warp & 3, half = (warp - 8) >> 2;
     const int row = quarter * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t lane_base = ((uint32_t)(quarter * 32) << 16) + 64u * half;
     int gkb = 0, it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < p.ntiles; tile += gridDim.x, ++it) {
       int t0, co0, b, g;
       tile_of(tile, t0, co0, b, g);
       const int cp = it & 1;
-      float acc[BN];
+      float acc[64];
 #pragma unroll
-      for (int c = 0; c < BN; ++c) acc[c] = 0.f;
+      for (int c = 0; c < 64; ++c) acc[c] = 0.f;
       for (int kb = 0; kb < nk; ++kb, ++gkb) {
-        const int set = gkb % NSET;
-        if (!ready(&S.accfull[set], (uint32_t)(gkb / NSET) & 1, 5)) {
+        const int set = gkb % C::NSET;
+        if (!ready(&S.accfull[set], (uint32_t)(gkb / C::NSET) & 1, 5)) {
           ok = false;
           break;
         }
         fence_after();
-        float m[BN];
-        tmem_ld64(tmem + lane_base + 64u * set, m);
-#pragma unroll
-        for (int j = 0; j < BN; ++j) acc[j] = __fadd_rn(acc[j], m[j]);
+        fold64<BNW == 64>(tmem + lane_base + (uint32_t)BNW * set, acc);
         const bool last = kb == nk - 1;  // its MMAs are the tile's last: the remainder sum is final
         if (last) {
-          tmem_ld64(tmem + lane_base + C_CROSS + 64u * cp, m);
-#pragma unroll
-          for (int j = 0; j < BN; ++j) acc[j] = __fadd_rn(acc[j], m[j]);
+          fold64<BNW == 64>(tmem + lane_base + C::C_CROSS + (uint32_t)BNW * cp, acc);
         }
         fence_before();
         __syncwarp();
@@ -787,7 +817,7 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
       }
       if (!ok) break;
       const int t = t0 + row;
-      if (t < a.t_out) store_row<ACT, SNAKE>(a, acc, b, g, co0, t);
+      if (t < a.t_out) store_row<ACT, SNAKE>(a, acc, b, g, co0 + 64 * half, t);
     }
     if (!ok) *abort_flag = 1;
   }
@@ -872,10 +902,16 @@ GatherFn gather_fn(bool sn) {
 }
 
 // token-major inputs come from the DiT (no snake): that layout is built without one
+template <int ACT, int BNW>
+WindowFn window_fn_w(bool sn, int layout) {
+  if (layout == 1)
+    return sn ? wk::conv_window_kernel<ACT, true, 1, BNW> : wk::conv_window_kernel<ACT, false, 1, BNW>;
+  return sn ? nullptr : wk::conv_window_kernel<ACT, false, 2, BNW>;
+}
+
 template <int ACT>
-WindowFn window_fn(bool sn, int layout) {
-  if (layout == 1) return sn ? wk::conv_window_kernel<ACT, true, 1> : wk::conv_window_kernel<ACT, false, 1>;
-  return sn ? nullptr : wk::conv_window_kernel<ACT, false, 2>;
+WindowFn window_fn(bool sn, int layout, bool wide) {
+  return wide ? window_fn_w<ACT, 128>(sn, layout) : window_fn_w<ACT, 64>(sn, layout);
 }
 
 }  // namespace
@@ -924,9 +960,13 @@ extern "C" int cv3_conv1d_tc(const float* x, int64_t xsb, int64_t xsc, int64_t x
                    (int)k, (int)stride, (int)dilation, (int)pad_left, (int)groups, (int)(ci_pad / 32), wt_lo ? 1 : 0};
   const bool sn = snake_alpha != nullptr;
 
-  // window kernel: stride 1 and a window of <= 256 rows
+  // window kernel: stride 1 and a window of <= 256 rows; tiles 128 channels wide where a
+  // group has that many
   const int64_t frames = BM + (k - 1) * dilation;
-  const int64_t ntiles = nx * ny * nz;
+  const bool wide = cout_g >= 128;
+  const int bnw = wide ? 128 : BN;
+  const int64_t nyw = (cout_g + bnw - 1) / bnw;
+  const int64_t ntiles = nx * nyw * nz;
   if (g_window_enabled && stride == 1 && ntiles < (1LL << 31)) {
     wk::WinArgs p{};
     CUtensorMap mx;
@@ -941,21 +981,29 @@ extern "C" int cv3_conv1d_tc(const float* x, int64_t xsb, int64_t xsc, int64_t x
     WindowFn fn = nullptr;
     if (layout) {
       switch (act) {
-        case -1: fn = window_fn<-1>(sn, layout); break;
-        case CV3_ACT_MISH: fn = window_fn<CV3_ACT_MISH>(sn, layout); break;
-        case CV3_ACT_ELU: fn = window_fn<CV3_ACT_ELU>(sn, layout); break;
-        default: fn = window_fn<CV3_ACT_LEAKY_RELU>(sn, layout); break;
+        case -1: fn = window_fn<-1>(sn, layout, wide); break;
+        case CV3_ACT_MISH: fn = window_fn<CV3_ACT_MISH>(sn, layout, wide); break;
+        case CV3_ACT_ELU: fn = window_fn<CV3_ACT_ELU>(sn, layout, wide); break;
+        default: fn = window_fn<CV3_ACT_LEAKY_RELU>(sn, layout, wide); break;
       }
+    }
+    CUtensorMap mww = mw, mwlw = mwl;  // weight tiles of the window kernel: bnw rows
+    if (fn && wide) {
+      rc = make_w_map(&mww, wt, cout, k * ci_pad, bnw);
+      if (rc) return rc;
+      rc = make_w_map(&mwlw, wt_lo ? wt_lo : wt, cout, k * ci_pad, bnw);
+      if (rc) return rc;
     }
     p.c = a;
     p.frames = (int)frames;
     p.abytes = (int)((frames * 128 + 1023) / 1024 * 1024);
     p.nx = (int)nx;
-    p.ny = (int)ny;
+    p.ny = (int)nyw;
     p.ntiles = (int)ntiles;
     // the weight ring takes what the windows leave: deep rings hide the L2 latency of
-    // one 8 KB (16 KB with the remainder) tile per K block
-    p.stage_bytes = wt_lo ? 2 * TILE_B : TILE_B;
+    // one 8 / 16 KB (x2 with the remainder) tile per K block
+    const int tile_w = bnw * BK * 4;
+    p.stage_bytes = wt_lo ? 2 * tile_w : tile_w;
     const int fixed = wk::bars_at(p.abytes, 0, 0) + (int)sizeof(wk::Bars) + 1024;
     p.nstages = std::min(wk::MAX_STAGES, (SMEM_MAX - fixed) / p.stage_bytes);
     const int smem = fixed + p.nstages * p.stage_bytes;
@@ -964,7 +1012,8 @@ extern "C" int cv3_conv1d_tc(const float* x, int64_t xsb, int64_t xsc, int64_t x
       if (rc) return rc;
       const int grid = (int)std::min<int64_t>(ntiles, cv3::sm_count());
       g_last_path = layout;
-      fn<<<grid, wk::THREADS, smem, cv3::as_stream(stream)>>>(mw, mwl, mx, p);
+      fn<<<grid, wide ? wk::Wide<128>::THREADS : wk::Wide<64>::THREADS, smem, cv3::as_stream(stream)>>>(mww, mwlw, mx,
+                                                                                                   p);
       return cv3::check_launch("conv1d_tc");
     }
   }
