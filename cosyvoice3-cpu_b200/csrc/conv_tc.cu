@@ -48,6 +48,7 @@
 #include <algorithm>
 #include <cstring>
 
+#include "snake.cuh"
 #include "tc_common.cuh"
 
 namespace {
@@ -86,34 +87,42 @@ struct ConvArgs {
   int has_lo;
 };
 
-// bias, activation, snake of one accumulator value (channel parameters passed in)
-template <int ACT, bool SNAKE>
-__device__ __forceinline__ float epilogue_value(const ConvArgs& a, float acc, float bias, float alpha) {
+// bias and activation of one accumulator value (channel parameters passed in)
+template <int ACT>
+__device__ __forceinline__ float pre_snake(const ConvArgs& a, float acc, float bias) {
   float o = acc;
   if (a.bias) o = __fadd_rn(o, bias);
   if (ACT >= 0) o = act_apply(ACT, a.act_p, o);
-  if (SNAKE) {  // snake (cv3cpu/models/hift.py: x + 1/(alpha + 1e-9) * sin(alpha x)^2)
-    const float sn = sinf(alpha * o);
-    o = o + (1.0f / (alpha + 1e-9f)) * (sn * sn);
-  }
   return o;
 }
 
-// Epilogue of one output frame t (this thread's row): 64 channels from co0 of group g.
-// Works in chunks of 16 channels whose bias / alpha / residual loads are all issued
-// before the chunk's stores: y may alias the residual, so a load placed after a store
-// could not be hoisted and every channel would pay a full load latency.
-template <int ACT, bool SNAKE>
-__device__ __forceinline__ void store_row(const ConvArgs& a, const float (&acc)[BN], int b, int g, int co0, int t) {
-  constexpr int CH = 16;
+// ... then the snake (cv3cpu/ops.py:77-81), whose squared sine is the branch-free form
+// (FAST) or the one valid for any argument
+template <int ACT, bool SNAKE, bool FAST>
+__device__ __forceinline__ float epilogue_value(const ConvArgs& a, float acc, float bias, float alpha) {
+  const float o = pre_snake<ACT>(a, acc, bias);
+  if (!SNAKE) return o;
+  const float z = __fmul_rn(alpha, o);
+  return cv3snake::snake_combine(o, cv3snake::inv_alpha(alpha), FAST ? cv3snake::sin_sq_fast(z) : cv3snake::sin_sq(z));
+}
+
+// Epilogue of one output frame t (this thread's row): NC channels from co0 of group g,
+// in chunks of CH channels whose bias / alpha / residual loads are all issued before the
+// chunk's stores (y may alias the residual, so a load placed after a store could not be
+// hoisted and every channel would pay a full load latency).  A chunk first checks its
+// snake arguments against the branch-free sine's range, so that its values are one
+// straight line of independent arithmetic that interleaves (sinf's range branch
+// serialised them); the values replace acc in place.
+template <int ACT, bool SNAKE, int CH = 16, int NC = BN>
+__device__ __forceinline__ void store_row(const ConvArgs& a, float (&acc)[NC], int b, int g, int co0, int t) {
   const bool yvec = a.ysc == 1 && a.yst % 4 == 0 && ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0) &&
                     (a.ysb % 4 == 0) && (a.cout_g % 4 == 0) &&
                     (!a.res || (reinterpret_cast<uintptr_t>(a.res) & 15) == 0);
   const int ch0 = g * a.cout_g + co0;  // first output channel (global index)
   const int64_t ybase = (int64_t)b * a.ysb + (int64_t)ch0 * a.ysc + (int64_t)t * a.yst;
-  const int nco = min(BN, a.cout_g - co0);
+  const int nco = min(NC, a.cout_g - co0);
 #pragma unroll
-  for (int c0 = 0; c0 < BN; c0 += CH) {
+  for (int c0 = 0; c0 < NC; c0 += CH) {
     float bv[CH], av[CH], rv[CH];
 #pragma unroll
     for (int e = 0; e < CH; ++e) {
@@ -121,7 +130,20 @@ __device__ __forceinline__ void store_row(const ConvArgs& a, const float (&acc)[
       bv[e] = (a.bias && in) ? __ldg(a.bias + ch0 + c0 + e) : 0.f;
       av[e] = (SNAKE && in) ? __ldg(a.alpha + ch0 + c0 + e) : 0.f;
     }
-    if (yvec && nco == BN) {
+    bool big = false;
+    if (SNAKE) {
+#pragma unroll
+      for (int e = 0; e < CH; ++e)
+        big |= !(fabsf(__fmul_rn(av[e], pre_snake<ACT>(a, acc[c0 + e], bv[e]))) <= cv3snake::FAST_MAX);
+    }
+    if (SNAKE && big) {
+#pragma unroll
+      for (int e = 0; e < CH; ++e) acc[c0 + e] = epilogue_value<ACT, SNAKE, false>(a, acc[c0 + e], bv[e], av[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < CH; ++e) acc[c0 + e] = epilogue_value<ACT, SNAKE, true>(a, acc[c0 + e], bv[e], av[e]);
+    }
+    if (yvec && nco == NC) {
       // token-major y: this thread's channels are contiguous
       if (a.res) {
 #pragma unroll
@@ -138,8 +160,7 @@ __device__ __forceinline__ void store_row(const ConvArgs& a, const float (&acc)[
         float o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int c = c0 + 4 * q + e;
-          o[e] = epilogue_value<ACT, SNAKE>(a, acc[c], bv[4 * q + e], av[4 * q + e]);
+          o[e] = acc[c0 + 4 * q + e];
           if (a.res) o[e] = __fadd_rn(o[e], rv[4 * q + e]);
         }
         *reinterpret_cast<float4*>(a.y + ybase + c0 + 4 * q) = make_float4(o[0], o[1], o[2], o[3]);
@@ -153,7 +174,7 @@ __device__ __forceinline__ void store_row(const ConvArgs& a, const float (&acc)[
 #pragma unroll
       for (int e = 0; e < CH; ++e) {
         if (c0 + e < nco) {
-          float o = epilogue_value<ACT, SNAKE>(a, acc[c0 + e], bv[e], av[e]);
+          float o = acc[c0 + e];
           if (a.res) o = __fadd_rn(o, rv[e]);
           a.y[ybase + (int64_t)(c0 + e) * a.ysc] = o;
         }
@@ -415,13 +436,15 @@ constexpr int FMAX = 256;                // window rows (TMA box limit)
 // Tile width: 64 output channels, or 128 where a group has that many (one MMA then does
 // twice the work: at these widths the tensor pipe is paced by the reduction length, not
 // by N).  TMEM holds NSET main accumulators (K blocks in flight between MMA and drain)
-// and two remainder accumulators (even / odd tiles), BNW columns each; the drain warps
-// (two per TMEM lane quarter at BNW = 128) fold 64 channels each.
+// and two remainder accumulators (even / odd tiles), BNW columns each.  Eight drain warps,
+// two per TMEM lane quarter, fold BNW / 2 channels each: two warps per SM sub-partition
+// hide each other's TMEM-load and barrier latencies.
 template <int BNW>
 struct Wide {
-  static constexpr int THREADS = BNW == 64 ? 384 : 512;
+  static constexpr int THREADS = 512;
   static constexpr int NSET = BNW == 64 ? 6 : 2;
-  static constexpr int NDRAIN = BNW / 16;  // drain warps
+  static constexpr int NDRAIN = 8;         // drain warps
+  static constexpr int DW = BNW / 2;       // channels per drain warp
   static constexpr uint32_t C_CROSS = NSET * BNW;
   static constexpr int TILE = BNW * BK * 4;  // one BNW x 32 weight tile
   static constexpr uint32_t IDESC = idesc_tf32(BM, BNW);
@@ -526,23 +549,15 @@ __device__ __forceinline__ float4 split_lo(float4 h) {
   return make_float4(h.x - tf32_hi(h.x), h.y - tf32_hi(h.y), h.z - tf32_hi(h.z), h.w - tf32_hi(h.w));
 }
 
-// acc[j] += TMEM row columns j (64 of them), rounded to nearest; one 64-column load, or
-// two of 32 where registers are tighter (the 128-wide tile's 512 threads)
-template <bool ONE_LOAD>
-__device__ __forceinline__ void fold64(uint32_t taddr, float (&acc)[64]) {
-  if (ONE_LOAD) {
-    float m[64];
-    tmem_ld64(taddr, m);
+// acc[j] += TMEM row columns j (NC of them), rounded to nearest, in loads of 32 columns
+template <int NC>
+__device__ __forceinline__ void fold_cols(uint32_t taddr, float (&acc)[NC]) {
 #pragma unroll
-    for (int j = 0; j < 64; ++j) acc[j] = __fadd_rn(acc[j], m[j]);
-  } else {
+  for (int h = 0; h < NC / 32; ++h) {
+    float m[32];
+    tmem_ld32(taddr + 32 * h, m);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float m[32];
-      tmem_ld32(taddr + 32 * h, m);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) acc[32 * h + j] = __fadd_rn(acc[32 * h + j], m[j]);
-    }
+    for (int j = 0; j < 32; ++j) acc[32 * h + j] = __fadd_rn(acc[32 * h + j], m[j]);
   }
 }
 
@@ -783,19 +798,19 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
     if (!ok) *abort_flag = 1;
   } else if (warp >= 8) {
     // drainers + epilogue: thread = output frame t0 + row (its TMEM lane), channels
-    // 64 half .. 64 half + 63 of the tile
+    // DW half .. DW half + DW - 1 of the tile
     const int quarter = warp & 3, half = (warp - 8) >> 2;
     const int row = quarter * 32 + lane;
-    const uint32_t lane_base = ((uint32_t)(quarter * 32) << 16) + 64u * half;
+    const uint32_t lane_base = ((uint32_t)(quarter * 32) << 16) + (uint32_t)(C::DW * half);
     int gkb = 0, it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < p.ntiles; tile += gridDim.x, ++it) {
       int t0, co0, b, g;
       tile_of(tile, t0, co0, b, g);
       const int cp = it & 1;
-      float acc[64];
+      float acc[C::DW];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+      for (int c = 0; c < C::DW; ++c) acc[c] = 0.f;
       for (int kb = 0; kb < nk; ++kb, ++gkb) {
         const int set = gkb % C::NSET;
         if (!ready(&S.accfull[set], (uint32_t)(gkb / C::NSET) & 1, 5)) {
@@ -803,10 +818,10 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
           break;
         }
         fence_after();
-        fold64<BNW == 64>(tmem + lane_base + (uint32_t)BNW * set, acc);
+        fold_cols<C::DW>(tmem + lane_base + (uint32_t)BNW * set, acc);
         const bool last = kb == nk - 1;  // its MMAs are the tile's last: the remainder sum is final
         if (last) {
-          fold64<BNW == 64>(tmem + lane_base + C::C_CROSS + (uint32_t)BNW * cp, acc);
+          fold_cols<C::DW>(tmem + lane_base + C::C_CROSS + (uint32_t)BNW * cp, acc);
         }
         fence_before();
         __syncwarp();
@@ -817,7 +832,7 @@ conv_window_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_const
       }
       if (!ok) break;
       const int t = t0 + row;
-      if (t < a.t_out) store_row<ACT, SNAKE>(a, acc, b, g, co0 + 64 * half, t);
+      if (t < a.t_out) store_row<ACT, SNAKE, BNW == 64 ? 16 : 8, C::DW>(a, acc, b, g, co0 + C::DW * half, t);
     }
     if (!ok) *abort_flag = 1;
   }

@@ -1,8 +1,10 @@
 // Elementwise activations and row reductions (norms, softmax), fp32.
 // Each follows the arithmetic order of the reference op it replaces
 // (cv3cpu/ops.py:30-118); transcendentals use CUDA's IEEE-accurate single
-// precision functions (no fast-math).
+// precision functions (no fast-math), the snake its own branch-free squared sine
+// (snake.cuh).
 #include "common.cuh"
+#include "snake.cuh"
 
 namespace {
 
@@ -70,8 +72,7 @@ __global__ void snake_kernel(const float* __restrict__ x, const float* __restric
        i += (int64_t)gridDim.x * blockDim.x) {
     const float a = alpha[(i / t) % channels];
     const float v = x[i];
-    const float s = sinf(a * v);
-    y[i] = v + (1.0f / (a + 1e-9f)) * (s * s);
+    y[i] = cv3snake::snake_combine(v, cv3snake::inv_alpha(a), cv3snake::sin_sq(__fmul_rn(a, v)));
   }
 }
 

@@ -177,3 +177,18 @@ def test_conv_tc_snake_and_residual():
     res = rng.normal(size=(2, 128, 333)).astype(np.float32)
     got = _conv_tc(x, w, b, pad=(6, 0), residual=res, fp16_weights=True)
     assert rel_err(got, res + _ref(x, w, b, pad=(6, 0))) < TOL
+
+
+@pytest.mark.parametrize("cout", [64, 128])
+def test_conv_tc_snake_large_arguments(cout):
+    """Snake epilogue with alpha x beyond the branch-free sine's range (|alpha x| > 8192) in
+    some chunks of a thread's channels and not in others: those chunks take CUDA's sinf."""
+    rng = np.random.default_rng(cout)
+    x, w, b = _data(rng, 2, cout, 500, cout, cout, 3, fp16=True)
+    alpha = np.where(np.arange(cout) % 24 < 8, rng.uniform(3000, 9000, size=cout),
+                     rng.uniform(0.2, 2.0, size=cout)).astype(np.float32)
+    got = _conv_tc(x, w, b, dilation=3, pad=(6, 0), alpha=alpha, fp16_weights=True)
+    pre = _ref(x, w, b, dilation=3, pad=(6, 0))
+    assert (np.abs(alpha[None, :, None] * pre) > 8192).any()
+    ref = np.stack([nx.snake(r, alpha) for r in pre])
+    assert rel_err(got, ref) < TOL

@@ -57,6 +57,30 @@ def test_snake(ops, rng):
     assert rel_err(ops.snake(x, a), nx.snake(x, a)) < 1e-6
 
 
+def test_snake_sine_against_cuda_sinf(ops, rng):
+    """The snake's branch-free squared sine (|alpha x| <= 8192; CUDA's sinf beyond, and for
+    inf / nan) against float64 and against the same formula on CUDA's sinf (torch.sin):
+    per element within 2 ulp of the terms, and on the whole as accurate as sinf."""
+    import torch
+    a = np.exp(rng.uniform(np.log(1e-3), np.log(3e4), size=64)).astype(np.float32)
+    x = (rng.normal(size=(64, 4097)) * np.exp(rng.uniform(-3, 3, size=(64, 4097)))).astype(np.float32)
+    x[0, :4] = [np.inf, -np.inf, np.nan, 0.0]
+    got = ops.snake(x, a)
+    ad, xd = torch.from_numpy(a).cuda()[:, None], torch.from_numpy(x).cuda()
+    cuda = (xd + (1.0 / (ad + 1e-9)) * torch.sin(ad * xd) ** 2).cpu().numpy()
+    fin = np.isfinite(x)
+    assert np.array_equal(np.isnan(got[~fin]), np.isnan(cuda[~fin]))
+    a64 = a.astype(np.float64)[:, None]
+    inv = 1.0 / (a64 + np.float32(1e-9))
+    ref = x + inv * np.sin(np.float32(a)[:, None] * x).astype(np.float64) ** 2
+    bound = 2.0 ** -22 * (np.abs(x) + inv)
+    err, err_cuda = np.abs(got - ref)[fin], np.abs(cuda - ref)[fin]
+    assert (err <= bound[fin]).all(), float((err / bound[fin]).max())
+    assert err.mean() <= 1.5 * err_cuda.mean() and err.max() <= 2.0 * err_cuda.max()
+    big = np.abs(np.float32(a)[:, None] * x) > 8192
+    assert big.sum() > 1000 and (~big).sum() > 1000  # both forms ran
+
+
 @pytest.mark.parametrize("rows,dim", [(1, 896), (7, 1024), (300, 17), (2, 6761)])
 def test_norms_and_softmax(ops, rng, rows, dim):
     x = (rng.normal(size=(rows, dim)) * 3).astype(np.float32)
