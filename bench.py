@@ -171,6 +171,30 @@ def cpu_sample(W, req, decode_steps: int = 4):
                               "hift_s": t_hift}
 
 
+def cpu_full_utterance(W, req):
+    """Seconds of one complete config-4 utterance on the CPU oracle, nothing extrapolated:
+    the LM prompt, prefill and all 250 greedy steps (head + argmax each), the flow's
+    conditioning and its 10-step CFG Euler solve at 2 x 650 frames, and the 500-frame
+    vocoder (chunk 250).  ``cpu_sample`` models the same utterance from a few timed pieces;
+    this measurement is what that model is checked against."""
+    import oracle.stages as st
+    meta = W.meta
+    lm, flow, hift = st.SpeechLM(W, meta), st.Flow(W, meta), st.HiFT(W, meta)
+    v = req.voice
+    t0 = time.perf_counter()
+    x0 = lm.prompt_embedding(req.text_ids, req.prompt_ids, v.speech_token.tolist())
+    toks, _ = lm.generate_greedy(x0, TOKENS)
+    t_lm = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    mel = flow.inference(np.asarray(toks), v.speech_token, v.mel, v.embedding)
+    t_flow = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    wav = hift.inference(mel, chunk=250)
+    t_hift = time.perf_counter() - t0
+    return {"s": t_lm + t_flow + t_hift, "lm_s": t_lm, "flow_s": t_flow, "hift_s": t_hift,
+            "tokens": len(toks), "samples": int(np.asarray(wav).size)}
+
+
 def host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -215,13 +239,22 @@ def run_reference(args, rank: int, world: int) -> None:
     """The reference arm: the CPU implementation of the path (the oracle port of cv3cpu's
     kernel layer and stages) on all host cores.  Each step times one bounded sample of a
     config-4 utterance (``cpu_sample``); ``ms_per_step`` is that sample's wall time and
-    ``value`` the utterance rate the sample implies (see CPU_SAMPLE_DESC)."""
+    ``value`` the utterance rate the sample implies (see CPU_SAMPLE_DESC).  Once per run,
+    before the steps, one complete utterance is synthesised with nothing extrapolated
+    (``cpu_full_utterance``, skipped by ``--no-full-utterance``); the line reports its time
+    and the model's error against it for the same utterance."""
     if rank != 0:
         return
     _limits = use_all_host_threads()
     synth = pkg("synth")
     W = synth.synthetic_weights("balanced")
     reqs = make_requests(range(UTTS), W.meta)
+    full = None
+    if not args.no_full_utterance:
+        full = cpu_full_utterance(W, reqs[0])
+        modelled, _, _ = cpu_sample(W, reqs[0])
+        full["modelled_s"] = modelled
+        full["model_error"] = modelled / full["s"] - 1.0
     per, walls = [], []
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
@@ -240,6 +273,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port",
                          "sample": CPU_SAMPLE_DESC, "modelled_s_per_utterance": per_utt},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "full_utterance": full,
     }), flush=True)
 
 
@@ -823,6 +857,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-full-utterance", action="store_true",
+                    help="reference arm: skip the one complete (unextrapolated) CPU utterance")
     ap.add_argument("--no-stages", action="store_true", help="skip the config 1-3 and 5 stage numbers")
     ap.add_argument("--sweep", action="store_true",
                     help="config 5 alone: all 256 utterances, sharded over the ranks, every batch timed")
