@@ -842,7 +842,7 @@ def run_lm_step(args) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--lm-step", type=int, default=0, metavar="B",
-                    help="time the LM decode step alone at batch B (1..8)")
+                    help="time the LM decode step alone at batch B (1..32)")
     ap.add_argument("--persistent", action="store_true",
                     help="with --lm-step: the persistent decode kernel (every step in one launch)")
     ap.add_argument("--trace", action="store_true",

@@ -174,7 +174,8 @@ class ConvTC:
 
 
 class DecodeGemv:
-    """A q8 weight streamed by ``cv3_q8_decode_gemv`` for <= 8 activation rows.
+    """A q8 weight streamed by ``cv3_q8_decode_gemv_mma`` for <= 32 activation rows
+    (``cv3_q8_decode_gemv`` for <= 8 where the tensor-core kernel does not apply).
 
     Small matrices split K over several CTAs so every SM streams part of the
     weight; the split needs a private partial-sum workspace and per-row-tile
@@ -209,7 +210,7 @@ class DecodeGemv:
             self.splits = max(1, min(64, -(-target_ctas // tiles), self.kp // 64))
             kps = -(-(self.kp // self.splits) // 16) * 16
             eff = -(-self.kp // kps)
-        self.ws = D.empty((eff * 8 * self.n,)) if eff > 1 else None
+        self.ws = D.empty((eff * (32 if self.mma else 8) * self.n,)) if eff > 1 else None
         self.cnt = torch.zeros(tiles, dtype=torch.int32, device="cuda") if eff > 1 else None
 
     def __call__(self, x: int, m: int, y: int, residual: int = None, ldx: int = None, ldy: int = None,

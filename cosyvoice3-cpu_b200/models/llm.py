@@ -24,7 +24,7 @@ torch = D.torch
 
 SPEECH_TOKEN_SIZE = 6561
 SAMPLER_MAX_TOP_K = 32  # cv3_sample_select's largest top_k (larger ones use the host sampler)
-MAX_DECODE_BATCH = 8    # sequences one decode engine advances together
+MAX_DECODE_BATCH = 32   # sequences one decode engine advances together (the decode GEMV's row limit)
 ENDOFPROMPT_ID = 151646
 
 

@@ -432,7 +432,7 @@ class DecodeEngine:
             L.gu(self.n.data_ptr(), B, self.gu.data_ptr(), stream=st)
             call("cv3_swiglu", self.gu.data_ptr(), B, c.intermediate_size, self.act.data_ptr(), st)
             L.down(self.act.data_ptr(), B, self.h.data_ptr(), residual=self.h.data_ptr(), stream=st)
-        if self.fast_head is not None and B <= 8:
+        if self.fast_head is not None and B <= 32:
             self.fast_head(self.h.data_ptr(), B, self.logits.data_ptr(), stream=st)
             self.select_and_feed(st, logits_ready=True)
             return

@@ -88,13 +88,18 @@ int cv3_q8_decode_gemv(const float* x, int64_t m, int64_t k, int64_t ldx, const 
 
 /* cv3_q8_decode_gemv on the tensor cores (warp MMA m16n8k16: int8 weights are
  * exact bf16, the activations enter as three exact bf16 parts, the fp16 group
- * scale multiplies each 64-wide group's fp32 partial sum).  Same operands,
- * fusions and output as cv3_q8_decode_gemv; needs K a multiple of 64 with no
- * padding (kp == k), K <= 5120, 16-byte aligned x rows.  `splits` > 1 (no
- * fused RMSNorm) spreads K over that many CTAs per row tile with a
- * deterministic reduction: workspace >= splits*n*8 floats and counters (one
- * per 16-row tile, or 32-row when n >= 4096 and a CTA takes at most 16 scale
- * groups) zeroed once, left zeroed. */
+ * scale multiplies each 64-wide group's fp32 partial sum), for 1..32 activation
+ * rows (the batch-32 decode of config 5; a row's result does not depend on m).
+ * Same operands, fusions and output as cv3_q8_decode_gemv; needs K a multiple
+ * of 64 with no padding (kp == k), K <= 5120, 16-byte aligned x rows; a CTA
+ * stages its rows' K range in shared memory, so m > 8 with a long K needs
+ * `splits` (CV3_ERR_VALUE otherwise).  `splits` > 1 (no fused RMSNorm) spreads
+ * K over that many CTAs per row tile with a deterministic reduction (a cluster
+ * for up to 8 splits); more than 8 splits need workspace >= splits*n*8*B floats
+ * (B = 1 for m <= 8, 2 for m <= 16, else 4) and counters (one per 16-row tile,
+ * or 32-row when n >= 4096 and a CTA takes at most 16 scale groups) zeroed
+ * once, left zeroed.  Replaces the per-token ops.linear calls of
+ * qwen2.py:156-177 and llm.py:74-78 (quant.py:156-204 with m <= 32). */
 int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int64_t ldx, const int8_t* q,
                            const uint16_t* scales, int64_t n, int64_t kp, const float* bias, const float* residual,
                            const float* norm_w, float eps, int swiglu, float* y, int64_t ldy, int64_t splits,

@@ -1,8 +1,9 @@
 """The fused decode GEMV (cv3_q8_decode_gemv) and the decode engine's fused path.
 
 Kernel vs the oracle: RMSNorm-fused input, bias, residual, SwiGLU row pairs,
-K split over CTAs (deterministic reduction), 1..8 rows; tolerance 1e-5 (the
-int8 dequantisation is exact).  Engine: a small LM whose every linear is q8,
+K split over CTAs (deterministic reduction), 1..32 rows (8-sequence column
+blocks; a row's result does not depend on how many rows share the call);
+tolerance 1e-5 (the int8 dequantisation is exact).  Engine: a small LM whose every linear is q8,
 so the fused path runs, against the oracle's greedy decode.
 """
 
@@ -24,9 +25,11 @@ def _dg(qt, **kw):
 
 
 @pytest.mark.parametrize("n,k", [(1152, 896), (896, 896), (896, 4864), (9728, 896), (6761, 896), (96, 100)])
-@pytest.mark.parametrize("m", [1, 3, 8])
+@pytest.mark.parametrize("m", [1, 3, 8, 12, 32])
 def test_decode_gemv_plain_and_residual(n, k, m):
     import torch
+    if m > 8 and k % 64:
+        pytest.skip("K not a multiple of 64: the CUDA-core GEMV, which takes up to 8 rows")
     rng = np.random.default_rng(n + k + m)
     w = (rng.normal(size=(n, k)) * 0.02).astype(np.float32)
     qt = pkg("quant").make_qtensor(w)
@@ -34,7 +37,7 @@ def test_decode_gemv_plain_and_residual(n, k, m):
     x = rng.normal(size=(m, k)).astype(np.float32)
     b = rng.normal(size=n).astype(np.float32)
     r = rng.normal(size=(m, n)).astype(np.float32)
-    g = _dg(qt, bias=torch.from_numpy(b).cuda())
+    g = _dg(qt, bias=torch.from_numpy(b).cuda(), mma_splits=5 if (k > 1024 and m > 8) else 1)
     xd, y = torch.from_numpy(x).cuda(), torch.from_numpy(r).cuda()
     for _ in range(2):                       # twice: the split counters must be left at zero
         y.copy_(torch.from_numpy(r))
@@ -43,7 +46,7 @@ def test_decode_gemv_plain_and_residual(n, k, m):
         assert rel_err(y.cpu().numpy(), nx.qmatmul(x, oq, b) + r) < 1e-5
 
 
-@pytest.mark.parametrize("m", [1, 5, 8])
+@pytest.mark.parametrize("m", [1, 5, 8, 20, 32])
 def test_decode_gemv_fused_norm_and_swiglu(m):
     import torch
     C = pkg("models._common")
@@ -166,3 +169,37 @@ def test_decode_rope_attention_matches_separate_kernels(m, cap):
     code = ctypes.c_int(-1)
     L.load().cv3_decode_attention_status(ctypes.byref(code))
     assert code.value == 0
+
+
+@pytest.mark.parametrize("m", [9, 17, 32])
+def test_decode_gemv_rows_independent_of_batch(m):
+    """Each row of an m-row call equals the same row computed alone, bit for bit (the
+    batch-32 decode must choose the ids a sequence gets alone)."""
+    import torch
+    rng = np.random.default_rng(100 + m)
+    n, k = 1152, 896
+    w = (rng.normal(size=(n, k)) * 0.02).astype(np.float32)
+    qt = pkg("quant").make_qtensor(w)
+    nw = torch.from_numpy((1 + 0.1 * rng.normal(size=k)).astype(np.float32)).cuda()
+    b = torch.from_numpy(rng.normal(size=n).astype(np.float32)).cuda()
+    g = _dg(qt, bias=b, norm_w=nw, eps=1e-6)
+    x = torch.from_numpy(rng.normal(size=(m, k)).astype(np.float32)).cuda()
+    y = torch.empty(m, n, device="cuda")
+    g(x.data_ptr(), m, y.data_ptr())
+    y1 = torch.empty(1, n, device="cuda")
+    for i in (0, m // 2, m - 1):
+        g(x[i:i + 1].data_ptr(), 1, y1.data_ptr())
+        torch.cuda.synchronize()
+        assert torch.equal(y[i], y1[0]), i
+
+
+def test_decode_gemv_long_k_many_rows_needs_splits():
+    """32 rows of K = 4864 do not fit one CTA's shared memory unsplit: a ValueError, not a launch."""
+    import torch
+    rng = np.random.default_rng(5)
+    qt = pkg("quant").make_qtensor((rng.normal(size=(896, 4864)) * 0.02).astype(np.float32))
+    g = _dg(qt)
+    x = torch.zeros(32, 4864, device="cuda")
+    y = torch.zeros(32, 896, device="cuda")
+    with pytest.raises(ValueError):
+        g(x.data_ptr(), 32, y.data_ptr())

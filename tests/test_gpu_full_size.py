@@ -167,8 +167,8 @@ def test_config5_dit_forward_batch2_1500_frames():
 
 def test_config5_lm_batch32_ids_equal_batch1():
     """Config 5 decodes 32 sequences per GPU: the full-size balanced LM on 32 prompts of
-    40-80 text ids (four graph-replayed groups of eight) gives every sequence exactly the
-    ids it gets when decoded alone."""
+    40-80 text ids (one graph-replayed batch of 32: the decode GEMV streams each weight once
+    for all 32 rows) gives every sequence exactly the ids it gets when decoded alone."""
     W = pkg("synth").synthetic_weights("balanced", stages=("llm",))
     lm = pkg("models.llm").CosyVoice3LM(_device(W))
     rng = np.random.default_rng(32)
