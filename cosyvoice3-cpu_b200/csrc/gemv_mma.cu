@@ -290,20 +290,18 @@ q8_gemv_mma_kernel(MmaArgs a) {
           mma_group(A, bp, s0[i][t], s1[i][t], acc[0][t]);
         }
       } else {
-        // several blocks: each row tile's weights widened once, then every block's
-        // activations split against them (the split repeats per row tile)
+        // several blocks: every row tile's weights widened once, then each block's
+        // activations split once and multiplied into all row tiles
+        uint32_t A[RT][4][4];
 #pragma unroll
-        for (int t = 0; t < RT; ++t) {
-          uint32_t A[4][4];
-          weight_fragments(w0[i][t], w1[i][t], A);
+        for (int t = 0; t < RT; ++t) weight_fragments(w0[i][t], w1[i][t], A[t]);
 #pragma unroll
-          for (int nb = 0; nb < NB; ++nb) {
-            uint32_t bp[3][4][2];
-            float dummy = 0.f;
-            split_activations(xs + (MAXB * nb + g) * kw + 64 * G + 16 * c,
-                              a.norm_w ? nws + 64 * G + 16 * c : nullptr, t == 0 ? ssq[nb] : dummy, bp);
-            mma_group(A, bp, s0[i][t], s1[i][t], acc[nb][t]);
-          }
+        for (int nb = 0; nb < NB; ++nb) {
+          uint32_t bp[3][4][2];
+          split_activations(xs + (MAXB * nb + g) * kw + 64 * G + 16 * c, a.norm_w ? nws + 64 * G + 16 * c : nullptr,
+                            ssq[nb], bp);
+#pragma unroll
+          for (int t = 0; t < RT; ++t) mma_group(A[t], bp, s0[i][t], s1[i][t], acc[nb][t]);
         }
       }
     }

@@ -58,12 +58,14 @@ __global__ void rope_qkv_append_kernel(const float* __restrict__ qkv, int64_t ld
 constexpr int AT = 256;
 constexpr int DM = 64;
 constexpr int HPG = 8;       // most query heads sharing one kv head (Qwen2-0.5B: 7)
-constexpr int HC = 1;        // query heads per CTA (measured: 1 beats 2 and 7)
 constexpr int PG = AT / 16;  // key groups of the V pass (16 lanes x float4 per group)
 
-// One CTA per (sequence, kv head, query head of that group): the query heads
+// One CTA per (sequence, kv head, HC query heads of that group): the query heads
 // of a group are spread over hpg / HC CTAs, each reading the group's cached
-// key/value rows (the repeats hit L2).  Scores: one key per
+// key/value rows (the repeats hit L2).  HC is the smallest of 1, 2, 4, 8 whose
+// grid fits one CTA per SM (measured at 8 sequences: 1 head per CTA beats 2 and
+// 7; at 32 sequences 1 head per CTA would need four waves).  A head's arithmetic
+// does not depend on HC.  Scores: one key per
 // thread (its 256-byte row as 16 independent float4 loads) against the CTA's
 // heads.  Softmax: one warp per head.  V pass: 16 key groups x 16 lanes of
 // float4 dims, eight keys' value loads in flight per group, per-group partial
@@ -82,10 +84,11 @@ constexpr int PG = AT / 16;  // key groups of the V pass (16 lanes x float4 per 
 // dependency wait).  So before the wait, bulk copies bring up to `kmax` of those
 // key and value rows into shared memory, overlapping the qkv projection; after
 // the wait the position is read again and the staged rows are used only if it is
-// unchanged (else every row is read from global memory).  Staged keys are read
-// with the float4 columns rotated by the row index (conflict-free banks), which
-// changes only the order of a dot product's sums.
-template <bool ROPE>
+// unchanged (else every row is read from global memory).  Every key's dot product
+// takes its float4 columns rotated by the row index (conflict-free banks for the
+// staged rows), wherever the row is read from, so a score does not depend on how
+// many rows were staged (the staging budget varies with the cache capacity and HC).
+template <bool ROPE, int HC>
 __global__ void __launch_bounds__(AT)
 decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ cosT,
                         const float* __restrict__ sinT, const int* __restrict__ pos, float* kc, float* vc,
@@ -180,18 +183,17 @@ decode_attention_kernel(const float* __restrict__ q, int64_t ldq, const float* _
   }
   for (int j = tid; j < m; j += AT) {
     float4 kr[DM / 4];
-    int rot = 0;  // staged rows: float4 column c of kr holds column (c + rot) % 16
+    const int rot = j & (DM / 4 - 1);  // float4 column c of kr holds column (c + rot) % 16
     if (j < ns) {
-      rot = j & (DM / 4 - 1);
 #pragma unroll
       for (int c = 0; c < DM / 4; ++c) kr[c] = sk[(int64_t)j * (DM / 4) + ((c + rot) & (DM / 4 - 1))];
     } else if (j == pnew) {
 #pragma unroll
-      for (int c = 0; c < DM / 4; ++c) kr[c] = knew[c];
+      for (int c = 0; c < DM / 4; ++c) kr[c] = knew[(c + rot) & (DM / 4 - 1)];
     } else {
       const float4* src = reinterpret_cast<const float4*>(kb + (int64_t)j * DM);
 #pragma unroll
-      for (int c = 0; c < DM / 4; ++c) kr[c] = src[c];
+      for (int c = 0; c < DM / 4; ++c) kr[c] = src[(c + rot) & (DM / 4 - 1)];
     }
 #pragma unroll
     for (int h = 0; h < HC; ++h) {
@@ -363,8 +365,17 @@ int launch_decode_attention(bool rope, const float* q, int64_t ldq, const float*
   CV3_REQUIRE(head_dim == DM, CV3_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (built for %d)",
               (long long)head_dim, DM);
   CV3_REQUIRE(heads / kv_heads <= HPG, CV3_ERR_UNSUPPORTED, "decode_attention: more than %d heads per kv head", HPG);
-  const int64_t score_bytes = HC * cap * 4;
-  CV3_REQUIRE(cap > 0 && score_bytes <= 150 * 1024, CV3_ERR_UNSUPPORTED, "decode_attention: cap too large");
+  const int64_t hpg = heads / kv_heads;
+  // query heads per CTA: the fewest that keep the grid within one CTA per SM
+  int HC = 8;
+  for (int hc : {1, 2, 4}) {
+    if (batch * kv_heads * ((hpg + hc - 1) / hc) <= cv3::sm_count()) {
+      HC = hc;
+      break;
+    }
+  }
+  CV3_REQUIRE(cap > 0 && cap * 4 <= 150 * 1024, CV3_ERR_UNSUPPORTED, "decode_attention: cap too large");
+  while (HC > 1 && HC * cap * 4 > 150 * 1024) HC /= 2;  // long caches: fewer heads per CTA, more waves
   // staged key/value rows (RoPE launches): as many as fit next to the scores in 200 KB
   const int64_t kv_off = (HC * cap + 3) / 4 * 4;  // floats, 16-byte aligned
   const int64_t kmax = rope ? std::min<int64_t>(cap, (200 * 1024 - kv_off * 4) / (2 * DM * 4)) : 0;
@@ -372,10 +383,17 @@ int launch_decode_attention(bool rope, const float* q, int64_t ldq, const float*
   CV3_REQUIRE(((uintptr_t)q & 15) == 0 && ((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0,
               CV3_ERR_VALUE, "decode_attention: 16-byte aligned tensors required");
   if (batch == 0) return CV3_OK;
-  auto fn = rope ? decode_attention_kernel<true> : decode_attention_kernel<false>;
+  using Fn = void (*)(const float*, int64_t, const float*, const float*, const int*, float*, float*, const int*, int,
+                      int, int64_t, float, float*, int, int64_t);
+  Fn fn;
+  switch (HC) {
+    case 1: fn = rope ? decode_attention_kernel<true, 1> : decode_attention_kernel<false, 1>; break;
+    case 2: fn = rope ? decode_attention_kernel<true, 2> : decode_attention_kernel<false, 2>; break;
+    case 4: fn = rope ? decode_attention_kernel<true, 4> : decode_attention_kernel<false, 4>; break;
+    default: fn = rope ? decode_attention_kernel<true, 8> : decode_attention_kernel<false, 8>; break;
+  }
   int rc = cv3::allow_smem((const void*)fn, (int)smem);
   if (rc) return rc;
-  const int64_t hpg = heads / kv_heads;
   dim3 grid((unsigned)kv_heads, (unsigned)batch, (unsigned)((hpg + HC - 1) / HC));
   return cv3::check_launch("decode_attention",
                            cv3::launch_dep(fn, grid, dim3(AT), (size_t)smem, cv3::as_stream(stream), q, ldq,
