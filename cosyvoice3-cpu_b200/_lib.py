@@ -29,6 +29,12 @@ SIGNATURES = {
     "cv3_abi_version": [],
     "cv3_launch_count": [],
     "cv3_device_info": [P, P, P],
+    "cv3_device_alloc": [I64, P],
+    "cv3_device_free": [P],
+    "cv3_memcpy": [P, P, I64, I32, P],
+    "cv3_memset": [P, I32, I64, P],
+    "cv3_stream_synchronize": [P],
+    "cv3_mem_get_info": [P, P],
     "cv3_q8_linear": [P, I64, I64, I64, P, P, I64, I64, P, P, P, I64, P],
     "cv3_f32_linear": [P, I64, I64, I64, P, I64, I64, P, P, P, I64, P],
     "cv3_q8_dequant": [P, P, I64, I64, I64, P, P],

@@ -85,3 +85,54 @@ extern "C" int cv3_device_info(int* sm, int* major, int* minor) {
   if (minor) *minor = p.minor;
   return CV3_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Device memory, copies and stream order for hosts without a GPU framework: the
+// NumPy + ctypes host of the ops layer allocates its device arrays and moves data
+// through these (plain cudaMalloc / cudaMemcpyAsync, one copy per call).
+// ---------------------------------------------------------------------------
+
+extern "C" int cv3_device_alloc(int64_t bytes, void** ptr) {
+  CV3_REQUIRE(ptr && bytes >= 0, CV3_ERR_VALUE, "device_alloc: bad arguments");
+  *ptr = nullptr;
+  if (bytes == 0) return CV3_OK;
+  CV3_CUDA(cudaMalloc(ptr, (size_t)bytes));
+  return CV3_OK;
+}
+
+extern "C" int cv3_device_free(void* ptr) {
+  if (ptr) CV3_CUDA(cudaFree(ptr));
+  return CV3_OK;
+}
+
+// kind: 0 host -> device, 1 device -> host, 2 device -> device; stream-ordered (a copy
+// from or to pageable host memory returns once the host side may be reused)
+extern "C" int cv3_memcpy(void* dst, const void* src, int64_t bytes, int kind, void* stream) {
+  CV3_REQUIRE(bytes >= 0 && kind >= 0 && kind <= 2 && (bytes == 0 || (dst && src)), CV3_ERR_VALUE,
+              "memcpy: bad arguments");
+  if (bytes == 0) return CV3_OK;
+  const cudaMemcpyKind k = kind == 0 ? cudaMemcpyHostToDevice
+                                     : (kind == 1 ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice);
+  CV3_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, k, cv3::as_stream(stream)));
+  return CV3_OK;
+}
+
+extern "C" int cv3_memset(void* dst, int value, int64_t bytes, void* stream) {
+  CV3_REQUIRE(bytes >= 0 && (bytes == 0 || dst), CV3_ERR_VALUE, "memset: bad arguments");
+  if (bytes == 0) return CV3_OK;
+  CV3_CUDA(cudaMemsetAsync(dst, value, (size_t)bytes, cv3::as_stream(stream)));
+  return CV3_OK;
+}
+
+extern "C" int cv3_stream_synchronize(void* stream) {
+  CV3_CUDA(cudaStreamSynchronize(cv3::as_stream(stream)));
+  return CV3_OK;
+}
+
+extern "C" int cv3_mem_get_info(int64_t* free_bytes, int64_t* total_bytes) {
+  size_t f = 0, t = 0;
+  CV3_CUDA(cudaMemGetInfo(&f, &t));
+  if (free_bytes) *free_bytes = (int64_t)f;
+  if (total_bytes) *total_bytes = (int64_t)t;
+  return CV3_OK;
+}

@@ -36,7 +36,7 @@ ACT = {"silu": 0, "sigmoid": 1, "gelu_tanh": 2, "gelu": 3, "mish": 4, "elu": 5,
 def _unary(name: str, x, param: float = 0.0):
     host = D.is_host(x)
     xd = D.dev(x)
-    y = torch.empty_like(xd)
+    y = D.empty_like(xd)
     call("cv3_unary", ACT[name], float(param), D.ptr(xd), xd.numel(), D.ptr(y), D.stream())
     return D.out(y, host)
 
@@ -78,7 +78,7 @@ def snake(x, alpha, eps: float = 1e-9):
     c = xd.shape[0] if xd.dim() > 1 else 1
     if ad.numel() != c:
         raise ValueError(f"snake: {ad.numel()} alphas for {c} channels")
-    y = torch.empty_like(xd)
+    y = D.empty_like(xd)
     call("cv3_snake", D.ptr(xd), D.ptr(ad), 1, c, xd.numel() // max(c, 1), D.ptr(y), D.stream())
     return D.out(y, host)
 
@@ -94,7 +94,7 @@ def softmax(x, axis: int = -1):    # cv3cpu/ops.py:84
     host = D.is_host(x)
     xd = D.dev(x)
     rows, dim = _rows(xd, axis)
-    y = torch.empty_like(xd)
+    y = D.empty_like(xd)
     call("cv3_softmax", D.ptr(xd), rows, dim, 0, D.ptr(y), D.stream())
     return D.out(y, host)
 
@@ -103,7 +103,7 @@ def log_softmax(x, axis: int = -1):   # cv3cpu/ops.py:90
     host = D.is_host(x)
     xd = D.dev(x)
     rows, dim = _rows(xd, axis)
-    y = torch.empty_like(xd)
+    y = D.empty_like(xd)
     call("cv3_softmax", D.ptr(xd), rows, dim, 1, D.ptr(y), D.stream())
     return D.out(y, host)
 
@@ -112,7 +112,7 @@ def rms_norm(x, weight, eps: float = 1e-6):   # cv3cpu/ops.py:101
     host = D.is_host(x)
     xd, wd = D.dev(x), D.dev(weight)
     rows, dim = _rows(xd, -1)
-    y = torch.empty_like(xd)
+    y = D.empty_like(xd)
     call("cv3_rms_norm", D.ptr(xd), D.ptr(wd), rows, dim, float(eps), D.ptr(y), D.stream())
     return D.out(y, host)
 
@@ -123,7 +123,7 @@ def layer_norm(x, weight=None, bias=None, eps: float = 1e-5):   # cv3cpu/ops.py:
     wd = D.dev(weight) if weight is not None else None
     bd = D.dev(bias) if bias is not None else None
     rows, dim = _rows(xd, -1)
-    y = torch.empty_like(xd)
+    y = D.empty_like(xd)
     call("cv3_layer_norm", D.ptr(xd), D.ptr(wd), D.ptr(bd), rows, dim, float(eps), D.ptr(y), D.stream())
     return D.out(y, host)
 
@@ -173,33 +173,33 @@ def linear(x, weight: Weight, bias=None, residual=None, out=None):
 def _table_kind(table):
     if isinstance(table, QTensor):
         return 3 if table.kind == "q4" else 2
-    t = table if isinstance(table, torch.Tensor) else np.asarray(table)
-    return 1 if t.dtype in (np.float16, torch.float16) else 0
+    t = table if D.is_device(table) else np.asarray(table)
+    return 1 if D.is_half(t) else 0
 
 
 def embedding(table: Weight, ids):
     """Row gather widened to fp32; IndexError outside the table; cv3cpu/ops.py:126-144."""
-    host_ids = not isinstance(ids, torch.Tensor)
+    host_ids = not D.is_device(ids)
     rows = int(table.shape[0])
     if host_ids:
         ids = np.asarray(ids)
         if ids.size and (int(ids.min()) < 0 or int(ids.max()) >= rows):
             raise IndexError(f"token id {int(ids.max())} is outside the {rows}-row embedding table")
-    idd = D.dev(ids, torch.int64).reshape(-1)
+    idd = D.dev(ids, D.I64).reshape(-1)
     kind = _table_kind(table)
     if kind >= 2:
         t = table.to_device()
         dim, kp = int(t.shape[1]), t.padded_k
         tab, sc = t.q, t.scales
     else:
-        tab = D.dev(table, torch.float16 if kind == 1 else torch.float32)
+        tab = D.dev(table, D.F16 if kind == 1 else D.F32)
         dim, kp, sc = int(tab.shape[1]), int(tab.shape[1]), None
     shape = tuple(ids.shape) if host_ids else tuple(ids.shape)
     y = D.empty((idd.numel(), dim))
     call("cv3_embedding", D.ptr(tab), kind, D.ptr(sc), rows, dim, kp, D.ptr(idd), idd.numel(),
          D.ptr(y), dim, None, D.stream())
     y = y.reshape(shape + (dim,))
-    dev_table = isinstance(table, torch.Tensor) or (isinstance(table, QTensor) and isinstance(table.q, torch.Tensor))
+    dev_table = D.is_device(table) or (isinstance(table, QTensor) and D.is_device(table.q))
     return D.out(y, host_ids and not dev_table)
 
 
@@ -308,7 +308,7 @@ def interpolate_linear(x, size: int, align_corners: bool = False):   # cv3cpu/op
     y = D.empty((c, size))
     # keep every temporary alive until the launch is queued (a freed block could
     # otherwise be handed to the next temporary of the same call)
-    i0d, i1d, wd = D.dev(i0, torch.int64), D.dev(i1, torch.int64), D.dev(w)
+    i0d, i1d, wd = D.dev(i0, D.I64), D.dev(i1, D.I64), D.dev(w)
     call("cv3_interpolate_linear", D.ptr(xd), c, t, D.ptr(i0d), D.ptr(i1d), D.ptr(wd), size, D.ptr(y), D.stream())
     return D.out(y, host)
 
@@ -343,6 +343,9 @@ def stft(x, n_fft: int, hop: int, win, center: bool = True, pad_mode: str = "ref
     if host:
         s = s.cpu().numpy()
         return (s[:nb] + 1j * s[nb:]).astype(np.complex64)
+    if torch is None or not isinstance(s, torch.Tensor):
+        raise TypeError("a complex device result needs PyTorch tensors: pass NumPy input (NumPy output) "
+                        "or use stft_stacked")
     return torch.complex(s[:nb], s[nb:])
 
 
@@ -362,11 +365,12 @@ def istft_stacked(spec, n_fft: int, hop: int, win, mode: int = 0, limit: float =
     wd = D.dev(win)
     call("cv3_istft", D.ptr(sd), mode, b, frames, n_fft, hop, D.ptr(wd), float(limit), off,
          D.ptr(scratch), D.ptr(y), n_out, D.stream())
-    if length is not None:
-        if n_out >= length:
-            y = y[..., :length]
-        else:
-            y = torch.nn.functional.pad(y, (0, length - n_out))
+    if length is not None and length != n_out:
+        if torch is not None and isinstance(y, torch.Tensor):
+            y = y[..., :length] if n_out >= length else torch.nn.functional.pad(y, (0, length - n_out))
+        else:   # device arrays of the NumPy host: trimmed or padded on the host
+            h = y.numpy()
+            y = h[..., :length] if n_out >= length else np.pad(h, [(0, 0)] * (h.ndim - 1) + [(0, length - n_out)])
     return y
 
 

@@ -54,11 +54,11 @@ class QTensor:
         return int(self.scales.shape[1]) * self.block
 
     def to_device(self, device="cuda") -> "QTensor":
-        import torch
-        if isinstance(self.q, torch.Tensor) and self.q.is_cuda:
+        from . import _dev as D
+        if D.is_device(self.q):
             return self
-        q = torch.from_numpy(np.ascontiguousarray(self.q)).to(device)
-        s = torch.from_numpy(np.ascontiguousarray(self.scales).view(np.int16)).to(device)
+        q = D.upload(np.asarray(self.q))
+        s = D.upload(np.ascontiguousarray(self.scales).view(np.int16))
         return QTensor(self.kind, q, s, tuple(self.shape), self.block, self.orig_shape)
 
     def dequant_rows(self, r0: int, r1: int) -> np.ndarray:

@@ -57,7 +57,7 @@ class TorchMT19937:
 
     def next_u32(self, n: int, device: bool = False):
         """The next ``n`` tempered 32-bit words (cv3cpu/torch_rng.py:71-86)."""
-        out = torch.empty(n, dtype=torch.int32, device="cuda")
+        out = D.empty((n,), D.I32)
         if n:
             call("cv3_torch_u32", self.seed, self.pos, n, D.ptr(out), D.stream())
         self.pos += n
@@ -65,7 +65,7 @@ class TorchMT19937:
 
     def random_float64(self, n: int, device: bool = False):
         """``n`` double uniforms from word pairs, first word high (cv3cpu/torch_rng.py:93-102)."""
-        out = torch.empty(n, dtype=torch.float64, device="cuda")
+        out = D.empty((n,), D.F64)
         if n:
             call("cv3_torch_rand64", self.seed, self.pos, n, D.ptr(out), D.stream())
         self.pos += 2 * n

@@ -57,6 +57,20 @@ unsigned long long cv3_launch_count(void);
 /* SM count and compute capability of the current device. */
 int cv3_device_info(int* sm_count, int* cc_major, int* cc_minor);
 
+/* Device memory and copies for a host without a GPU framework (the NumPy +
+ * ctypes host of the ops layer, which replaces cv3cpu/ops.py's NumPy arrays by
+ * device arrays made here): cudaMalloc / cudaFree of `bytes` (0: *ptr = NULL),
+ * one cudaMemcpyAsync per call (kind 0 host->device, 1 device->host, 2
+ * device->device; pageable host memory makes the copy return once the host side
+ * may be reused), cudaMemsetAsync, cudaStreamSynchronize, cudaMemGetInfo.  No
+ * counterpart in the reference (NumPy owns its memory there). */
+int cv3_device_alloc(int64_t bytes, void** ptr);
+int cv3_device_free(void* ptr);
+int cv3_memcpy(void* dst, const void* src, int64_t bytes, int kind, void* stream);
+int cv3_memset(void* dst, int value, int64_t bytes, void* stream);
+int cv3_stream_synchronize(void* stream);
+int cv3_mem_get_info(int64_t* free_bytes, int64_t* total_bytes);
+
 /* ------------------------------------------------------------------ */
 /* linear layers                                                        */
 /* ------------------------------------------------------------------ */

@@ -6,7 +6,7 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import REFERENCE, have_reference, pkg
+from conftest import REFERENCE, REPO, have_reference, pkg
 
 import oracle.numerics as nx
 
@@ -135,3 +135,31 @@ def test_synthetic_small_model_geometry():
     assert syn["llm.llm_decoder.weight"].shape == (456, 128)
     assert syn["hift.conv_pre.weight"].shape == (64, 80, 5)
     assert syn["hift.f0_predictor.condnet.1.weight"].shape == (512, 512, 3)
+
+
+def test_ops_import_without_pytorch_and_fail_loudly_without_a_device():
+    """The NumPy host: with ``import torch`` blocked, ops / quant / torch_rng import and pick
+    the library's own device memory; on a machine without a GPU an op raises (there is no
+    CPU path)."""
+    import subprocess
+    import sys
+    child = (
+        "import importlib, sys\n"
+        "sys.modules['torch'] = None\n"
+        "sys.path.insert(0, sys.argv[1])\n"
+        "import numpy as np\n"
+        "D = importlib.import_module('cosyvoice3-cpu_b200._dev')\n"
+        "ops = importlib.import_module('cosyvoice3-cpu_b200.ops')\n"
+        "importlib.import_module('cosyvoice3-cpu_b200.quant')\n"
+        "importlib.import_module('cosyvoice3-cpu_b200.torch_rng')\n"
+        "assert D.BACKEND == 'numpy' and D.torch is None\n"
+        "try:\n"
+        "    ops.silu(np.ones(4, np.float32))\n"
+        "    print('RAN')\n"
+        "except RuntimeError as e:\n"
+        "    print('RAISED', e)\n")
+    p = subprocess.run([sys.executable, "-c", child, REPO], capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stderr[-3000:]
+    out = p.stdout.strip().splitlines()[-1]
+    # without a GPU the op must raise; on a GPU machine it runs
+    assert out.startswith("RAISED no CUDA device") or out == "RAN", out
