@@ -712,6 +712,16 @@ def run_kernel(args) -> None:
         fn()
     torch.cuda.synchronize()
     print("kernel %s: 5 launches done" % args.kernel, flush=True)
+    if args.time:
+        reps = 20
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        print(json.dumps({"kernel": args.kernel, "us_per_launch": round(e0.elapsed_time(e1) / reps * 1e3, 2)}),
+              flush=True)
 
 
 def trace_persistent(eng, B):
@@ -852,6 +862,8 @@ def main():
     ap.add_argument("--slice", action="store_true", help="profiling slice (see run_slice)")
     ap.add_argument("--kernel", choices=["ff1", "ff1q8", "ff1q8p", "attention", "conv", "gemv"],
                     help="run one hot kernel alone at its bench shape (for ncu captures)")
+    ap.add_argument("--time", action="store_true",
+                    help="with --kernel: also time 20 more launches (CUDA events on the launching stream)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
