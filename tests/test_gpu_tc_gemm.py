@@ -311,3 +311,19 @@ def test_ln_modulate_planes_match_fp32():
     torch.cuda.synchronize()
     ref = y.cpu().numpy().astype(np.float64)
     assert np.all(np.abs(_unplanes(pl, ex, rows, d) - ref) <= np.abs(ref) * 2.0 ** -21 + 1e-30)
+
+
+@pytest.mark.parametrize("k,bound", [(1024, 3e-6), (2048, 5e-6), (4096, 1e-5)])
+def test_split_gemm_error_growth_with_k(k, bound):
+    """The precision claim behind the split GEMM's accumulator layout (two hi*hi chains of
+    alternate K blocks plus the cross terms, added in fp32 by the epilogue): the error
+    against fp64 grows slowly with K -- measured 0.9-1.9e-6 at the DiT shapes -- and stays
+    inside the 1e-5 bar at K = 4096 (during development a single accumulator over all
+    products measured 3.3e-5 there: the tensor core truncates each addition into it)."""
+    rng = np.random.default_rng(k)
+    a = rng.normal(size=(512, k)).astype(np.float32)
+    b = (rng.normal(size=(384, k)) * 0.02).astype(np.float32)
+    ref = a.astype(np.float64) @ b.astype(np.float64).T
+    err = rel_err(_run(a, b, kind="presplit_b"), ref)
+    print(f"K={k}: {err:.2e} of max")
+    assert err < bound, err
