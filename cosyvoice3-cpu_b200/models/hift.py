@@ -21,7 +21,7 @@ import numpy as np
 from .. import _dev as D
 from .. import ops
 from .._lib import call
-from ._common import ConvTC
+from ._common import ConvTC, Graph
 
 torch = D.torch
 
@@ -59,6 +59,7 @@ class HiFTGenerator:
         self.window = ops.hann_window(self.n_fft)
         self._win = None
         self._convs = {}
+        self._graphs = {}   # input shape -> (graph, static input, static output, dither buffer)
         self.noise_seed = int(m.get("noise_seed", 0))
         self._src_noise = None
         self._user_noise = False
@@ -146,6 +147,7 @@ class HiFTGenerator:
         """Use a caller-supplied dither buffer ``[samples, harmonics]`` (hift.py:83-88)."""
         self._src_noise = D.dev(np.asarray(buf, np.float32) if D.is_host(buf) else buf)
         self._user_noise = True
+        self._graphs.clear()    # captured passes read the previous buffer
 
     def excitation(self, f0):
         """``[B, T]`` F0 -> ``[B, up*T]`` merged harmonic source."""
@@ -228,11 +230,52 @@ class HiFTGenerator:
             x = self.spectral_chunked(mel, s_stft, chunk, context)
         return ops.istft_stacked(x, self.n_fft, self.hop_len, self.win(), mode=1, limit=self.audio_limit)
 
-    def inference_batch(self, mels, chunk: Optional[int] = None, context: int = 64):
-        """Device ``[B, 80, T]`` mels -> ``[B, 480T]`` waveforms."""
+    GRAPH_SHAPES = 2    # captured input shapes kept (each holds its activations' memory)
+
+    def inference_batch(self, mels, chunk: Optional[int] = None, context: int = 64, use_graph: bool = False):
+        """Device ``[B, 80, T]`` mels -> ``[B, 480T]`` waveforms.
+
+        ``use_graph``: the whole pass (F0 convs, source, ~100 convolution and elementwise
+        launches, iSTFT) replays a CUDA graph captured for this input shape, so its cost is
+        the kernels' alone; the first call of a shape runs eagerly (building the convolution
+        operands, tables and the dither buffer), the second captures.  The result is a new
+        tensor either way and equals the eager pass bit for bit."""
         mel = D.dev(mels)
+        if use_graph and chunk is None:
+            key = tuple(int(s) for s in mel.shape)
+            entry = self._graphs.get(key)
+            if entry is None:
+                entry = self._capture(mel, key)
+            if entry is not None:
+                g, x_in, y, _noise = entry
+                x_in.copy_(mel)
+                g.replay()
+                return y.clone()
         f0 = self.f0_predict(mel)
         return self.decode(mel, self.excitation(f0), chunk=chunk, context=context)
+
+    def _capture(self, mel, key):
+        """Warm up eagerly, then capture one pass on a static input of ``mel``'s shape.  The
+        entry keeps the dither buffer the graph reads alive (a longer utterance may replace
+        the module's buffer later)."""
+        if key not in getattr(self, "_warm", set()):
+            self._warm = getattr(self, "_warm", set()) | {key}
+            return None     # this call runs eagerly; the next one captures
+        x_in = D.empty(key)
+        x_in.copy_(mel)
+        out = {}
+
+        def body(_stream):
+            f0 = self.f0_predict(x_in)
+            out["y"] = self.decode(x_in, self.excitation(f0))
+
+        g = Graph()
+        g.capture(body)
+        if len(self._graphs) >= self.GRAPH_SHAPES:
+            self._graphs.pop(next(iter(self._graphs)))
+        entry = (g, x_in, out["y"], self._src_noise)
+        self._graphs[key] = entry
+        return entry
 
     def inference(self, mel, chunk: Optional[int] = 250, context: int = 64):
         """``(80, T)`` mel -> ``(480 T,)`` waveform (hift.py:212-218).

@@ -187,7 +187,7 @@ class CosyVoice3CUDA:
             conds.append(cond)
         x = flow.solve_batch(mus, spks, conds)                                        # [U, 80, N]
         mel = x[:, :, pf:].contiguous()
-        return hift.inference_batch(mel), toks
+        return hift.inference_batch(mel, use_graph=True), toks
 
     def synthesize_greedy_batch(self, requests: Sequence[Request], n_tokens: int = 250, to_host: bool = True):
         """Greedy synthesis of a batch of utterances, each producing ``n_tokens`` speech tokens."""
