@@ -163,3 +163,25 @@ def test_ops_import_without_pytorch_and_fail_loudly_without_a_device():
     out = p.stdout.strip().splitlines()[-1]
     # without a GPU the op must raise; on a GPU machine it runs
     assert out.startswith("RAISED no CUDA device") or out == "RAN", out
+
+
+def test_device_array_views_without_a_device():
+    """The NumPy host's device arrays: shapes, views and byte offsets (no memory touched:
+    an array made on a given address owns nothing and frees nothing)."""
+    D = pkg("_dev")
+    a = D.DeviceArray((4, 3, 5), np.float32, _ptr=0x10000)
+    assert a.numel() == 60 and a.nbytes == 240 and a.dim() == 3
+    r = a.reshape(-1, 5)
+    assert r.shape == (12, 5) and r.data_ptr() == 0x10000
+    assert a.reshape((2, 30)).shape == (2, 30)
+    with pytest.raises(ValueError):
+        a.reshape(7, -1, 3)
+    assert a.unsqueeze(0).shape == (1, 4, 3, 5) and a.unsqueeze(-1).shape == (4, 3, 5, 1)
+    assert a[2].shape == (3, 5) and a[2].data_ptr() == 0x10000 + 2 * 15 * 4
+    assert a[-1].data_ptr() == 0x10000 + 3 * 15 * 4
+    with pytest.raises(IndexError):
+        a[4]
+    with pytest.raises(TypeError):
+        a[1:2]
+    h = D.DeviceArray((8,), np.float16, _ptr=0x20000)
+    assert h.nbytes == 16 and D.is_half(h) and D.is_device(h) and not D.is_host(h)
