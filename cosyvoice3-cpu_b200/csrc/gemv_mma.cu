@@ -213,11 +213,11 @@ q8_gemv_mma_kernel(MmaArgs a) {
   // constants of the epilogue and the RMSNorm weight (staged behind x) do not depend on
   // the previous kernels either
   const int k4 = kw >> 2;
-  float* nws = xs + SEQ * kw;  // [kw] RMSNorm weight (only with norm_w; then kw == k)
+  float* nws = xs + SEQ * kw;  // [kw] RMSNorm weight of this CTA's K range (only with norm_w)
   if (a.norm_w)
     for (int i = tid; i < k4; i += NWARP * 32)
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(nws + 4 * i)),
-                   "l"(a.norm_w + 4 * i)
+                   "l"(a.norm_w + 64 * g0 + 4 * i)
                    : "memory");
   // epilogue outputs of this thread: index tid + 256 e -> (row inside the CTA, sequence)
   float bias_v[EPI], bias_u[EPI];
@@ -340,11 +340,15 @@ q8_gemv_mma_kernel(MmaArgs a) {
     for (int w = 0; w < NWARP; ++w) v += red[w][rt][bb];
     tot[rt][bb] = v;
   }
+  // this CTA's sum of squares per sequence (its K range); with K splits split 0 adds the
+  // others' in split order below, before the row factor is formed
+  __shared__ float sqt[SEQ];
   if (a.norm_w && tid < SEQ) {
     float q = 0.f;
 #pragma unroll
     for (int w = 0; w < NWARP; ++w) q += sq[w][tid];
-    rnorm[tid] = 1.0f / sqrtf(q / (float)a.k + a.eps);
+    sqt[tid] = q;
+    if (gridDim.y == 1) rnorm[tid] = 1.0f / sqrtf(q / (float)a.k + a.eps);
   }
   if (gridDim.y > 1 && a.cluster) {
     // the K splits of this row tile are one cluster: split 0 adds the others' sums from
@@ -352,6 +356,18 @@ q8_gemv_mma_kernel(MmaArgs a) {
     // them and leave; no global round trip
     float v[EPI];
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (a.norm_w && blockIdx.y == 0 && tid < SEQ) {
+      float q = sqt[tid];
+      const uint32_t local = (uint32_t)__cvta_generic_to_shared(&sqt[tid]);
+      for (int sp = 1; sp < (int)gridDim.y; ++sp) {
+        uint32_t remote;
+        float pv;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(sp));
+        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(remote) : "memory");
+        q += pv;
+      }
+      rnorm[tid] = 1.0f / sqrtf(q / (float)a.k + a.eps);
+    }
 #pragma unroll
     for (int e = 0; e < EPI; ++e) {
       const int idx = tid + NWARP * 32 * e, rt = idx / SEQ, bb = idx - rt * SEQ;
@@ -452,8 +468,7 @@ extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int6
   CV3_REQUIRE(swiglu ? (n % 2 == 0 && ldy >= n / 2 && !residual) : ldy >= n, CV3_ERR_VALUE,
               "q8_decode_gemv_mma: bad output layout");
   CV3_REQUIRE(!norm_w || ((uintptr_t)norm_w & 15) == 0, CV3_ERR_VALUE, "q8_decode_gemv_mma: norm weight alignment");
-  CV3_REQUIRE(splits >= 1 && splits <= 16 && (splits == 1 || !norm_w), CV3_ERR_VALUE,
-              "q8_decode_gemv_mma: 1..16 K splits, and no split with a fused RMSNorm");
+  CV3_REQUIRE(splits >= 1 && splits <= 16, CV3_ERR_VALUE, "q8_decode_gemv_mma: 1..16 K splits");
   const int ngroups = (int)(k / 64);
   const int gsplit = (ngroups + (int)splits - 1) / (int)splits;
   const int nsplit = (ngroups + gsplit - 1) / gsplit;
@@ -462,6 +477,8 @@ extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int6
   const int rows = wide ? 32 : 16;
   const int tiles = (int)((n + rows - 1) / rows);
   const bool cluster = nsplit > 1 && nsplit <= 8;  // portable cluster size
+  CV3_REQUIRE(!norm_w || nsplit == 1 || cluster, CV3_ERR_VALUE,
+              "q8_decode_gemv_mma: a fused RMSNorm takes at most 8 K splits (one cluster)");
   if (nsplit > 1 && !cluster) {
     CV3_REQUIRE(workspace && counters && workspace_floats >= (int64_t)nsplit * n * seq, CV3_ERR_VALUE,
                 "q8_decode_gemv_mma: more than 8 K splits need a workspace of splits*n*8*ceil(m/8) floats "
@@ -471,7 +488,7 @@ extern "C" int cv3_q8_decode_gemv_mma(const float* x, int64_t m, int64_t k, int6
             gsplit, workspace, counters, cluster ? 1 : 0};
   const int smem = (seq + (norm_w ? 1 : 0)) * 64 * gsplit * 4;
   // the kernel's static shared memory: warp partials and totals per (row, sequence), sums of squares
-  const int static_smem = (NWARP + 1) * rows * seq * 4 + NWARP * seq * 4 + seq * 4 + 64;
+  const int static_smem = (NWARP + 1) * rows * seq * 4 + NWARP * seq * 4 + 2 * seq * 4 + 64;
   CV3_REQUIRE(smem + static_smem <= 226 * 1024 && (nb == 1 || gsplit <= NWARP * 4), CV3_ERR_VALUE,
               "q8_decode_gemv_mma: %lld rows x %d columns per CTA do not fit in shared memory: split K", (long long)m,
               64 * gsplit);

@@ -194,13 +194,14 @@ class DecodeGemv:
         self.eps = float(eps)
         self.swiglu = 1 if swiglu else 0
         # the tensor-core kernel takes every unpadded K up to 5120 (all of Qwen2's linears);
-        # mma_splits > 1 splits K over CTAs (not with a fused RMSNorm, which needs whole rows).
+        # mma_splits > 1 splits K over CTAs (with a fused RMSNorm only as one cluster of at
+        # most 8, whose first CTA adds the others' sums of squares).
         # Measured in the batch-8 decode graph: the down projection (896 rows, K 4864) gains
         # from 2 splits (112 CTAs instead of 56), 4 splits and the out projection lose.
         self.mma = self.kp == self.k and self.k % 64 == 0 and self.k <= 5120
         if self.mma:
             groups = self.k // 64
-            self.splits = max(1, min(int(mma_splits), groups)) if norm_w is None else 1
+            self.splits = max(1, min(int(mma_splits), groups, 8 if norm_w is not None else groups))
             gs = -(-groups // self.splits)
             eff = -(-groups // gs)
             # the kernel's row tiles: 32 rows for n >= 4096 with <= 16 scale groups per CTA, else 16

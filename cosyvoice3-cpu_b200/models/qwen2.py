@@ -257,6 +257,10 @@ def pk_sm_count() -> int:
 class DecodeEngine:
     """Batched greedy decode, one CUDA graph per step.
 
+    The fused qkv projection runs as ``QKV_SPLITS`` K splits of one cluster (its 1152 rows
+    alone fill only half the SMs; the splits' sums of squares for the folded RMSNorm are
+    added by the cluster's first CTA).
+
     Device state per sequence: ``pos`` (position of the token being fed),
     ``lens`` (cache length after it is appended), ``next_ids`` (token fed next)
     and ``history`` (tokens chosen so far).  A step runs every layer on the
@@ -264,6 +268,8 @@ class DecodeEngine:
     first argmax over the speech tokens, bookkeeping) and the embedding gather
     of the chosen tokens into the next step's input.
     """
+
+    QKV_SPLITS = 2
 
     def __init__(self, model: Qwen2Model, head_w, speech_emb, speech_tokens: int, batch: int, cap: int,
                  max_steps: int):
@@ -304,7 +310,7 @@ class DecodeEngine:
                   model._t(p + "mlp.up_proj.weight"), L.down._keep[0]]
             if all(isinstance(w, QTensor) and w.kind == "q8" for w in ws):   # (q4 layers: generic path)
                 gu = model.w.cache((model.prefix + p + "gate_up_interleaved",), lambda ws=ws: interleave_rows(ws[2], ws[3]))
-                self.fast.append((DecodeGemv(ws[0], L.qkv._keep[1], L.ln1, c.rms_norm_eps),
+                self.fast.append((DecodeGemv(ws[0], L.qkv._keep[1], L.ln1, c.rms_norm_eps, mma_splits=self.QKV_SPLITS),
                                   DecodeGemv(ws[1]),
                                   DecodeGemv(gu, norm_w=L.ln2, eps=c.rms_norm_eps, swiglu=True),
                                   DecodeGemv(ws[4], mma_splits=5)))

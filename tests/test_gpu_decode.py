@@ -227,3 +227,28 @@ def test_decode_attention_sequence_independent_of_batch(cap):
                lens[i:i + 1].data_ptr(), 1, H, Hk, hd, cap, scale, a1.data_ptr(), st)
         torch.cuda.synchronize()
         assert torch.equal(a[i], a1[0]), i
+
+
+@pytest.mark.parametrize("m", [1, 8, 32])
+@pytest.mark.parametrize("splits", [2, 4])
+def test_decode_gemv_fused_norm_with_cluster_k_splits(m, splits):
+    """The fused-RMSNorm GEMV with K split over a cluster (the decode step's qkv projection):
+    each CTA folds its K range, the first adds the others' dot products and sums of squares
+    in split order; against the oracle's rms_norm then q8 linear (1e-5), repeated twice."""
+    import torch
+    rng = np.random.default_rng(200 + m + splits)
+    n, k = 1152, 896
+    w = (rng.normal(size=(n, k)) * 0.02).astype(np.float32)
+    qt = pkg("quant").make_qtensor(w)
+    oq = nx.QTensor("q8", qt.q, qt.scales, qt.shape, 64)
+    nw = (1 + 0.1 * rng.normal(size=k)).astype(np.float32)
+    b = rng.normal(size=n).astype(np.float32)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    ref = nx.qmatmul(nx.rms_norm(x, nw, 1e-6), oq, b)
+    g = _dg(qt, bias=torch.from_numpy(b).cuda(), norm_w=torch.from_numpy(nw).cuda(), eps=1e-6, mma_splits=splits)
+    assert g.splits == splits
+    xd, y = torch.from_numpy(x).cuda(), torch.empty(m, n, device="cuda")
+    for _ in range(2):
+        g(xd.data_ptr(), m, y.data_ptr())
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), ref) < 1e-5
