@@ -107,9 +107,10 @@ int cv3_q8_decode_gemv(const float* x, int64_t m, int64_t k, int64_t ldx, const 
  * Same operands, fusions and output as cv3_q8_decode_gemv; needs K a multiple
  * of 64 with no padding (kp == k), K <= 5120, 16-byte aligned x rows; a CTA
  * stages its rows' K range in shared memory, so m > 8 with a long K needs
- * `splits` (CV3_ERR_VALUE otherwise).  `splits` > 1 (no fused RMSNorm) spreads
- * K over that many CTAs per row tile with a deterministic reduction (a cluster
- * for up to 8 splits); more than 8 splits need workspace >= splits*n*8*B floats
+ * `splits` (CV3_ERR_VALUE otherwise).  `splits` > 1 spreads K over that many
+ * CTAs per row tile with a deterministic reduction (a cluster for up to 8
+ * splits; with a fused RMSNorm at most 8, the cluster's first CTA adding the
+ * others' sums of squares); more than 8 splits need workspace >= splits*n*8*B floats
  * (B = 1 for m <= 8, 2 for m <= 16, else 4) and counters (one per 16-row tile,
  * or 32-row when n >= 4096 and a CTA takes at most 16 scale groups) zeroed
  * once, left zeroed.  Replaces the per-token ops.linear calls of
